@@ -1,0 +1,421 @@
+#!/usr/bin/env python
+"""KVForge codec benchmark on B200.
+
+Workload (default): Aggressive preset (INT4 KIVI, SVD projection at 75%
+variance, rANS, calibration) compress + decompress of a Llama-3-8B-shaped KV
+cache: 32 layers x keys and values [8 heads, 32768 tokens, 128] fp16, layer
+seed 100 + l, low-rank (rank 24) + 0.1 N(0,1) noise, 4 outlier key channels per
+head at U[8, 16]. Layers are sharded across ranks (one process per GPU); the
+total work is fixed, so scaling is strong. The calibrated projection bases are
+computed once per layer before timing (the basis step may stay outside the
+timed path); the timed step is everything else, on the device.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "KV compress+decompress GB/s (fp16 K+V input bytes per second), Aggressive preset"
+UNIT = "GB/s"
+GB = 1e9
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _traffic():
+    """Per-launch DRAM traffic of the dominant kernel from the committed ncu
+    summary (profiles/), scaled to the workload; None when absent."""
+    path = os.path.join(ROOT, "profiles", "reconstruct_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                pw.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def _dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle: a C restatement of the reference CPU crate)
+# ---------------------------------------------------------------------------
+def _oracle_time(O, keys, values, bases, preset, threads, min_seconds, max_reps):
+    """Times oracle compress + decompress of one layer (basis given)."""
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        c = O.compress(keys, values, preset, 0, bases, threads=threads)
+        O.decompress(c, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            return el / reps, O.ratio(c)
+
+
+def cpu_baseline(workload, k16, v16, bases, threads=1, min_seconds=10.0):
+    from oracle import oracle as O
+    O.build()
+    k = k16.astype(np.float32)
+    v = v16.astype(np.float32)
+    w = workload
+    sec, ratio = _oracle_time(O, k, v, bases, w["preset"], threads, min_seconds, 5)
+    nbytes = k16.nbytes + v16.nbytes
+    return {"value": nbytes / sec / GB, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 layer [{k.shape[0]},{k.shape[1]},{k.shape[2]}] fp16 K+V ({nbytes / 2**20:.0f} MiB), "
+                      f"compress+decompress with the calibrated basis, {threads} thread(s), "
+                      f"{sec:.2f} s per layer", "ratio": ratio}
+
+
+def reference_arm(args):
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return 0
+    from kvforge_b200 import synth
+    from oracle import oracle as O
+    O.build()
+    w = dict(synth.WORKLOADS[args.workload])
+    threads = os.cpu_count() or 1
+    k16, v16 = synth.workload_layer(args.workload, 0, backend="numpy")
+    k, v = k16.astype(np.float32), v16.astype(np.float32)
+    thr = O.PRESETS[w["preset"]]["thr"]
+    bases = None
+    if O.PRESETS[w["preset"]]["proj"]:
+        bases = (O.basis_for(k, thr, threads=threads), O.basis_for(v, thr, threads=threads))
+    for _ in range(args.warmup):
+        c = O.compress(k, v, w["preset"], 0, bases, threads=threads)
+        O.decompress(c, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        c = O.compress(k, v, w["preset"], 0, bases, threads=threads)
+        O.decompress(c, threads=threads)
+    sec = (time.perf_counter() - t0) / args.steps
+    nbytes = k16.nbytes + v16.nbytes
+    val = nbytes / sec / GB
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config(args, w),
+        "ratio": O.ratio(c),
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"layer 0 of the workload ([{k.shape[0]},{k.shape[1]},{k.shape[2]}] fp16 K+V, "
+                                   f"{nbytes / 2**20:.0f} MiB) per step, CPU oracle (C restatement of the "
+                                   f"reference crate; Rust is not installed) with {threads} OpenMP threads, "
+                                   f"calibrated basis precomputed"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _config(args, w):
+    return {"workload": args.workload, "preset": w["preset"], "layers": args.layers or w.get("layers", 1),
+            "heads": w["H"], "tokens": w["T"], "head_dim": w["D"], "input_dtype": w["dtype"],
+            "output_dtype": "f32", "basis": "calibrated per layer, computed before the timed region",
+            "l2": "inputs larger than L2 (no flush)", "parallelism": f"layer-sharded x{args.gpus}"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def gpu_arm(args):
+    import torch
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = local
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(f"cuda:{dev}"))
+    import kvforge_b200 as K
+    from kvforge_b200 import _lib as L
+    from kvforge_b200 import synth
+    from kvforge_b200.dist import gather_stats, layer_shard, reduce_stats
+
+    w = dict(synth.WORKLOADS[args.workload])
+    n_layers = args.layers or w.get("layers", 1)
+    mine = list(layer_shard(n_layers, world, rank))
+    lib = L.lib()
+    ctx = L.context(dev)
+    cfg = K.config_from_preset(w["preset"])
+    H, T, D = w["H"], w["T"], w["D"]
+    in_code = L.IN_F16 if w["dtype"] == "float16" else L.IN_F32
+
+    # inputs (device-resident, generated on the GPU) and calibrated bases
+    layers = []
+    t_basis = 0.0
+    for l in mine:
+        k, v = synth.workload_layer(args.workload, l, backend="torch", device=f"cuda:{dev}")
+        kb = vb = None
+        if cfg.enable_projection:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            kb = K.Basis.compute(k, cfg.projection_variance_threshold, device=dev)
+            vb = K.Basis.compute(v, cfg.projection_variance_threshold, device=dev)
+            t_basis += time.perf_counter() - t0
+        layers.append((l, k, v, kb, vb))
+    torch.cuda.synchronize()
+    ko = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+    vo = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def run_layer(l, k, v, kb, vb, keep=False):
+        h = C.c_void_p()
+        L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), in_code, H, T, D, l,
+                                       C.byref(cfg), kb.handle if kb else None, vb.handle if vb else None,
+                                       C.byref(h), sptr))
+        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sptr))
+        if keep:
+            return h
+        lib.kvf_compressed_free(h)
+        return None
+
+    def step():
+        for lay in layers:
+            run_layer(*lay)
+
+    for _ in range(args.warmup):
+        step()
+    L.check(lib.kvf_sync(ctx, sptr))
+
+    # ratio, sizes and reconstruction error of this rank's layers (untimed)
+    comp_bytes = 0
+    err = {"err2_k": 0.0, "ref2_k": 0.0, "err2_v": 0.0, "ref2_v": 0.0}
+    for lay in layers:
+        h = run_layer(*lay, keep=True)
+        n = C.c_size_t()
+        L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
+        comp_bytes += n.value
+        kf, vf = lay[1].float(), lay[2].float()
+        err["err2_k"] += float(((ko - kf) ** 2).sum())
+        err["ref2_k"] += float((kf ** 2).sum())
+        err["err2_v"] += float(((vo - vf) ** 2).sum())
+        err["ref2_v"] += float((vf ** 2).sum())
+        lib.kvf_compressed_free(h)
+    L.check(lib.kvf_sync(ctx, sptr))
+    in_bytes = sum(lay[1].numel() * lay[1].element_size() * 2 for lay in layers)
+    orig_bytes = len(layers) * 2 * H * T * D * 4
+
+    # timed region
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    L.check(lib.kvf_profile_enable(ctx, 1))
+    L.profile_read(dev)
+    n0 = lib.kvf_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n1 = lib.kvf_launch_count()
+    prof = L.profile_read(dev)
+    L.check(lib.kvf_profile_enable(ctx, 0))
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    L.check(lib.kvf_sync(ctx, sptr))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+    # end-to-end through the host-buffer C-ABI entry points
+    e2e = None
+    if args.e2e_steps > 0:
+        kh = [torch.empty((H, T, D), dtype=lay[1].dtype, pin_memory=True) for lay in layers]
+        vh = [torch.empty((H, T, D), dtype=lay[2].dtype, pin_memory=True) for lay in layers]
+        for i, lay in enumerate(layers):
+            kh[i].copy_(lay[1])
+            vh[i].copy_(lay[2])
+        koh = torch.empty((H, T, D), dtype=torch.float32, pin_memory=True)
+        voh = torch.empty((H, T, D), dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            for i, (l, _, _, kb, vb) in enumerate(layers):
+                h = C.c_void_p()
+                L.check(lib.kvf_compress_layer_host(ctx, C.c_void_p(kh[i].data_ptr()), C.c_void_p(vh[i].data_ptr()),
+                                                    in_code, H, T, D, l, C.byref(cfg), kb.handle if kb else None,
+                                                    vb.handle if vb else None, C.byref(h), sptr))
+                L.check(lib.kvf_decompress_layer_host(ctx, h, C.c_void_p(koh.data_ptr()), C.c_void_p(voh.data_ptr()),
+                                                      sptr))
+                lib.kvf_compressed_free(h)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        e2e = {"ms": e2e_ms, "h2d": in_bytes, "d2h": orig_bytes}
+    else:
+        e2e_ms = float("nan")
+
+    stats = {"layers": len(layers), "input_bytes": in_bytes, "compressed_bytes": comp_bytes,
+             "original_bytes": orig_bytes, "ms": ms, **err}
+    per = gather_stats(stats, device=f"cuda:{dev}" if world > 1 else None)
+    tot = reduce_stats(per)
+    e2e_per = gather_stats({"ms": e2e_ms, "input_bytes": in_bytes, "original_bytes": orig_bytes},
+                           device=f"cuda:{dev}" if world > 1 else None)
+    e2e_tot = reduce_stats(e2e_per)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        lay = layers[0]
+        bases = None
+        if lay[3] is not None:
+            kbh, vbh = lay[3].host(), lay[4].host()
+            bases = ((kbh[0], kbh[1]), (vbh[0], vbh[1]))
+        cpu = cpu_baseline(w, lay[1].cpu().numpy(), lay[2].cpu().numpy(), bases, threads=1,
+                           min_seconds=args.cpu_seconds)
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_kind = _peaks()
+    step_ms = tot["ms"]
+    value = tot["input_bytes"] / (step_ms / 1e3) / GB
+    # algorithmic bytes per step: inputs + compressed (written) + compressed (read) + f32 outputs
+    alg = tot["input_bytes"] + 2 * tot["compressed_bytes"] + tot["original_bytes"]
+    dom = max(prof.items(), key=lambda kv: kv[1][0])
+    dname, (dms, dcount, dbytes) = dom
+    achieved = (dbytes / dcount) / ((dms / dcount) / 1e3) / GB if dcount and dms > 0 else None
+    traffic = _traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded low-rank + noise + outlier channels)",
+        "config": _config(args, w),
+        "ratio": tot["original_bytes"] / tot["compressed_bytes"],
+        "rel_err": {"keys": (tot["err2_k"] / tot["ref2_k"]) ** 0.5, "values": (tot["err2_v"] / tot["ref2_v"]) ** 0.5},
+        "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak,
+                          "frac": alg / (step_ms / 1e3) / GB / peak, "peak_kind": peak_kind},
+        "roofline": {"kernel": dname, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None,
+                     "traffic": (traffic or {}).get("bytes_per_launch"),
+                     "algorithmic_bytes_per_launch": dbytes / dcount if dcount else None,
+                     "launches": dcount, "avg_launch_ms": dms / dcount if dcount else None,
+                     "peak_kind": peak_kind},
+        "stages_ms_per_step": {k: v[0] / args.steps for k, v in prof.items() if v[1]},
+        "basis_ms_per_layer_untimed": 1e3 * t_basis / max(len(layers), 1),
+        "gpu_launches": int(n1 - n0),
+        "clocks": clk,
+    }
+    if e2e is not None:
+        e2e_val = e2e_tot["input_bytes"] / (e2e_tot["ms"] / 1e3) / GB
+        line["e2e"] = {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(e2e_tot["input_bytes"]),
+                       "d2h_bytes_per_step": int(e2e_tot["original_bytes"]), "ms_per_step": e2e_tot["ms"],
+                       "api": "kvf_compress_layer_host + kvf_decompress_layer_host (pinned host buffers)"}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="llama3_8b_32k")
+    ap.add_argument("--layers", type=int, default=0, help="number of layers (default: the workload's)")
+    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return gpu_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,266 @@
+/*
+ * kvforge.h -- C ABI of the B200-native KVForge codec (libkvforge_b200.so).
+ *
+ * This is the drop-in boundary for the reference's codec path. It replaces the
+ * stubbed CUDA crate (crates/kvforge-cuda: KernelLauncher in
+ * src/kernel_launcher.rs:7-77 and GpuCompressionPipeline in
+ * src/gpu_pipeline.rs:10-37) and serves the kvforge-core traits
+ * (crates/kvforge-core/src/codec.rs:27-137, src/pipeline.rs:73-80).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only. Tensor pointers are DEVICE pointers unless
+ *    a parameter name ends in _host. Streams are cudaStream_t passed as void*
+ *    (NULL = legacy default stream).
+ *  - Every call returns kvf_status; KVF_OK is 0. The numbering mirrors the
+ *    reference KvForgeError variants (crates/kvforge-core/src/error.rs:3-28)
+ *    plus two device-side conditions. kvf_last_error() returns the message of
+ *    the last failing call on the calling thread.
+ *  - Calls are stream-ordered. The only host synchronisations are the ones a
+ *    function documents (sizes that must reach the host, and the one-off basis
+ *    step, which runs its eigen-solve on the host).
+ *  - One kvf_ctx per device. Calls on one context may be issued from one host
+ *    thread at a time; all scratch memory is taken per call from the device's
+ *    stream-ordered pool, so calls on different streams do not share scratch.
+ *  - Layout: tensors are [num_heads, seq_len, head_dim] row-major, as in the
+ *    reference KVCache (crates/kvforge-core/src/types.rs:5-12).
+ */
+#ifndef KVFORGE_B200_H
+#define KVFORGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVF_ABI_VERSION 1
+
+typedef enum {
+  KVF_OK = 0,
+  KVF_ERR_SHAPE_MISMATCH = 1,  /* KvForgeError::ShapeMismatch */
+  KVF_ERR_INVALID_CONFIG = 2,  /* KvForgeError::InvalidConfig */
+  KVF_ERR_QUANTIZATION = 3,    /* KvForgeError::QuantizationError */
+  KVF_ERR_PROJECTION = 4,      /* KvForgeError::ProjectionError */
+  KVF_ERR_ENTROPY = 5,         /* KvForgeError::EntropyError */
+  KVF_ERR_SERIALIZATION = 6,   /* KvForgeError::SerializationError */
+  KVF_ERR_CUDA = 7,            /* KvForgeError::CudaError */
+  KVF_ERR_PIPELINE = 8,        /* KvForgeError::PipelineError */
+  KVF_ERR_DEVICE_TIMEOUT = 9,  /* a bounded device-side wait gave up */
+  KVF_ERR_CORRUPT_STREAM = 10  /* rANS container failed validation on the device */
+} kvf_status;
+
+/* DataType (types.rs:106-113) */
+typedef enum { KVF_INT4 = 0, KVF_INT8 = 1, KVF_F32 = 2 } kvf_data_type;
+/* QuantAxis (types.rs:97-103) */
+typedef enum { KVF_PER_CHANNEL = 0, KVF_PER_TOKEN = 1 } kvf_quant_axis;
+/* element type of an input tensor; the reference takes f32 only
+ * (crates/kvforge-python/src/py_types.rs:21-25); f16 is up-cast exactly. */
+typedef enum { KVF_IN_F32 = 0, KVF_IN_F16 = 1 } kvf_in_dtype;
+/* CompressionPreset (crates/kvforge-core/src/pipeline.rs:5-15) */
+typedef enum {
+  KVF_CONSERVATIVE = 0,
+  KVF_BALANCED = 1,
+  KVF_AGGRESSIVE = 2,
+  KVF_ADAPTIVE = 3
+} kvf_preset;
+
+/* PipelineConfig (crates/kvforge-core/src/pipeline.rs:17-28) */
+typedef struct {
+  int32_t preset;
+  int32_t key_data_type;
+  int32_t value_data_type;
+  int32_t enable_projection;
+  double projection_variance_threshold;
+  int32_t enable_entropy_coding;
+  int32_t enable_calibration;
+} kvf_pipeline_config;
+
+typedef struct kvf_ctx kvf_ctx;
+typedef struct kvf_basis kvf_basis;
+typedef struct kvf_compressed kvf_compressed;
+
+/* ---- context ---------------------------------------------------------- */
+/* replaces KernelLauncher::new (kernel_launcher.rs:13-17) */
+kvf_status kvf_init(int device, kvf_ctx** out);
+kvf_status kvf_destroy(kvf_ctx* ctx);
+const char* kvf_last_error(void);
+int kvf_abi_version(void);
+/* 1: reconstruction uses separate multiply and add in the reference's order
+ * (projection.rs:160-166), bit-identical to the CPU oracle.
+ * 0 (default): one fused multiply-add per term (same order), within 1e-6. */
+kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
+/* waits for `stream` and reports any error a device kernel recorded
+ * (corrupt rANS container, bounded wait expiry) since the last check */
+kvf_status kvf_sync(kvf_ctx* ctx, void* stream);
+
+/* ---- observability (no counterpart in the reference, which has no tracing) --
+ * kvf_launch_count: kernels this library has launched in the process.
+ * Stage timing: when enabled on a context, each pipeline stage is bracketed by
+ * CUDA events on its stream; kvf_profile_read synchronises those events,
+ * returns per-stage totals (ms, launches of the stage, algorithmic bytes) for
+ * stages 0..KVF_NUM_STAGES-1 and clears them. */
+#define KVF_NUM_STAGES 8
+enum {
+  KVF_STAGE_CALIBRATE = 0,
+  KVF_STAGE_PROJECT = 1,
+  KVF_STAGE_QUANTIZE = 2,
+  KVF_STAGE_ENTROPY_ENCODE = 3,
+  KVF_STAGE_ENTROPY_DECODE = 4,
+  KVF_STAGE_RECONSTRUCT = 5,
+  KVF_STAGE_DEQUANTIZE = 6,
+  KVF_STAGE_BASIS = 7
+};
+uint64_t kvf_launch_count(void);
+const char* kvf_stage_name(int32_t stage);
+kvf_status kvf_profile_enable(kvf_ctx* ctx, int enable);
+kvf_status kvf_profile_read(kvf_ctx* ctx, double* ms, uint64_t* count, double* bytes);
+
+/* PipelineConfig::from_preset (crates/kvforge-core/src/pipeline.rs:30-71) */
+kvf_status kvf_pipeline_config_from_preset(int32_t preset, kvf_pipeline_config* out);
+
+/* ---- stage-level entry points (the kvforge-core traits) ----------------- */
+
+/* SensitivityCalibrator::calibrate (codec.rs:27-29; calibration.rs:25-73).
+ * keys [H,T,D]; scores out: H floats (device). KVF_ERR_INVALID_CONFIG when
+ * T < min_tokens. */
+kvf_status kvf_calibrate(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_t H, size_t T,
+                         size_t D, size_t min_tokens, float* scores, void* stream);
+
+/* Quantizer::quantize (codec.rs:105-111; quantize.rs:47-163).
+ * packed: INT8 -> H*T*D bytes, INT4 -> ceil(H*T*D/2) bytes (low nibble first,
+ * pairs over the flat index). scales/mins: H*D (per-channel) or H*T (per-token). */
+kvf_status kvf_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T,
+                        size_t D, int32_t data_type, int32_t axis, uint8_t* packed, float* scales,
+                        float* mins, void* stream);
+
+/* Quantizer::dequantize (codec.rs:113-114; quantize.rs:165-231). out f32 [H,T,D]. */
+kvf_status kvf_dequantize(kvf_ctx* ctx, const uint8_t* packed, size_t packed_len,
+                          const float* scales, const float* mins, int32_t data_type,
+                          int32_t axis, size_t H, size_t T, size_t D, float* out, void* stream);
+
+/* Projector::project (codec.rs:50-57; projection.rs:61-140) against a basis.
+ * basis_vt [H,R,D] f32 (rows >= ranks[h] are zero), ranks [H] uint64 (device).
+ * projected out f32 [H,T,R]; column r of head h is sum_c x[h,t,c]*basis_vt[h,r,c]
+ * as one fused multiply-add chain over c = 0..D-1, and +0.0 for r >= ranks[h]. */
+kvf_status kvf_project(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T,
+                       size_t D, const float* basis_vt, const uint64_t* ranks, size_t R,
+                       float* projected, void* stream);
+
+/* Projector::reconstruct (codec.rs:59-64; projection.rs:142-172). out f32 [H,T,D]. */
+kvf_status kvf_reconstruct(kvf_ctx* ctx, const float* projected, size_t H, size_t T, size_t R,
+                           size_t D, const float* basis_vt, const uint64_t* ranks, float* out,
+                           void* stream);
+
+/* KernelLauncher::fused_project_quantize_int4/int8 (kernel_launcher.rs:19-41):
+ * projection then quantization in one call; same outputs as kvf_project
+ * followed by kvf_quantize on the projected tensor. */
+kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H,
+                                      size_t T, size_t D, const float* basis_vt,
+                                      const uint64_t* ranks, size_t R, int32_t data_type,
+                                      int32_t axis, uint8_t* packed, float* scales, float* mins,
+                                      void* stream);
+
+/* EntropyCodec::encode (codec.rs:131-133; entropy.rs:42-86), container format
+ * in the library's documentation. freq out: 256 u32 counts (device) -- the
+ * reference's EntropyState.frequencies. out_cap must be at least
+ * kvf_rans_max_encoded_len(n). SYNCHRONISES `stream` to return *out_len_host. */
+size_t kvf_rans_max_encoded_len(size_t n);
+kvf_status kvf_rans_encode(kvf_ctx* ctx, const uint8_t* data, size_t n, uint8_t* out,
+                           size_t out_cap, size_t* out_len_host, uint32_t* freq, void* stream);
+
+/* EntropyCodec::decode (codec.rs:135-136; entropy.rs:88-123). freq: 256 u32
+ * counts (device). KVF_ERR_ENTROPY when comp_len % 4 != 0 (entropy.rs:94-98).
+ * SYNCHRONISES `stream` to report KVF_ERR_CORRUPT_STREAM. */
+kvf_status kvf_rans_decode(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len,
+                           const uint32_t* freq, size_t original_len, uint8_t* out, void* stream);
+
+/* KernelLauncher::entropy_decode_dequant (kernel_launcher.rs:64-76): rANS
+ * decode then dequantize to f32 [H,T,D]. Asynchronous; a corrupt stream is
+ * reported by kvf_sync. */
+kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len,
+                                      const uint32_t* freq, const float* scales,
+                                      const float* mins, int32_t data_type, int32_t axis,
+                                      size_t H, size_t T, size_t D, float* out, void* stream);
+
+/* ---- projection basis (the calibrated basis) ----------------------------
+ * The reference takes a full SVD of each head inside project
+ * (projection.rs:81-90). Here the basis step is separate: a Gram matrix
+ * X_h^T X_h per head on the device, then an fp64 symmetric eigen-solve on the
+ * host; eigenvectors sorted by descending eigenvalue are the right singular
+ * vectors, sqrt(eigenvalue) the singular values. Ranks follow select_rank
+ * (projection.rs:31-59); R = max rank. SYNCHRONISES `stream`. */
+kvf_status kvf_basis_compute(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H,
+                             size_t T, size_t D, double variance_threshold, size_t max_rank,
+                             kvf_basis** out, void* stream);
+/* basis from host arrays: basis_vt_host [H,R,D], ranks_host [H] */
+kvf_status kvf_basis_from_host(kvf_ctx* ctx, size_t H, size_t R, size_t D,
+                               const float* basis_vt_host, const uint64_t* ranks_host,
+                               kvf_basis** out);
+kvf_status kvf_basis_info(const kvf_basis* b, size_t* H, size_t* R, size_t* D);
+/* copies out (host): basis_vt [H,R,D], ranks [H], singular values [H,D]
+ * (any pointer may be NULL; singular values are zero for a basis from host) */
+kvf_status kvf_basis_download(const kvf_basis* b, float* basis_vt_host, uint64_t* ranks_host,
+                              float* sv_host);
+const float* kvf_basis_device_vt(const kvf_basis* b);
+const uint64_t* kvf_basis_device_ranks(const kvf_basis* b);
+kvf_status kvf_basis_free(kvf_basis* b);
+
+/* ---- whole-layer pipeline (CompressionPipeline, core/src/pipeline.rs:73-80;
+ *      CpuCompressionPipeline::compress/decompress, cpu/src/pipeline.rs:99-186)
+ * keys, values: [H,T,D] device tensors of in_dtype. k_basis / v_basis: the
+ * calibrated bases for projection presets; NULL computes them inside the
+ * call (a synchronising host eigen-solve, as the reference does an SVD per
+ * call). The result lives on the device; sizes that depend on the entropy
+ * coder's output are read back on first request. */
+kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values,
+                              int32_t in_dtype, size_t H, size_t T, size_t D, size_t layer_idx,
+                              const kvf_pipeline_config* cfg, const kvf_basis* k_basis,
+                              const kvf_basis* v_basis, kvf_compressed** out, void* stream);
+/* keys_out, values_out: f32 [H,T,D] device */
+kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* keys_out,
+                                float* values_out, void* stream);
+
+/* Host-buffer variants (pinned or pageable host memory): copy in, run, copy
+ * out on `stream`; they synchronise before returning. */
+kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host,
+                                   int32_t in_dtype, size_t H, size_t T, size_t D,
+                                   size_t layer_idx, const kvf_pipeline_config* cfg,
+                                   const kvf_basis* k_basis, const kvf_basis* v_basis,
+                                   kvf_compressed** out, void* stream);
+kvf_status kvf_decompress_layer_host(kvf_ctx* ctx, const kvf_compressed* c, float* keys_host,
+                                     float* values_host, void* stream);
+
+/* CompressedKV accessors (types.rs:36-56). Sizes SYNCHRONISE on first call
+ * when entropy coding was enabled. */
+kvf_status kvf_compressed_shape(const kvf_compressed* c, size_t* H, size_t* T, size_t* D,
+                                size_t* layer_idx);
+kvf_status kvf_compressed_size_bytes(kvf_compressed* c, size_t* out);
+kvf_status kvf_original_size_bytes(const kvf_compressed* c, size_t* out);
+kvf_status kvf_compression_ratio(kvf_compressed* c, double* out);
+/* per tensor (0 = keys, 1 = values): rank width R (0 when not projected),
+ * quantized byte length before entropy coding, final data length */
+kvf_status kvf_compressed_tensor_info(kvf_compressed* c, int32_t which, size_t* R,
+                                      size_t* packed_len, size_t* data_len, int32_t* has_entropy);
+/* device views of one tensor's buffers (NULL where absent) */
+kvf_status kvf_compressed_tensor_views(const kvf_compressed* c, int32_t which,
+                                       const uint8_t** data, const float** scales,
+                                       const float** mins, const uint32_t** freq,
+                                       const float** basis_vt, const uint64_t** ranks);
+/* calibration scores of the keys (H floats, device), or NULL when calibration
+ * was disabled or failed (the reference discards both, pipeline.rs:104-111) */
+const float* kvf_compressed_calibration(const kvf_compressed* c);
+
+/* serialisation to host bytes and back (CompressedKV.to_bytes/from_bytes,
+ * crates/kvforge-python/src/py_types.rs:98-110); format in the library's
+ * documentation. kvf_compressed_serialize with buf == NULL returns the size. */
+kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf_host, size_t cap,
+                                    size_t* len);
+kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf_host, size_t len,
+                                      kvf_compressed** out, void* stream);
+kvf_status kvf_compressed_free(kvf_compressed* c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVFORGE_B200_H */

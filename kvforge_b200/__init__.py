@@ -1,0 +1,519 @@
+"""kvforge_b200 -- B200-native KVForge KV-cache codec.
+
+Python face of libkvforge_b200.so, mirroring the reference Python API
+(crates/kvforge-python/kvforge/__init__.py:3-17): KVCache, CompressedKV,
+CompressionPipeline, compress, decompress -- plus stage-level classes that
+mirror the kvforge-core traits (crates/kvforge-core/src/codec.rs:27-137).
+
+Tensors may be numpy arrays or torch tensors, float32 or float16, on the host
+or on the GPU; the codec itself always runs on the GPU through the C ABI.
+PyTorch supplies device memory and the current stream only.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import KvForgeError
+
+__all__ = [
+    "KVCache", "CompressedKV", "CompressionPipeline", "compress", "decompress", "KvForgeError",
+    "Basis", "QuantParams", "EntropyState", "GpuQuantizer", "GpuProjector", "GpuSensitivityCalibrator",
+    "GpuEntropyCodec", "config_from_preset", "parse_preset", "INT4", "INT8", "F32", "PER_CHANNEL", "PER_TOKEN",
+]
+
+INT4, INT8, F32 = L.INT4, L.INT8, L.F32
+PER_CHANNEL, PER_TOKEN = L.PER_CHANNEL, L.PER_TOKEN
+
+_PRESETS = {"conservative": L.CONSERVATIVE, "balanced": L.BALANCED, "aggressive": L.AGGRESSIVE,
+            "adaptive": L.ADAPTIVE}
+
+
+def parse_preset(preset) -> int:
+    """Case-insensitive preset name (crates/kvforge-python/src/py_pipeline.rs:16-27)."""
+    if isinstance(preset, int):
+        return preset
+    p = _PRESETS.get(str(preset).lower())
+    if p is None:
+        raise ValueError(f"Unknown preset '{preset}'. Choose from: conservative, balanced, aggressive, adaptive")
+    return p
+
+
+def config_from_preset(preset) -> L.PipelineConfig:
+    """PipelineConfig::from_preset (crates/kvforge-core/src/pipeline.rs:30-71)."""
+    cfg = L.PipelineConfig()
+    L.check(L.lib().kvf_pipeline_config_from_preset(parse_preset(preset), C.byref(cfg)))
+    return cfg
+
+
+def _device_index(device) -> int:
+    if device is None:
+        return torch.cuda.current_device() if torch.cuda.is_available() else 0
+    if isinstance(device, torch.device):
+        return device.index or 0
+    if isinstance(device, str):
+        return torch.device(device).index or 0
+    return int(device)
+
+
+def _stream(dev: int) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _as_device(x, dev: int) -> torch.Tensor:
+    """Contiguous float32/float16 tensor on cuda:dev (other dtypes are rejected)."""
+    if isinstance(x, np.ndarray):
+        if x.dtype not in (np.float32, np.float16):
+            raise TypeError(f"expected float32 or float16 data, got {x.dtype}")
+        x = torch.from_numpy(np.ascontiguousarray(x))
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("expected a numpy array or a torch tensor")
+    if x.dtype not in (torch.float32, torch.float16):
+        raise TypeError(f"expected float32 or float16 data, got {x.dtype}")
+    return x.to(device=f"cuda:{dev}").contiguous()
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    return L.IN_F16 if t.dtype == torch.float16 else L.IN_F32
+
+
+def _ptr(t: Optional[torch.Tensor]) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+class _CudaView:
+    """Zero-copy view of library-owned device memory for torch.as_tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def _view(ptr: int, shape, typestr: str, dev: int) -> torch.Tensor:
+    if int(np.prod(shape)) == 0 or not ptr:
+        dt = {"<f4": torch.float32, "|u1": torch.uint8, "<u4": torch.int32, "<u8": torch.int64}[typestr]
+        return torch.empty(shape, dtype=dt, device=f"cuda:{dev}")
+    return torch.as_tensor(_CudaView(ptr, shape, typestr), device=f"cuda:{dev}")
+
+
+# ---------------------------------------------------------------------------
+# KVCache / CompressedKV (crates/kvforge-python/src/py_types.rs)
+# ---------------------------------------------------------------------------
+class KVCache:
+    """One layer's KV cache, keys and values of shape [num_heads, seq_len, head_dim]."""
+
+    def __init__(self, keys, values, layer_idx: int = 0):
+        ks, vs = tuple(keys.shape), tuple(values.shape)
+        if ks != vs:
+            raise ValueError("keys and values must have the same shape")  # py_types.rs:29-33
+        if len(ks) != 3:
+            raise ValueError("keys and values must be 3-D [num_heads, seq_len, head_dim]")
+        self._keys = keys
+        self._values = values
+        self._layer_idx = int(layer_idx)
+
+    @property
+    def layer_idx(self) -> int:
+        return self._layer_idx
+
+    @property
+    def shape(self):
+        return tuple(int(s) for s in self._keys.shape)
+
+    @staticmethod
+    def _np(x) -> np.ndarray:
+        if isinstance(x, torch.Tensor):
+            return x.detach().to("cpu", torch.float32).numpy()
+        return np.asarray(x, dtype=np.float32)
+
+    def keys(self) -> np.ndarray:
+        return self._np(self._keys)
+
+    def values(self) -> np.ndarray:
+        return self._np(self._values)
+
+    @property
+    def keys_tensor(self):
+        return self._keys
+
+    @property
+    def values_tensor(self):
+        return self._values
+
+    def size_bytes(self) -> int:
+        """Size as f32 (crates/kvforge-core/src/types.rs:30-32)."""
+        H, T, D = self.shape
+        return 2 * H * T * D * 4
+
+    def __repr__(self):
+        H, T, D = self.shape
+        return f"KVCache(num_heads={H}, seq_len={T}, head_dim={D}, layer_idx={self._layer_idx})"
+
+
+class CompressedKV:
+    """Device-resident compressed layer (crates/kvforge-core/src/types.rs:36-56)."""
+
+    def __init__(self, handle: C.c_void_p, device: int):
+        self._h = handle
+        self._dev = device
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and L._lib is not None:
+            L.lib().kvf_compressed_free(h)
+            self._h = None
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    @property
+    def device(self) -> int:
+        return self._dev
+
+    def ratio(self) -> float:
+        r = C.c_double()
+        L.check(L.lib().kvf_compression_ratio(self._h, C.byref(r)))
+        return r.value
+
+    def compressed_size_bytes(self) -> int:
+        n = C.c_size_t()
+        L.check(L.lib().kvf_compressed_size_bytes(self._h, C.byref(n)))
+        return n.value
+
+    def original_size_bytes(self) -> int:
+        n = C.c_size_t()
+        L.check(L.lib().kvf_original_size_bytes(self._h, C.byref(n)))
+        return n.value
+
+    @property
+    def shape(self):
+        H, T, D = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        L.check(L.lib().kvf_compressed_shape(self._h, C.byref(H), C.byref(T), C.byref(D), None))
+        return H.value, T.value, D.value
+
+    @property
+    def layer_idx(self) -> int:
+        li = C.c_size_t()
+        L.check(L.lib().kvf_compressed_shape(self._h, None, None, None, C.byref(li)))
+        return li.value
+
+    def tensor_info(self, which: int) -> dict:
+        """which: 0 keys, 1 values -> {R, packed_len, data_len, entropy}."""
+        R, pl, dl, he = C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_int32()
+        L.check(L.lib().kvf_compressed_tensor_info(self._h, which, C.byref(R), C.byref(pl), C.byref(dl),
+                                                  C.byref(he)))
+        return {"R": R.value, "packed_len": pl.value, "data_len": dl.value, "entropy": bool(he.value)}
+
+    def tensor_parts(self, which: int) -> dict:
+        """Device tensors (zero-copy views) of one tensor's compressed state:
+        data, scales, mins, freq (or None), basis_vt and ranks (or None)."""
+        info = self.tensor_info(which)
+        ptrs = [C.c_void_p() for _ in range(6)]
+        L.check(L.lib().kvf_compressed_tensor_views(self._h, which, *[C.byref(p) for p in ptrs]))
+        data, scales, mins, freq, bvt, ranks = [p.value or 0 for p in ptrs]
+        H, T, D = self.shape
+        R = info["R"]
+        q = R if R else D
+        axis = PER_CHANNEL if which == 0 else PER_TOKEN
+        npar = H * q if axis == PER_CHANNEL else H * T
+        out = {
+            "data": _view(data, (info["data_len"],), "|u1", self._dev),
+            "scales": _view(scales, (npar,), "<f4", self._dev),
+            "mins": _view(mins, (npar,), "<f4", self._dev),
+            "freq": _view(freq, (256,), "<u4", self._dev) if freq else None,
+            "basis_vt": _view(bvt, (H, R, D), "<f4", self._dev) if bvt else None,
+            "ranks": _view(ranks, (H,), "<u8", self._dev) if ranks else None,
+            "packed_len": info["packed_len"],
+            "R": R,
+        }
+        return out
+
+    def calibration_scores(self) -> Optional[np.ndarray]:
+        """Per-head key sensitivity scores, or None (calibration off or T < 64)."""
+        p = L.lib().kvf_compressed_calibration(self._h)
+        if not p:
+            return None
+        torch.cuda.current_stream(self._dev).synchronize()
+        return _view(p, (self.shape[0],), "<f4", self._dev).cpu().numpy()
+
+    def to_bytes(self) -> bytes:
+        n = C.c_size_t()
+        L.check(L.lib().kvf_compressed_serialize(self._h, None, 0, C.byref(n)))
+        buf = (C.c_uint8 * n.value)()
+        L.check(L.lib().kvf_compressed_serialize(self._h, buf, n.value, C.byref(n)))
+        return bytes(buf)
+
+    @staticmethod
+    def from_bytes(data: bytes, device=None) -> "CompressedKV":
+        dev = _device_index(device)
+        h = C.c_void_p()
+        buf = (C.c_uint8 * len(data)).from_buffer_copy(data)
+        L.check(L.lib().kvf_compressed_deserialize(L.context(dev), buf, len(data), C.byref(h), _stream(dev)))
+        return CompressedKV(h, dev)
+
+    def __repr__(self):
+        return (f"CompressedKV(ratio={self.ratio():.1f}x, compressed_bytes={self.compressed_size_bytes()}, "
+                f"original_bytes={self.original_size_bytes()})")
+
+
+# ---------------------------------------------------------------------------
+# Projection basis (the calibrated basis)
+# ---------------------------------------------------------------------------
+class Basis:
+    """Per-head projection basis: basis_vt [H, R, D] (rows >= ranks[h] zero) and ranks [H]."""
+
+    def __init__(self, handle: C.c_void_p, device: int):
+        self._h = handle
+        self._dev = device
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and L._lib is not None:
+            L.lib().kvf_basis_free(h)
+            self._h = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    @staticmethod
+    def compute(data, variance_threshold: float, max_rank: Optional[int] = None, device=None) -> "Basis":
+        """Gram matrix on the GPU + fp64 eigen-solve on the host (projection.rs:77-92)."""
+        dev = _device_index(device)
+        x = _as_device(data, dev)
+        H, T, D = x.shape
+        h = C.c_void_p()
+        L.check(L.lib().kvf_basis_compute(L.context(dev), _ptr(x), _dtype_code(x), H, T, D,
+                                          float(variance_threshold), int(max_rank or 0), C.byref(h), _stream(dev)))
+        return Basis(h, dev)
+
+    @staticmethod
+    def from_host(basis_vt: np.ndarray, ranks, device=None) -> "Basis":
+        dev = _device_index(device)
+        bvt = np.ascontiguousarray(basis_vt, np.float32)
+        rk = np.ascontiguousarray(ranks, np.uint64)
+        H, R, D = bvt.shape
+        h = C.c_void_p()
+        L.check(L.lib().kvf_basis_from_host(L.context(dev), H, R, D, bvt.ctypes.data_as(C.c_void_p),
+                                            rk.ctypes.data_as(C.c_void_p), C.byref(h)))
+        return Basis(h, dev)
+
+    @property
+    def dims(self):
+        H, R, D = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        L.check(L.lib().kvf_basis_info(self._h, C.byref(H), C.byref(R), C.byref(D)))
+        return H.value, R.value, D.value
+
+    @property
+    def R(self) -> int:
+        return self.dims[1]
+
+    def host(self):
+        """-> (basis_vt [H,R,D] f32, ranks [H] u64, singular values [H,D] f32)."""
+        H, R, D = self.dims
+        bvt = np.zeros((H, R, D), np.float32)
+        rk = np.zeros(H, np.uint64)
+        sv = np.zeros((H, D), np.float32)
+        L.check(L.lib().kvf_basis_download(self._h, bvt.ctypes.data_as(C.c_void_p), rk.ctypes.data_as(C.c_void_p),
+                                           sv.ctypes.data_as(C.c_void_p)))
+        return bvt, rk, sv
+
+    @property
+    def ranks(self) -> np.ndarray:
+        return self.host()[1]
+
+    def device_vt(self) -> int:
+        return L.lib().kvf_basis_device_vt(self._h) or 0
+
+    def device_ranks(self) -> int:
+        return L.lib().kvf_basis_device_ranks(self._h) or 0
+
+
+# ---------------------------------------------------------------------------
+# Pipeline (crates/kvforge-python/src/py_pipeline.rs, cpu/src/pipeline.rs:99-186)
+# ---------------------------------------------------------------------------
+class CompressionPipeline:
+    """GPU compression pipeline. compress() takes a KVCache and a preset name."""
+
+    def __init__(self, device=None):
+        self._dev = _device_index(device)
+
+    def compress(self, kv: KVCache, preset="balanced", key_basis: Optional[Basis] = None,
+                 value_basis: Optional[Basis] = None) -> CompressedKV:
+        cfg = config_from_preset(preset)
+        return self.compress_with_config(kv, cfg, key_basis, value_basis)
+
+    def compress_with_config(self, kv: KVCache, cfg: L.PipelineConfig, key_basis: Optional[Basis] = None,
+                             value_basis: Optional[Basis] = None) -> CompressedKV:
+        dev = self._dev
+        k = _as_device(kv.keys_tensor, dev)
+        v = _as_device(kv.values_tensor, dev)
+        if k.dtype != v.dtype:
+            v = v.to(k.dtype)
+        H, T, D = k.shape
+        h = C.c_void_p()
+        L.check(L.lib().kvf_compress_layer(L.context(dev), _ptr(k), _ptr(v), _dtype_code(k), H, T, D, kv.layer_idx,
+                                           C.byref(cfg), key_basis.handle if key_basis else None,
+                                           value_basis.handle if value_basis else None, C.byref(h), _stream(dev)))
+        c = CompressedKV(h, dev)
+        c._inputs = (k, v)  # keep the inputs alive until the stream has consumed them
+        return c
+
+    def decompress(self, compressed: CompressedKV) -> KVCache:
+        dev = compressed.device
+        H, T, D = compressed.shape
+        ko = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+        vo = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+        L.check(L.lib().kvf_decompress_layer(L.context(dev), compressed.handle, _ptr(ko), _ptr(vo), _stream(dev)))
+        L.check(L.lib().kvf_sync(L.context(dev), _stream(dev)))
+        return KVCache(ko, vo, compressed.layer_idx)
+
+
+def compress(kv: KVCache, preset="balanced") -> CompressedKV:
+    """Module-level compress (crates/kvforge-python/src/py_pipeline.rs:65-70)."""
+    return CompressionPipeline().compress(kv, preset)
+
+
+def decompress(compressed: CompressedKV) -> KVCache:
+    """Module-level decompress (crates/kvforge-python/src/py_pipeline.rs:73-77)."""
+    return CompressionPipeline(compressed.device).decompress(compressed)
+
+
+# ---------------------------------------------------------------------------
+# Stage-level API, mirroring the kvforge-core traits
+# ---------------------------------------------------------------------------
+@dataclass
+class QuantParams:
+    """QuantParams (crates/kvforge-core/src/types.rs:81-95)."""
+    scales: torch.Tensor
+    mins: torch.Tensor
+    data_type: int
+    axis: int
+    shape: tuple
+
+    def size_bytes(self) -> int:
+        return (self.scales.numel() + self.mins.numel()) * 4
+
+
+@dataclass
+class EntropyState:
+    """EntropyState (crates/kvforge-core/src/types.rs:138-148)."""
+    frequencies: torch.Tensor  # uint32 counts [256], or empty when coding was skipped
+    original_len: int
+
+    def size_bytes(self) -> int:
+        return self.frequencies.numel() * 4 + 8
+
+
+class GpuQuantizer:
+    """Quantizer trait (codec.rs:104-115) on the GPU."""
+
+    def __init__(self, device=None):
+        self._dev = _device_index(device)
+
+    def quantize(self, data, data_type: int, axis: int):
+        dev = self._dev
+        x = _as_device(data, dev)
+        H, T, D = x.shape
+        n = H * T * D
+        plen = (n + 1) // 2 if data_type == INT4 else n
+        npar = H * D if axis == PER_CHANNEL else H * T
+        packed = torch.empty(plen, dtype=torch.uint8, device=f"cuda:{dev}")
+        scales = torch.empty(npar, dtype=torch.float32, device=f"cuda:{dev}")
+        mins = torch.empty(npar, dtype=torch.float32, device=f"cuda:{dev}")
+        L.check(L.lib().kvf_quantize(L.context(dev), _ptr(x), _dtype_code(x), H, T, D, data_type, axis,
+                                     _ptr(packed), _ptr(scales), _ptr(mins), _stream(dev)))
+        return packed, QuantParams(scales, mins, data_type, axis, (H, T, D))
+
+    def dequantize(self, packed: torch.Tensor, params: QuantParams) -> torch.Tensor:
+        dev = self._dev
+        H, T, D = params.shape
+        out = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+        p = packed.to(f"cuda:{dev}").contiguous()
+        L.check(L.lib().kvf_dequantize(L.context(dev), _ptr(p), p.numel(), _ptr(params.scales), _ptr(params.mins),
+                                       params.data_type, params.axis, H, T, D, _ptr(out), _stream(dev)))
+        return out
+
+
+class GpuProjector:
+    """Projector trait (codec.rs:49-65) on the GPU, against a calibrated basis."""
+
+    def __init__(self, device=None):
+        self._dev = _device_index(device)
+
+    def compute_basis(self, data, variance_threshold: float, max_rank: Optional[int] = None) -> Basis:
+        return Basis.compute(data, variance_threshold, max_rank, self._dev)
+
+    def project(self, data, basis: Basis) -> torch.Tensor:
+        dev = self._dev
+        x = _as_device(data, dev)
+        H, T, D = x.shape
+        R = basis.R
+        out = torch.empty((H, T, R), dtype=torch.float32, device=f"cuda:{dev}")
+        L.check(L.lib().kvf_project(L.context(dev), _ptr(x), _dtype_code(x), H, T, D,
+                                    C.c_void_p(basis.device_vt()), C.c_void_p(basis.device_ranks()), R, _ptr(out),
+                                    _stream(dev)))
+        return out
+
+    def reconstruct(self, projected, basis: Basis) -> torch.Tensor:
+        dev = self._dev
+        p = _as_device(projected, dev).float()
+        H, T, R = p.shape
+        D = basis.dims[2]
+        out = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+        L.check(L.lib().kvf_reconstruct(L.context(dev), _ptr(p), H, T, R, D, C.c_void_p(basis.device_vt()),
+                                        C.c_void_p(basis.device_ranks()), _ptr(out), _stream(dev)))
+        return out
+
+
+class GpuSensitivityCalibrator:
+    """SensitivityCalibrator trait (codec.rs:26-29) on the GPU; takes the keys."""
+
+    def __init__(self, device=None):
+        self._dev = _device_index(device)
+
+    def calibrate(self, keys, min_tokens: int = 64) -> torch.Tensor:
+        dev = self._dev
+        x = _as_device(keys.keys_tensor if isinstance(keys, KVCache) else keys, dev)
+        H, T, D = x.shape
+        out = torch.empty(H, dtype=torch.float32, device=f"cuda:{dev}")
+        L.check(L.lib().kvf_calibrate(L.context(dev), _ptr(x), _dtype_code(x), H, T, D, min_tokens, _ptr(out),
+                                      _stream(dev)))
+        return out
+
+
+class GpuEntropyCodec:
+    """EntropyCodec trait (codec.rs:130-137) on the GPU, chunked rANS container."""
+
+    def __init__(self, device=None):
+        self._dev = _device_index(device)
+
+    def encode(self, data: torch.Tensor, enabled: bool = True):
+        dev = self._dev
+        d = data.to(f"cuda:{dev}").contiguous().view(torch.uint8).reshape(-1)
+        if not enabled or d.numel() == 0:  # entropy.rs:43-49
+            return d.clone(), EntropyState(torch.empty(0, dtype=torch.int32, device=f"cuda:{dev}"), d.numel())
+        cap = int(L.lib().kvf_rans_max_encoded_len(d.numel()))
+        out = torch.empty(cap, dtype=torch.uint8, device=f"cuda:{dev}")
+        freq = torch.empty(256, dtype=torch.int32, device=f"cuda:{dev}")
+        n = C.c_size_t()
+        L.check(L.lib().kvf_rans_encode(L.context(dev), _ptr(d), d.numel(), _ptr(out), cap, C.byref(n), _ptr(freq),
+                                        _stream(dev)))
+        return out[: n.value].clone(), EntropyState(freq, d.numel())
+
+    def decode(self, data: torch.Tensor, state: EntropyState) -> torch.Tensor:
+        dev = self._dev
+        d = data.to(f"cuda:{dev}").contiguous().view(torch.uint8).reshape(-1)
+        if state.frequencies.numel() == 0 or state.original_len == 0:  # entropy.rs:89-91
+            return d.clone()
+        out = torch.empty(state.original_len, dtype=torch.uint8, device=f"cuda:{dev}")
+        f = state.frequencies.to(f"cuda:{dev}").contiguous()
+        L.check(L.lib().kvf_rans_decode(L.context(dev), _ptr(d), d.numel(), _ptr(f), state.original_len, _ptr(out),
+                                        _stream(dev)))
+        return out

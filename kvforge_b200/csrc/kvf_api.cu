@@ -1,0 +1,1218 @@
+// C-ABI layer of libkvforge_b200: contexts, the whole-layer pipeline, the
+// basis step, size accounting and serialisation. Declarations and contracts
+// are in include/kvforge.h.
+//
+// Pipeline (crates/kvforge-cpu/src/pipeline.rs:38-186): keys are quantized
+// per channel and values per token; with projection each tensor is first
+// projected on its calibrated basis; with entropy coding the packed codes go
+// through the chunked rANS coder. Scratch memory comes from the device's
+// stream-ordered pool (cudaMallocAsync) and is released in stream order at the
+// end of each call; result buffers belong to the kvf_compressed object.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "kvf_internal.cuh"
+
+using namespace kvf;
+
+namespace kvf {
+static std::atomic<uint64_t> g_launches{0};
+void note_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+}  // namespace kvf
+
+namespace {
+
+thread_local std::string g_err;
+
+kvf_status fail(kvf_status s, const std::string& msg) {
+  g_err = msg;
+  return s;
+}
+
+#define KVF_CUDA(expr)                                                                   \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    if (_e != cudaSuccess)                                                               \
+      return fail(KVF_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e));     \
+  } while (0)
+
+#define KVF_TRY(expr)                 \
+  do {                                \
+    kvf_status _s = (expr);           \
+    if (_s != KVF_OK) return _s;      \
+  } while (0)
+
+inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+// makes ctx->device current for the duration of a call and restores the
+// caller's device afterwards
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// per-call scratch, released in stream order when the call returns
+struct Scratch {
+  cudaStream_t st;
+  std::vector<void*> ptrs;
+  explicit Scratch(cudaStream_t s) : st(s) {}
+  ~Scratch() {
+    for (void* p : ptrs) cudaFreeAsync(p, st);
+  }
+  template <class T>
+  T* get(size_t count) {
+    void* p = nullptr;
+    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), st) != cudaSuccess) return nullptr;
+    ptrs.push_back(p);
+    return static_cast<T*>(p);
+  }
+};
+
+struct BasisData {
+  size_t H = 0, R = 0, D = 0;
+  float* d_vt = nullptr;        // [H, R, D]
+  uint64_t* d_ranks = nullptr;  // [H]
+  std::vector<float> vt;
+  std::vector<uint64_t> ranks;
+  std::vector<float> sv;  // [H, D] singular values (empty for a basis given by the caller)
+  int device = 0;
+  ~BasisData() {
+    if (d_vt || d_ranks) {
+      int prev = -1;
+      cudaGetDevice(&prev);
+      if (prev != device) cudaSetDevice(device);
+      if (d_vt) cudaFree(d_vt);
+      if (d_ranks) cudaFree(d_ranks);
+      if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    }
+  }
+};
+
+// CompressedTensor (crates/kvforge-core/src/types.rs:58-78)
+struct TensorC {
+  int data_type = KVF_INT8, axis = KVF_PER_CHANNEL;
+  bool entropy = false;   // entropy coding enabled (EntropyState present)
+  bool has_freq = false;  // container + 256 counts present (non-empty input)
+  size_t H = 0, T = 0, D = 0, qcols = 0;
+  size_t packed_len = 0, num_params = 0;
+  uint8_t* d_data = nullptr;
+  size_t data_cap = 0;
+  uint64_t* d_len = nullptr;
+  bool len_known = false;
+  size_t data_len = 0;
+  float* d_scales = nullptr;
+  float* d_mins = nullptr;
+  uint32_t* d_freq = nullptr;
+  std::shared_ptr<BasisData> basis;  // projection state, when projected
+};
+
+}  // namespace
+
+struct kvf_ctx {
+  int device = 0;
+  int exact_reconstruct = 0;
+  unsigned* d_status = nullptr;
+  // stage timing (kvf_profile_enable / kvf_profile_read)
+  struct Rec {
+    int stage;
+    cudaEvent_t a, b;
+    double bytes;
+  };
+  int profile = 0;
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> spare;
+  cudaEvent_t event() {
+    if (!spare.empty()) {
+      cudaEvent_t e = spare.back();
+      spare.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+
+namespace {
+// brackets one pipeline stage with CUDA events when profiling is on
+struct StageTimer {
+  kvf_ctx* ctx;
+  int stage;
+  double bytes;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr;
+  StageTimer(kvf_ctx* c, int s, double b, cudaStream_t stream) : ctx(c), stage(s), bytes(b), st(stream) {
+    if (ctx && ctx->profile) {
+      a = ctx->event();
+      cudaEventRecord(a, st);
+    }
+  }
+  ~StageTimer() {
+    if (a) {
+      cudaEvent_t b = ctx->event();
+      cudaEventRecord(b, st);
+      ctx->recs.push_back({stage, a, b, bytes});
+    }
+  }
+};
+}  // namespace
+
+struct kvf_basis {
+  std::shared_ptr<BasisData> d;
+};
+
+struct kvf_compressed {
+  kvf_ctx* ctx = nullptr;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  size_t layer_idx = 0, H = 0, T = 0, D = 0, original_size_bytes = 0;
+  TensorC key, value;
+  float* d_scores = nullptr;
+  std::vector<void*> owned;
+
+  template <class T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), stream) != cudaSuccess) return nullptr;
+    owned.push_back(p);
+    return static_cast<T*>(p);
+  }
+};
+
+namespace {
+
+kvf_status check_ctx(kvf_ctx* ctx) {
+  if (!ctx) return fail(KVF_ERR_INVALID_CONFIG, "null context");
+  return KVF_OK;
+}
+
+kvf_status check_qcfg(int dt, int axis) {
+  if (dt == KVF_F32) return fail(KVF_ERR_QUANTIZATION, "F32 data type does not need quantization");
+  if (dt != KVF_INT4 && dt != KVF_INT8) return fail(KVF_ERR_INVALID_CONFIG, "unknown data type");
+  if (axis != KVF_PER_CHANNEL && axis != KVF_PER_TOKEN) return fail(KVF_ERR_INVALID_CONFIG, "unknown quantization axis");
+  return KVF_OK;
+}
+
+kvf_status check_dtype(int in_dtype) {
+  if (in_dtype != KVF_IN_F32 && in_dtype != KVF_IN_F16) return fail(KVF_ERR_INVALID_CONFIG, "unknown input dtype");
+  return KVF_OK;
+}
+
+kvf_status check_shape(size_t H, size_t T, size_t D) {
+  if (D > 1024) return fail(KVF_ERR_SHAPE_MISMATCH, "head_dim > 1024 is not supported");
+  if (H > 65535) return fail(KVF_ERR_SHAPE_MISMATCH, "num_heads > 65535 is not supported");
+  if (H * T * D > (size_t(1) << 40)) return fail(KVF_ERR_SHAPE_MISMATCH, "tensor too large");
+  return KVF_OK;
+}
+
+// quantize (from f32/f16 input) into `packed`, optional histogram of the packed bytes
+kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t T, size_t D, int dt,
+                         int axis, uint8_t* packed, float* scales, float* mins, uint32_t* hist,
+                         cudaStream_t st) {
+  const size_t n = H * T * D;
+  int* keys = nullptr;
+  if (axis == KVF_PER_CHANNEL) {
+    keys = sc.get<int>(2 * H * D);
+    if (!keys) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  }
+  if (dt == KVF_INT8) {
+    KVF_CUDA(launch_quantize_codes(qin, qdt, H, T, D, dt, axis, packed, scales, mins, keys, st));
+    if (hist) KVF_CUDA(launch_histogram(packed, n, hist, st));
+  } else {
+    uint8_t* codes = sc.get<uint8_t>(n);
+    if (!codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    KVF_CUDA(launch_quantize_codes(qin, qdt, H, T, D, dt, axis, codes, scales, mins, keys, st));
+    KVF_CUDA(launch_pack_int4(codes, n, packed, hist, st));
+  }
+  return KVF_OK;
+}
+
+// histogram -> model -> chunk coding -> container in `out` (length -> d_len)
+kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, size_t plen,
+                            const uint32_t* freq, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
+  RansTables* tab = sc.get<RansTables>(1);
+  const size_t nc = rans_num_chunks(plen, kRansChunk);
+  uint8_t* slots = sc.get<uint8_t>(nc * rans_slot_bytes(kRansChunk));
+  if (!tab || !slots) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
+  KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, tab, slots, st));
+  KVF_CUDA(launch_rans_assemble(slots, plen, kRansChunk, out, d_len, st));
+  return KVF_OK;
+}
+
+// compress_tensor (crates/kvforge-cpu/src/pipeline.rs:38-72)
+kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, int in_dtype, size_t H,
+                           size_t T, size_t D, int dt, int axis, const std::shared_ptr<BasisData>& basis,
+                           bool entropy, bool calib, float* d_scores, TensorC* out, cudaStream_t st) {
+  KVF_TRY(check_qcfg(dt, axis));
+  Scratch sc(st);
+  out->data_type = dt;
+  out->axis = axis;
+  out->H = H;
+  out->T = T;
+  out->D = D;
+  out->entropy = entropy;
+  out->basis = basis;
+  const void* qin = x;
+  int qdt = in_dtype;
+  size_t qcols = D;
+  double* cpart = nullptr;
+  size_t ctiles = 0;
+  const bool do_calib = calib && d_scores && T >= 64;  // CalibrationConfig::default().min_tokens
+  if (basis) {
+    if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
+    if (basis->H != H || basis->D != D)
+      return fail(KVF_ERR_SHAPE_MISMATCH, "basis shape does not match the tensor");
+    qcols = basis->R;
+    float* P = sc.get<float>(H * T * qcols);
+    if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    if (do_calib) {
+      ctiles = project_num_tiles(T);
+      cpart = sc.get<double>(2 * H * ctiles);
+      if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    }
+    {
+      StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4) + (double)H * T * qcols * 4, st);
+      KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, P, cpart, st));
+    }
+    qin = P;
+    qdt = KVF_IN_F32;
+  } else if (do_calib) {
+    ctiles = calib_partial_tiles(T, D);
+    cpart = sc.get<double>(2 * H * ctiles);
+    if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    StageTimer tm(ctx, KVF_STAGE_CALIBRATE, (double)H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4), st);
+    KVF_CUDA(launch_calib_partials(x, in_dtype, H, T, D, cpart, st));
+  }
+  if (cpart) KVF_CUDA(launch_calib_finalize(cpart, H, ctiles, T, D, d_scores, st));
+
+  out->qcols = qcols;
+  const size_t n = H * T * qcols;
+  const size_t plen = packed_len(n, dt);
+  const size_t np = num_params(H, T, qcols, axis);
+  out->packed_len = plen;
+  out->num_params = np;
+  out->d_scales = owner->alloc<float>(np);
+  out->d_mins = owner->alloc<float>(np);
+  if (!out->d_scales || !out->d_mins) return fail(KVF_ERR_CUDA, "allocation failed");
+  const bool do_ent = entropy && plen > 0;
+  out->has_freq = do_ent;
+  uint8_t* packed = do_ent ? sc.get<uint8_t>(plen) : owner->alloc<uint8_t>(plen);
+  if (!packed) return fail(KVF_ERR_CUDA, "allocation failed");
+  if (do_ent) {
+    out->d_freq = owner->alloc<uint32_t>(256);
+    if (!out->d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
+    KVF_CUDA(cudaMemsetAsync(out->d_freq, 0, 256 * sizeof(uint32_t), st));
+  }
+  {
+    StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n * (qdt == KVF_IN_F16 ? 2 : 4) + (double)plen + 8.0 * np, st);
+    KVF_TRY(quantize_into(sc, qin, qdt, H, T, qcols, dt, axis, packed, out->d_scales, out->d_mins,
+                          do_ent ? out->d_freq : nullptr, st));
+  }
+  if (do_ent) {
+    out->data_cap = rans_max_len(plen, kRansChunk);
+    out->d_data = owner->alloc<uint8_t>(out->data_cap);
+    out->d_len = owner->alloc<uint64_t>(1);
+    if (!out->d_data || !out->d_len) return fail(KVF_ERR_CUDA, "allocation failed");
+    StageTimer tm(ctx, KVF_STAGE_ENTROPY_ENCODE, (double)plen, st);
+    KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_data, out->d_len, st));
+    out->len_known = false;
+  } else {
+    out->d_data = packed;
+    out->data_cap = plen;
+    out->data_len = plen;
+    out->len_known = true;
+  }
+  return KVF_OK;
+}
+
+// decompress_tensor (crates/kvforge-cpu/src/pipeline.rs:75-97)
+kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStream_t st) {
+  Scratch sc(st);
+  const uint8_t* codes = t.d_data;
+  if (t.has_freq) {
+    RansTables* tab = sc.get<RansTables>(1);
+    uint8_t* dec = sc.get<uint8_t>(t.packed_len);
+    if (!tab || !dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    StageTimer tm(ctx, KVF_STAGE_ENTROPY_DECODE, 2.0 * t.packed_len, st);
+    KVF_CUDA(launch_rans_normalize(t.d_freq, tab, ctx->d_status, st));
+    KVF_CUDA(launch_rans_decode(t.d_data, t.data_len, t.len_known ? nullptr : t.d_len, tab, t.packed_len,
+                                dec, ctx->d_status, st));
+    codes = dec;
+  }
+  const double out_bytes = (double)t.H * t.T * t.D * 4 + (double)t.packed_len + 8.0 * t.num_params;
+  if (t.basis) {
+    StageTimer tm(ctx, KVF_STAGE_RECONSTRUCT, out_bytes + (double)t.H * t.basis->R * t.D * 4, st);
+    KVF_CUDA(launch_dequant_reconstruct(codes, nullptr, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T,
+                                        t.qcols, t.D, t.basis->d_vt, t.basis->d_ranks, ctx->exact_reconstruct,
+                                        out, st));
+  } else {
+    StageTimer tm(ctx, KVF_STAGE_DEQUANTIZE, out_bytes, st);
+    KVF_CUDA(launch_dequantize(codes, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T, t.D, out, st));
+  }
+  return KVF_OK;
+}
+
+kvf_status resolve_len(TensorC& t, cudaStream_t st) {
+  if (t.len_known) return KVF_OK;
+  uint64_t len = 0;
+  KVF_CUDA(cudaMemcpyAsync(&len, t.d_len, sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+  KVF_CUDA(cudaStreamSynchronize(st));
+  t.data_len = (size_t)len;
+  t.len_known = true;
+  return KVF_OK;
+}
+
+// CompressedTensor::size_bytes (types.rs:66-78 with 91-95, 131-135, 144-148)
+size_t tensor_size(const TensorC& t) {
+  size_t total = t.data_len + 2 * t.num_params * 4;
+  if (t.basis) total += t.H * t.basis->R * t.D * 4 + t.H * 8;
+  if (t.entropy) total += (t.has_freq ? 256 * 4 : 0) + 8;
+  return total;
+}
+
+// ---- fp64 symmetric eigen-solver for the basis step (cyclic Jacobi) ---------
+// A (n x n, row-major) is overwritten; eigenvalues land on its diagonal and the
+// eigenvectors in the columns of V.
+void jacobi_eigen(std::vector<double>& A, size_t n, std::vector<double>& V) {
+  V.assign(n * n, 0.0);
+  for (size_t i = 0; i < n; ++i) V[i * n + i] = 1.0;
+  double fro = 0.0;
+  for (double a : A) fro += a * a;
+  if (fro == 0.0) return;
+  for (int sweep = 0; sweep < 60; ++sweep) {
+    double off = 0.0;
+    for (size_t p = 0; p < n; ++p)
+      for (size_t q = p + 1; q < n; ++q) off += A[p * n + q] * A[p * n + q];
+    if (off <= 1e-30 * fro) break;
+    for (size_t p = 0; p + 1 < n; ++p) {
+      for (size_t q = p + 1; q < n; ++q) {
+        const double apq = A[p * n + q];
+        if (std::fabs(apq) <= 1e-300) continue;
+        const double theta = (A[q * n + q] - A[p * n + p]) / (2.0 * apq);
+        const double t = (theta >= 0 ? 1.0 : -1.0) / (std::fabs(theta) + std::sqrt(theta * theta + 1.0));
+        const double c = 1.0 / std::sqrt(t * t + 1.0), s = t * c;
+        for (size_t k = 0; k < n; ++k) {
+          const double akp = A[k * n + p], akq = A[k * n + q];
+          A[k * n + p] = c * akp - s * akq;
+          A[k * n + q] = s * akp + c * akq;
+        }
+        for (size_t k = 0; k < n; ++k) {
+          const double apk = A[p * n + k], aqk = A[q * n + k];
+          A[p * n + k] = c * apk - s * aqk;
+          A[q * n + k] = s * apk + c * aqk;
+        }
+        for (size_t k = 0; k < n; ++k) {
+          const double vkp = V[k * n + p], vkq = V[k * n + q];
+          V[k * n + p] = c * vkp - s * vkq;
+          V[k * n + q] = s * vkp + c * vkq;
+        }
+      }
+    }
+  }
+}
+
+// select_rank (crates/kvforge-cpu/src/projection.rs:31-59)
+size_t select_rank(const float* sv, size_t n, double threshold, size_t max_rank) {
+  if (n == 0) return 0;
+  double total = 0.0;
+  for (size_t i = 0; i < n; ++i) total += (double)sv[i] * (double)sv[i];
+  if (total < 1e-12) return 1;
+  double cum = 0.0;
+  size_t rank = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cum += (double)sv[i] * (double)sv[i];
+    rank += 1;
+    if (cum / total >= threshold) break;
+  }
+  if (max_rank > 0) rank = std::min(rank, max_rank);
+  return std::max<size_t>(rank, 1);
+}
+
+kvf_status upload_basis(BasisData& b) {
+  KVF_CUDA(cudaMalloc(&b.d_vt, std::max<size_t>(b.vt.size(), 1) * sizeof(float)));
+  KVF_CUDA(cudaMalloc(&b.d_ranks, std::max<size_t>(b.H, 1) * sizeof(uint64_t)));
+  if (!b.vt.empty()) KVF_CUDA(cudaMemcpy(b.d_vt, b.vt.data(), b.vt.size() * sizeof(float), cudaMemcpyHostToDevice));
+  if (b.H) KVF_CUDA(cudaMemcpy(b.d_ranks, b.ranks.data(), b.H * sizeof(uint64_t), cudaMemcpyHostToDevice));
+  return KVF_OK;
+}
+
+kvf_status compute_basis(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                         double threshold, size_t max_rank, std::shared_ptr<BasisData>* out,
+                         cudaStream_t st) {
+  if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
+  auto b = std::make_shared<BasisData>();
+  b->device = ctx->device;
+  b->H = H;
+  b->D = D;
+  std::vector<double> G(H * D * D);
+  {
+    Scratch sc(st);
+    const size_t tiles = gram_num_tiles(T);
+    float* partial = sc.get<float>(H * tiles * D * D);
+    double* gram = sc.get<double>(H * D * D);
+    if (!partial || !gram) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    StageTimer tm(ctx, KVF_STAGE_BASIS, (double)H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4), st);
+    KVF_CUDA(launch_gram(x, in_dtype, H, T, D, partial, gram, st));
+    KVF_CUDA(cudaMemcpyAsync(G.data(), gram, G.size() * sizeof(double), cudaMemcpyDeviceToHost, st));
+    KVF_CUDA(cudaStreamSynchronize(st));
+  }
+  b->sv.assign(H * D, 0.0f);
+  std::vector<float> full(H * D * D);
+  std::atomic<size_t> next{0};
+  auto worker = [&]() {
+    std::vector<double> A, V;
+    std::vector<size_t> idx(D);
+    for (size_t h = next++; h < H; h = next++) {
+      A.assign(G.begin() + h * D * D, G.begin() + (h + 1) * D * D);
+      jacobi_eigen(A, D, V);
+      for (size_t i = 0; i < D; ++i) idx[i] = i;
+      std::stable_sort(idx.begin(), idx.end(), [&](size_t a, size_t c) { return A[a * D + a] > A[c * D + c]; });
+      for (size_t r = 0; r < D; ++r) {
+        const size_t k = idx[r];
+        const double lam = A[k * D + k];
+        b->sv[h * D + r] = (float)std::sqrt(lam > 0.0 ? lam : 0.0);
+        size_t big = 0;
+        for (size_t c = 1; c < D; ++c)
+          if (std::fabs(V[c * D + k]) > std::fabs(V[big * D + k])) big = c;
+        const double sgn = V[big * D + k] < 0 ? -1.0 : 1.0;
+        for (size_t c = 0; c < D; ++c) full[(h * D + r) * D + c] = (float)(sgn * V[c * D + k]);
+      }
+    }
+  };
+  const size_t nth = std::max<size_t>(1, std::min<size_t>(H, std::thread::hardware_concurrency()));
+  std::vector<std::thread> pool;
+  for (size_t i = 1; i < nth; ++i) pool.emplace_back(worker);
+  worker();
+  for (auto& th : pool) th.join();
+  const size_t k = std::min(T, D);  // the SVD yields min(T, D) singular values
+  b->ranks.assign(H, 1);
+  size_t R = 0;
+  for (size_t h = 0; h < H; ++h) {
+    b->ranks[h] = select_rank(&b->sv[h * D], k, threshold, max_rank);
+    R = std::max<size_t>(R, b->ranks[h]);
+  }
+  if (H == 0) R = 1;  // ranks.iter().max().unwrap_or(&1)
+  b->R = R;
+  b->vt.assign(H * R * D, 0.0f);
+  for (size_t h = 0; h < H; ++h)
+    for (size_t r = 0; r < b->ranks[h]; ++r)
+      std::memcpy(&b->vt[(h * R + r) * D], &full[(h * D + r) * D], D * sizeof(float));
+  KVF_TRY(upload_basis(*b));
+  *out = b;
+  return KVF_OK;
+}
+
+// ---- serialisation helpers --------------------------------------------------
+struct Writer {
+  uint8_t* buf;
+  size_t cap, len = 0;
+  void put(const void* p, size_t n) {
+    if (buf && len + n <= cap) std::memcpy(buf + len, p, n);
+    len += n;
+  }
+  template <class T>
+  void v(T x) { put(&x, sizeof(T)); }
+};
+struct Reader {
+  const uint8_t* buf;
+  size_t len, pos = 0;
+  bool ok = true;
+  bool get(void* p, size_t n) {
+    if (!ok || pos + n > len) { ok = false; return false; }
+    std::memcpy(p, buf + pos, n);
+    pos += n;
+    return true;
+  }
+  template <class T>
+  T v() { T x{}; get(&x, sizeof(T)); return x; }
+};
+
+constexpr uint32_t kSerMagic = 0x4346564Bu;  // "KVFC"
+constexpr uint32_t kSerVersion = 1;
+
+kvf_status ser_tensor(TensorC& t, Writer& w, cudaStream_t st) {
+  KVF_TRY(resolve_len(t, st));
+  w.v<int32_t>(t.data_type);
+  w.v<int32_t>(t.axis);
+  w.v<int32_t>(t.basis ? 1 : 0);
+  w.v<int32_t>(t.entropy ? 1 : 0);
+  w.v<int32_t>(t.has_freq ? 1 : 0);
+  w.v<uint64_t>(t.qcols);
+  w.v<uint64_t>(t.packed_len);
+  w.v<uint64_t>(t.data_len);
+  w.v<uint64_t>(t.num_params);
+  std::vector<uint8_t> host;
+  auto dl = [&](const void* d, size_t n) -> kvf_status {
+    host.resize(n);
+    if (n) {
+      KVF_CUDA(cudaMemcpyAsync(host.data(), d, n, cudaMemcpyDeviceToHost, st));
+      KVF_CUDA(cudaStreamSynchronize(st));
+    }
+    w.put(host.data(), n);
+    return KVF_OK;
+  };
+  if (t.basis) {
+    w.put(t.basis->ranks.data(), t.H * sizeof(uint64_t));
+    w.put(t.basis->vt.data(), t.basis->vt.size() * sizeof(float));
+  }
+  KVF_TRY(dl(t.d_scales, t.num_params * 4));
+  KVF_TRY(dl(t.d_mins, t.num_params * 4));
+  if (t.has_freq) KVF_TRY(dl(t.d_freq, 256 * 4));
+  KVF_TRY(dl(t.d_data, t.data_len));
+  return KVF_OK;
+}
+
+kvf_status deser_tensor(kvf_compressed* c, TensorC& t, Reader& r, cudaStream_t st) {
+  t.H = c->H; t.T = c->T; t.D = c->D;
+  t.data_type = r.v<int32_t>();
+  t.axis = r.v<int32_t>();
+  const bool proj = r.v<int32_t>() != 0;
+  t.entropy = r.v<int32_t>() != 0;
+  t.has_freq = r.v<int32_t>() != 0;
+  t.qcols = r.v<uint64_t>();
+  t.packed_len = r.v<uint64_t>();
+  t.data_len = r.v<uint64_t>();
+  t.num_params = r.v<uint64_t>();
+  if (!r.ok) return fail(KVF_ERR_SERIALIZATION, "truncated tensor header");
+  KVF_TRY(check_qcfg(t.data_type, t.axis));
+  const size_t n = t.H * t.T * t.qcols;
+  if (t.packed_len != packed_len(n, t.data_type) || t.num_params != num_params(t.H, t.T, t.qcols, t.axis) ||
+      (!t.has_freq && t.data_len != t.packed_len) || (t.has_freq && !t.entropy) || (!proj && t.qcols != t.D))
+    return fail(KVF_ERR_SERIALIZATION, "inconsistent tensor header");
+  if (proj) {
+    auto b = std::make_shared<BasisData>();
+    b->device = c->device;
+    b->H = t.H; b->R = t.qcols; b->D = t.D;
+    b->ranks.resize(t.H);
+    b->vt.resize(t.H * t.qcols * t.D);
+    if (!r.get(b->ranks.data(), t.H * 8) || !r.get(b->vt.data(), b->vt.size() * 4))
+      return fail(KVF_ERR_SERIALIZATION, "truncated projection state");
+    for (uint64_t rk : b->ranks)
+      if (rk > t.qcols) return fail(KVF_ERR_SERIALIZATION, "rank exceeds the projected width");
+    KVF_TRY(upload_basis(*b));
+    t.basis = b;
+  }
+  auto up = [&](void* d, size_t nbytes) -> kvf_status {
+    if (r.pos + nbytes > r.len) return fail(KVF_ERR_SERIALIZATION, "truncated payload");
+    if (nbytes) KVF_CUDA(cudaMemcpyAsync(d, r.buf + r.pos, nbytes, cudaMemcpyHostToDevice, st));
+    r.pos += nbytes;
+    return KVF_OK;
+  };
+  t.d_scales = c->alloc<float>(t.num_params);
+  t.d_mins = c->alloc<float>(t.num_params);
+  if (!t.d_scales || !t.d_mins) return fail(KVF_ERR_CUDA, "allocation failed");
+  KVF_TRY(up(t.d_scales, t.num_params * 4));
+  KVF_TRY(up(t.d_mins, t.num_params * 4));
+  if (t.has_freq) {
+    t.d_freq = c->alloc<uint32_t>(256);
+    if (!t.d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
+    KVF_TRY(up(t.d_freq, 256 * 4));
+  }
+  t.data_cap = t.data_len;
+  t.d_data = c->alloc<uint8_t>(t.data_len);
+  if (!t.d_data) return fail(KVF_ERR_CUDA, "allocation failed");
+  KVF_TRY(up(t.d_data, t.data_len));
+  t.len_known = true;
+  if (t.has_freq && t.data_len % 4 != 0)
+    return fail(KVF_ERR_ENTROPY, "Compressed data length not aligned to 4 bytes");
+  return KVF_OK;
+}
+
+kvf_status read_status(kvf_ctx* ctx, cudaStream_t st) {
+  unsigned bits = 0;
+  KVF_CUDA(cudaMemcpyAsync(&bits, ctx->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  KVF_CUDA(cudaStreamSynchronize(st));
+  if (bits) {
+    KVF_CUDA(cudaMemsetAsync(ctx->d_status, 0, sizeof(unsigned), st));
+    KVF_CUDA(cudaStreamSynchronize(st));
+    if (bits & kDevErrCorrupt) return fail(KVF_ERR_CORRUPT_STREAM, "rANS container failed validation");
+    if (bits & kDevErrTimeout) return fail(KVF_ERR_DEVICE_TIMEOUT, "a bounded device wait expired");
+    return fail(KVF_ERR_ENTROPY, "entropy model could not be built");
+  }
+  return KVF_OK;
+}
+
+}  // namespace
+
+// =============================================================================
+extern "C" {
+
+int kvf_abi_version(void) { return KVF_ABI_VERSION; }
+const char* kvf_last_error(void) { return g_err.c_str(); }
+
+kvf_status kvf_init(int device, kvf_ctx** out) {
+  if (!out) return fail(KVF_ERR_INVALID_CONFIG, "null output pointer");
+  int n = 0;
+  KVF_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(KVF_ERR_CUDA, "device ordinal out of range");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(KVF_ERR_CUDA, "cudaSetDevice failed");
+  auto* ctx = new kvf_ctx();
+  ctx->device = device;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;  // keep freed blocks cached in this process's pool
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  cudaError_t e = cudaMalloc(&ctx->d_status, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(unsigned));
+  if (e != cudaSuccess) {
+    delete ctx;
+    return fail(KVF_ERR_CUDA, std::string("context allocation: ") + cudaGetErrorString(e));
+  }
+  *out = ctx;
+  return KVF_OK;
+}
+
+kvf_status kvf_destroy(kvf_ctx* ctx) {
+  if (!ctx) return KVF_OK;
+  DeviceGuard g(ctx->device);
+  for (auto& r : ctx->recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : ctx->spare) cudaEventDestroy(e);
+  cudaFree(ctx->d_status);
+  delete ctx;
+  return KVF_OK;
+}
+
+kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact) {
+  KVF_TRY(check_ctx(ctx));
+  ctx->exact_reconstruct = exact ? 1 : 0;
+  return KVF_OK;
+}
+
+kvf_status kvf_sync(kvf_ctx* ctx, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  DeviceGuard g(ctx->device);
+  KVF_CUDA(cudaStreamSynchronize(S(stream)));
+  KVF_CUDA(cudaGetLastError());
+  return read_status(ctx, S(stream));
+}
+
+uint64_t kvf_launch_count(void) { return kvf::g_launches.load(std::memory_order_relaxed); }
+
+const char* kvf_stage_name(int32_t stage) {
+  static const char* names[KVF_NUM_STAGES] = {"calibrate", "project", "quantize", "entropy_encode",
+                                              "entropy_decode", "reconstruct", "dequantize", "basis"};
+  return (stage >= 0 && stage < KVF_NUM_STAGES) ? names[stage] : "unknown";
+}
+
+kvf_status kvf_profile_enable(kvf_ctx* ctx, int enable) {
+  KVF_TRY(check_ctx(ctx));
+  ctx->profile = enable ? 1 : 0;
+  return KVF_OK;
+}
+
+kvf_status kvf_profile_read(kvf_ctx* ctx, double* ms, uint64_t* count, double* bytes) {
+  KVF_TRY(check_ctx(ctx));
+  DeviceGuard g(ctx->device);
+  for (int i = 0; i < KVF_NUM_STAGES; ++i) {
+    if (ms) ms[i] = 0.0;
+    if (count) count[i] = 0;
+    if (bytes) bytes[i] = 0.0;
+  }
+  kvf_status st = KVF_OK;
+  for (auto& r : ctx->recs) {
+    float t = 0.0f;
+    cudaError_t e = cudaEventSynchronize(r.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.a, r.b);
+    if (e != cudaSuccess && st == KVF_OK) st = fail(KVF_ERR_CUDA, cudaGetErrorString(e));
+    if (r.stage >= 0 && r.stage < KVF_NUM_STAGES) {
+      if (ms) ms[r.stage] += t;
+      if (count) count[r.stage] += 1;
+      if (bytes) bytes[r.stage] += r.bytes;
+    }
+    ctx->spare.push_back(r.a);
+    ctx->spare.push_back(r.b);
+  }
+  ctx->recs.clear();
+  return st;
+}
+
+kvf_status kvf_pipeline_config_from_preset(int32_t preset, kvf_pipeline_config* out) {
+  if (!out) return fail(KVF_ERR_INVALID_CONFIG, "null output pointer");
+  kvf_pipeline_config c{};
+  c.preset = preset;
+  switch (preset) {  // crates/kvforge-core/src/pipeline.rs:31-70
+    case KVF_CONSERVATIVE:
+      c = {preset, KVF_INT8, KVF_INT8, 0, 0.99, 0, 0};
+      break;
+    case KVF_BALANCED:
+      c = {preset, KVF_INT4, KVF_INT4, 1, 0.90, 0, 0};
+      break;
+    case KVF_AGGRESSIVE:
+      c = {preset, KVF_INT4, KVF_INT4, 1, 0.75, 1, 1};
+      break;
+    case KVF_ADAPTIVE:
+      c = {preset, KVF_INT4, KVF_INT4, 1, 0.90, 1, 1};
+      break;
+    default:
+      return fail(KVF_ERR_INVALID_CONFIG, "unknown preset");
+  }
+  *out = c;
+  return KVF_OK;
+}
+
+kvf_status kvf_calibrate(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_t H, size_t T, size_t D,
+                         size_t min_tokens, float* scores, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (T < min_tokens)
+    return fail(KVF_ERR_INVALID_CONFIG, "Need at least " + std::to_string(min_tokens) +
+                                            " tokens for calibration, got " + std::to_string(T));
+  DeviceGuard g(ctx->device);
+  Scratch sc(S(stream));
+  const size_t tiles = calib_partial_tiles(T, D);
+  double* cpart = sc.get<double>(2 * H * tiles);
+  if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_calib_partials(keys, in_dtype, H, T, D, cpart, S(stream)));
+  KVF_CUDA(launch_calib_finalize(cpart, H, tiles, T, D, scores, S(stream)));
+  return KVF_OK;
+}
+
+kvf_status kvf_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
+                        int32_t data_type, int32_t axis, uint8_t* packed, float* scales, float* mins,
+                        void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_qcfg(data_type, axis));
+  KVF_TRY(check_shape(H, T, D));
+  DeviceGuard g(ctx->device);
+  Scratch sc(S(stream));
+  return quantize_into(sc, data, in_dtype, H, T, D, data_type, axis, packed, scales, mins, nullptr, S(stream));
+}
+
+kvf_status kvf_dequantize(kvf_ctx* ctx, const uint8_t* packed, size_t plen, const float* scales,
+                          const float* mins, int32_t data_type, int32_t axis, size_t H, size_t T, size_t D,
+                          float* out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (data_type == KVF_F32) return fail(KVF_ERR_QUANTIZATION, "Cannot dequantize F32 data type");
+  KVF_TRY(check_qcfg(data_type, axis));
+  KVF_TRY(check_shape(H, T, D));
+  const size_t total = H * T * D;
+  // quantize.rs:171-197: INT4 unpacks 2 values per byte then truncates
+  const size_t got = data_type == KVF_INT4 ? std::min(2 * plen, total) : plen;
+  if (got != total)
+    return fail(KVF_ERR_QUANTIZATION, "Expected " + std::to_string(total) + " values, got " +
+                                          std::to_string(data_type == KVF_INT4 ? 2 * plen : plen));
+  DeviceGuard g(ctx->device);
+  KVF_CUDA(launch_dequantize(packed, scales, mins, data_type, axis, H, T, D, out, S(stream)));
+  return KVF_OK;
+}
+
+kvf_status kvf_project(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
+                       const float* basis_vt, const uint64_t* ranks, size_t R, float* projected,
+                       void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
+  if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
+  DeviceGuard g(ctx->device);
+  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, projected, nullptr, S(stream)));
+  return KVF_OK;
+}
+
+kvf_status kvf_reconstruct(kvf_ctx* ctx, const float* projected, size_t H, size_t T, size_t R, size_t D,
+                           const float* basis_vt, const uint64_t* ranks, float* out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_shape(H, T, D));
+  if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
+  DeviceGuard g(ctx->device);
+  KVF_CUDA(launch_dequant_reconstruct(nullptr, projected, nullptr, nullptr, KVF_F32, KVF_PER_TOKEN, H, T, R, D,
+                                      basis_vt, ranks, ctx->exact_reconstruct, out, S(stream)));
+  return KVF_OK;
+}
+
+kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T,
+                                      size_t D, const float* basis_vt, const uint64_t* ranks, size_t R,
+                                      int32_t data_type, int32_t axis, uint8_t* packed, float* scales,
+                                      float* mins, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_qcfg(data_type, axis));
+  KVF_TRY(check_shape(H, T, D));
+  if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
+  if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
+  DeviceGuard g(ctx->device);
+  Scratch sc(S(stream));
+  float* P = sc.get<float>(H * T * R);
+  if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, P, nullptr, S(stream)));
+  return quantize_into(sc, P, KVF_IN_F32, H, T, R, data_type, axis, packed, scales, mins, nullptr, S(stream));
+}
+
+size_t kvf_rans_max_encoded_len(size_t n) { return rans_max_len(n, kRansChunk); }
+
+kvf_status kvf_rans_encode(kvf_ctx* ctx, const uint8_t* data, size_t n, uint8_t* out, size_t out_cap,
+                           size_t* out_len_host, uint32_t* freq, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (!out_len_host) return fail(KVF_ERR_INVALID_CONFIG, "null length pointer");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  KVF_CUDA(cudaMemsetAsync(freq, 0, 256 * sizeof(uint32_t), st));
+  if (n == 0) {
+    *out_len_host = 0;
+    return KVF_OK;
+  }
+  if (out_cap < rans_max_len(n, kRansChunk)) return fail(KVF_ERR_ENTROPY, "output capacity too small");
+  if (!aligned(out, 4)) return fail(KVF_ERR_INVALID_CONFIG, "output buffer must be 4-byte aligned");
+  Scratch sc(st);
+  uint64_t* d_len = sc.get<uint64_t>(1);
+  if (!d_len) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_histogram(data, n, freq, st));
+  KVF_TRY(rans_encode_into(ctx, sc, data, n, freq, out, d_len, st));
+  uint64_t len = 0;
+  KVF_CUDA(cudaMemcpyAsync(&len, d_len, sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+  KVF_TRY(read_status(ctx, st));
+  *out_len_host = (size_t)len;
+  return KVF_OK;
+}
+
+kvf_status kvf_rans_decode(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len, const uint32_t* freq,
+                           size_t original_len, uint8_t* out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (original_len == 0) return KVF_OK;
+  if (comp_len % 4 != 0) return fail(KVF_ERR_ENTROPY, "Compressed data length not aligned to 4 bytes");
+  if (!aligned(comp, 4)) return fail(KVF_ERR_INVALID_CONFIG, "container must be 4-byte aligned");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  Scratch sc(st);
+  RansTables* tab = sc.get<RansTables>(1);
+  if (!tab) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
+  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, tab, original_len, out, ctx->d_status, st));
+  return read_status(ctx, st);
+}
+
+kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len,
+                                      const uint32_t* freq, const float* scales, const float* mins,
+                                      int32_t data_type, int32_t axis, size_t H, size_t T, size_t D,
+                                      float* out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_qcfg(data_type, axis));
+  KVF_TRY(check_shape(H, T, D));
+  if (comp_len % 4 != 0) return fail(KVF_ERR_ENTROPY, "Compressed data length not aligned to 4 bytes");
+  if (!aligned(comp, 4)) return fail(KVF_ERR_INVALID_CONFIG, "container must be 4-byte aligned");
+  const size_t plen = packed_len(H * T * D, data_type);
+  if (plen == 0) return KVF_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  Scratch sc(st);
+  RansTables* tab = sc.get<RansTables>(1);
+  uint8_t* dec = sc.get<uint8_t>(plen);
+  if (!tab || !dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
+  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, tab, plen, dec, ctx->d_status, st));
+  KVF_CUDA(launch_dequantize(dec, scales, mins, data_type, axis, H, T, D, out, st));
+  return KVF_OK;
+}
+
+// ---- basis ------------------------------------------------------------------
+kvf_status kvf_basis_compute(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
+                             double variance_threshold, size_t max_rank, kvf_basis** out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (!out) return fail(KVF_ERR_INVALID_CONFIG, "null output pointer");
+  DeviceGuard g(ctx->device);
+  std::shared_ptr<BasisData> b;
+  KVF_TRY(compute_basis(ctx, data, in_dtype, H, T, D, variance_threshold, max_rank, &b, S(stream)));
+  *out = new kvf_basis{b};
+  return KVF_OK;
+}
+
+kvf_status kvf_basis_from_host(kvf_ctx* ctx, size_t H, size_t R, size_t D, const float* basis_vt_host,
+                               const uint64_t* ranks_host, kvf_basis** out) {
+  KVF_TRY(check_ctx(ctx));
+  if (!out || (H && (!basis_vt_host || !ranks_host))) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
+  DeviceGuard g(ctx->device);
+  auto b = std::make_shared<BasisData>();
+  b->device = ctx->device;
+  b->H = H; b->R = R; b->D = D;
+  b->vt.assign(basis_vt_host, basis_vt_host + H * R * D);
+  b->ranks.assign(ranks_host, ranks_host + H);
+  for (uint64_t r : b->ranks)
+    if (r > R) return fail(KVF_ERR_PROJECTION, "rank exceeds the projected width");
+  KVF_TRY(upload_basis(*b));
+  *out = new kvf_basis{b};
+  return KVF_OK;
+}
+
+kvf_status kvf_basis_info(const kvf_basis* b, size_t* H, size_t* R, size_t* D) {
+  if (!b) return fail(KVF_ERR_INVALID_CONFIG, "null basis");
+  if (H) *H = b->d->H;
+  if (R) *R = b->d->R;
+  if (D) *D = b->d->D;
+  return KVF_OK;
+}
+
+kvf_status kvf_basis_download(const kvf_basis* b, float* vt, uint64_t* ranks, float* sv) {
+  if (!b) return fail(KVF_ERR_INVALID_CONFIG, "null basis");
+  const BasisData& d = *b->d;
+  if (vt) std::memcpy(vt, d.vt.data(), d.vt.size() * sizeof(float));
+  if (ranks) std::memcpy(ranks, d.ranks.data(), d.H * sizeof(uint64_t));
+  if (sv) {
+    if (d.sv.empty()) std::memset(sv, 0, d.H * d.D * sizeof(float));
+    else std::memcpy(sv, d.sv.data(), d.sv.size() * sizeof(float));
+  }
+  return KVF_OK;
+}
+
+const float* kvf_basis_device_vt(const kvf_basis* b) { return b ? b->d->d_vt : nullptr; }
+const uint64_t* kvf_basis_device_ranks(const kvf_basis* b) { return b ? b->d->d_ranks : nullptr; }
+
+kvf_status kvf_basis_free(kvf_basis* b) {
+  delete b;
+  return KVF_OK;
+}
+
+// ---- whole layer --------------------------------------------------------------
+kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values, int32_t in_dtype, size_t H,
+                              size_t T, size_t D, size_t layer_idx, const kvf_pipeline_config* cfg,
+                              const kvf_basis* k_basis, const kvf_basis* v_basis, kvf_compressed** out,
+                              void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (!cfg || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  std::unique_ptr<kvf_compressed> c(new kvf_compressed());
+  c->ctx = ctx;
+  c->device = ctx->device;
+  c->stream = st;
+  c->layer_idx = layer_idx;
+  c->H = H; c->T = T; c->D = D;
+  c->original_size_bytes = 2 * H * T * D * 4;  // KVCache::size_bytes, f32 (types.rs:30-32)
+  std::shared_ptr<BasisData> kb, vb;
+  if (cfg->enable_projection) {
+    if (k_basis) kb = k_basis->d;
+    else KVF_TRY(compute_basis(ctx, keys, in_dtype, H, T, D, cfg->projection_variance_threshold, 0, &kb, st));
+    if (v_basis) vb = v_basis->d;
+    else KVF_TRY(compute_basis(ctx, values, in_dtype, H, T, D, cfg->projection_variance_threshold, 0, &vb, st));
+  }
+  if (cfg->enable_calibration && T >= 64 && H > 0) {
+    c->d_scores = c->alloc<float>(H);
+    if (!c->d_scores) return fail(KVF_ERR_CUDA, "allocation failed");
+  }
+  kvf_status s = compress_tensor(ctx, c.get(), keys, in_dtype, H, T, D, cfg->key_data_type, KVF_PER_CHANNEL, kb,
+                                 cfg->enable_entropy_coding != 0, cfg->enable_calibration != 0, c->d_scores,
+                                 &c->key, st);
+  if (s == KVF_OK)
+    s = compress_tensor(ctx, c.get(), values, in_dtype, H, T, D, cfg->value_data_type, KVF_PER_TOKEN, vb,
+                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, st);
+  if (s != KVF_OK) {
+    std::string msg = g_err;
+    kvf_compressed_free(c.release());
+    g_err = msg;
+    return s;
+  }
+  *out = c.release();
+  return KVF_OK;
+}
+
+kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* keys_out, float* values_out,
+                                void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
+  DeviceGuard g(ctx->device);
+  KVF_TRY(decompress_tensor(ctx, c->key, keys_out, S(stream)));
+  KVF_TRY(decompress_tensor(ctx, c->value, values_out, S(stream)));
+  return KVF_OK;
+}
+
+kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host, int32_t in_dtype,
+                                   size_t H, size_t T, size_t D, size_t layer_idx, const kvf_pipeline_config* cfg,
+                                   const kvf_basis* k_basis, const kvf_basis* v_basis, kvf_compressed** out,
+                                   void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  const size_t bytes = H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4);
+  kvf_status s;
+  {
+    Scratch sc(st);
+    uint8_t* dk = sc.get<uint8_t>(bytes);
+    uint8_t* dv = sc.get<uint8_t>(bytes);
+    if (!dk || !dv) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    if (bytes) {
+      KVF_CUDA(cudaMemcpyAsync(dk, keys_host, bytes, cudaMemcpyHostToDevice, st));
+      KVF_CUDA(cudaMemcpyAsync(dv, values_host, bytes, cudaMemcpyHostToDevice, st));
+    }
+    s = kvf_compress_layer(ctx, dk, dv, in_dtype, H, T, D, layer_idx, cfg, k_basis, v_basis, out, stream);
+  }
+  if (s != KVF_OK) return s;
+  KVF_CUDA(cudaStreamSynchronize(st));
+  return KVF_OK;
+}
+
+kvf_status kvf_decompress_layer_host(kvf_ctx* ctx, const kvf_compressed* c, float* keys_host, float* values_host,
+                                     void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  const size_t bytes = c->H * c->T * c->D * 4;
+  {
+    Scratch sc(st);
+    float* dk = sc.get<float>(c->H * c->T * c->D);
+    float* dv = sc.get<float>(c->H * c->T * c->D);
+    if (!dk || !dv) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    KVF_TRY(kvf_decompress_layer(ctx, c, dk, dv, stream));
+    if (bytes) {
+      KVF_CUDA(cudaMemcpyAsync(keys_host, dk, bytes, cudaMemcpyDeviceToHost, st));
+      KVF_CUDA(cudaMemcpyAsync(values_host, dv, bytes, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  KVF_CUDA(cudaStreamSynchronize(st));
+  return read_status(ctx, st);
+}
+
+kvf_status kvf_compressed_shape(const kvf_compressed* c, size_t* H, size_t* T, size_t* D, size_t* layer_idx) {
+  if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
+  if (H) *H = c->H;
+  if (T) *T = c->T;
+  if (D) *D = c->D;
+  if (layer_idx) *layer_idx = c->layer_idx;
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_size_bytes(kvf_compressed* c, size_t* out) {
+  if (!c || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(c->device);
+  KVF_TRY(resolve_len(c->key, c->stream));
+  KVF_TRY(resolve_len(c->value, c->stream));
+  *out = tensor_size(c->key) + tensor_size(c->value);
+  return KVF_OK;
+}
+
+kvf_status kvf_original_size_bytes(const kvf_compressed* c, size_t* out) {
+  if (!c || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  *out = c->original_size_bytes;
+  return KVF_OK;
+}
+
+kvf_status kvf_compression_ratio(kvf_compressed* c, double* out) {
+  size_t comp = 0;
+  KVF_TRY(kvf_compressed_size_bytes(c, &comp));
+  if (!out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  *out = (double)c->original_size_bytes / (double)comp;  // types.rs:34-36
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_tensor_info(kvf_compressed* c, int32_t which, size_t* R, size_t* plen, size_t* dlen,
+                                      int32_t* has_entropy) {
+  if (!c || (which != 0 && which != 1)) return fail(KVF_ERR_INVALID_CONFIG, "bad arguments");
+  TensorC& t = which == 0 ? c->key : c->value;
+  DeviceGuard g(c->device);
+  KVF_TRY(resolve_len(t, c->stream));
+  if (R) *R = t.basis ? t.basis->R : 0;
+  if (plen) *plen = t.packed_len;
+  if (dlen) *dlen = t.data_len;
+  if (has_entropy) *has_entropy = t.entropy ? 1 : 0;
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_tensor_views(const kvf_compressed* c, int32_t which, const uint8_t** data,
+                                       const float** scales, const float** mins, const uint32_t** freq,
+                                       const float** basis_vt, const uint64_t** ranks) {
+  if (!c || (which != 0 && which != 1)) return fail(KVF_ERR_INVALID_CONFIG, "bad arguments");
+  const TensorC& t = which == 0 ? c->key : c->value;
+  if (data) *data = t.d_data;
+  if (scales) *scales = t.d_scales;
+  if (mins) *mins = t.d_mins;
+  if (freq) *freq = t.d_freq;
+  if (basis_vt) *basis_vt = t.basis ? t.basis->d_vt : nullptr;
+  if (ranks) *ranks = t.basis ? t.basis->d_ranks : nullptr;
+  return KVF_OK;
+}
+
+const float* kvf_compressed_calibration(const kvf_compressed* c) { return c ? c->d_scores : nullptr; }
+
+kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf, size_t cap, size_t* len) {
+  if (!c || !len) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(c->device);
+  Writer w{buf, buf ? cap : 0};
+  w.v<uint32_t>(kSerMagic);
+  w.v<uint32_t>(kSerVersion);
+  w.v<uint64_t>(c->layer_idx);
+  w.v<uint64_t>(c->H);
+  w.v<uint64_t>(c->T);
+  w.v<uint64_t>(c->D);
+  w.v<uint64_t>(c->original_size_bytes);
+  KVF_TRY(ser_tensor(c->key, w, c->stream));
+  KVF_TRY(ser_tensor(c->value, w, c->stream));
+  *len = w.len;
+  if (buf && w.len > cap) return fail(KVF_ERR_SERIALIZATION, "buffer too small");
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf, size_t len, kvf_compressed** out,
+                                      void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (!buf || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(ctx->device);
+  Reader r{buf, len};
+  if (r.v<uint32_t>() != kSerMagic || r.v<uint32_t>() != kSerVersion)
+    return fail(KVF_ERR_SERIALIZATION, "not a serialised compressed layer");
+  std::unique_ptr<kvf_compressed> c(new kvf_compressed());
+  c->ctx = ctx;
+  c->device = ctx->device;
+  c->stream = S(stream);
+  c->layer_idx = r.v<uint64_t>();
+  c->H = r.v<uint64_t>();
+  c->T = r.v<uint64_t>();
+  c->D = r.v<uint64_t>();
+  c->original_size_bytes = r.v<uint64_t>();
+  if (!r.ok) return fail(KVF_ERR_SERIALIZATION, "truncated header");
+  if (check_shape(c->H, c->T, c->D) != KVF_OK) return fail(KVF_ERR_SERIALIZATION, "bad shape");
+  kvf_status s = deser_tensor(c.get(), c->key, r, c->stream);
+  if (s == KVF_OK) s = deser_tensor(c.get(), c->value, r, c->stream);
+  if (s == KVF_OK && r.pos != r.len) s = fail(KVF_ERR_SERIALIZATION, "trailing bytes");
+  if (s == KVF_OK) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (s != KVF_OK) {
+    std::string msg = g_err;
+    kvf_compressed_free(c.release());
+    g_err = msg;
+    return s;
+  }
+  *out = c.release();
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_free(kvf_compressed* c) {
+  if (!c) return KVF_OK;
+  {
+    DeviceGuard g(c->device);
+    for (void* p : c->owned) cudaFreeAsync(p, c->stream);
+  }
+  delete c;
+  return KVF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+// Internal declarations shared by the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/kvforge.h"
+
+namespace kvf {
+
+// ---- rANS container constants (documented in kvf_rans.cu) ----------------
+constexpr uint32_t kRansProbBits = 15;
+constexpr uint32_t kRansM = 1u << kRansProbBits;
+constexpr uint32_t kRansL = 1u << 16;
+constexpr uint32_t kRansLanes = 32;
+constexpr uint32_t kRansChunk = 16384;       // symbols per chunk (encoder default)
+constexpr uint32_t kRansMagic = 0x3152564Bu;  // "KVR1"
+constexpr size_t kRansHeader = 32;
+constexpr size_t kRansChunkHeader = 4 + 4 * kRansLanes;  // nwords + 32 lane states
+
+// device status bits (ctx->d_status); mapped to kvf_status by the host
+constexpr unsigned kDevErrCorrupt = 1u;
+constexpr unsigned kDevErrEntropy = 2u;
+constexpr unsigned kDevErrTimeout = 4u;
+
+// normalised model + decode table built on the device from 256 counts
+struct RansTables {
+  uint32_t q[256];     // quantised frequencies, sum 2^15
+  uint32_t cum[256];   // exclusive prefix of q
+  uint32_t rcp[256];   // 0xFFFFFFFF / q  (exact division with one correction)
+  uint8_t slot2sym[kRansM];
+};
+
+__host__ __device__ inline size_t rans_num_chunks(size_t n, uint32_t chunk) { return (n + chunk - 1) / chunk; }
+__host__ __device__ inline size_t rans_slot_words(uint32_t chunk) { return chunk + 2; }
+__host__ __device__ inline size_t rans_slot_bytes(uint32_t chunk) {
+  size_t b = kRansChunkHeader + 2 * rans_slot_words(chunk);
+  return (b + 15) & ~size_t(15);
+}
+inline size_t rans_max_len(size_t n, uint32_t chunk) {
+  size_t nc = rans_num_chunks(n, chunk);
+  return kRansHeader + 4 * (nc + 1) + nc * (kRansChunkHeader + 2) + 2 * n;
+}
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline float quant_levels(int dt) { return dt == KVF_INT4 ? 15.0f : 255.0f; }
+inline size_t packed_len(size_t n, int dt) { return dt == KVF_INT4 ? (n + 1) / 2 : n; }
+inline size_t num_params(size_t H, size_t T, size_t D, int axis) {
+  return axis == KVF_PER_CHANNEL ? H * D : H * T;
+}
+
+// process-wide count of kernels launched by this library (kvf_launch_count)
+void note_launches(unsigned n);
+
+// ---- kernel launchers (return the launch error, if any) -------------------
+// quantization (kvf_quant.cu)
+cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                                  int data_type, int axis, uint8_t* codes, float* scales,
+                                  float* mins, int* minmax_keys, cudaStream_t st);
+cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,
+                             cudaStream_t st);
+cudaError_t launch_histogram(const uint8_t* data, size_t n, uint32_t* hist, cudaStream_t st);
+cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, const float* mins,
+                              int data_type, int axis, size_t H, size_t T, size_t D, float* out,
+                              cudaStream_t st);
+
+// projection / calibration / gram (kvf_project.cu)
+size_t project_num_tiles(size_t T);
+cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                           const float* basis_vt, const uint64_t* ranks, size_t R, float* P,
+                           double* calib_part, cudaStream_t st);
+size_t calib_partial_tiles(size_t T, size_t D);
+cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                                  double* calib_part, cudaStream_t st);
+cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t tiles, size_t T,
+                                  size_t D, float* scores, cudaStream_t st);
+// packed codes (or raw f32 when data_type == KVF_F32) + params + basis -> f32 [H,T,D]
+cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
+                                       const float* mins, int data_type, int axis, size_t H,
+                                       size_t T, size_t R, size_t D, const float* basis_vt,
+                                       const uint64_t* ranks, int exact, float* out,
+                                       cudaStream_t st);
+size_t gram_num_tiles(size_t T);
+cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                        float* partial, double* gram, cudaStream_t st);
+
+// rANS (kvf_rans.cu)
+cudaError_t launch_rans_normalize(const uint32_t* freq, RansTables* tab, unsigned* status,
+                                  cudaStream_t st);
+cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk,
+                               const RansTables* tab, uint8_t* slots, cudaStream_t st);
+cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk, uint8_t* out,
+                                 uint64_t* out_len, cudaStream_t st);
+// comp_len_dev (when not NULL) supplies the container length from device memory
+cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
+                               const RansTables* tab, size_t n, uint8_t* out, unsigned* status,
+                               cudaStream_t st);
+
+}  // namespace kvf

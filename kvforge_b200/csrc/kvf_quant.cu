@@ -1,0 +1,479 @@
+// KIVI quantize / dequantize kernels (sm_100a).
+//
+// Arithmetic follows crates/kvforge-cpu/src/quantize.rs exactly:
+//   scale = (max - min) < 1e-10 ? 1 : (max - min) / levels          (quantize.rs:88-89)
+//   q     = clamp(round_half_away((v - min) / scale), 0, levels)     (quantize.rs:95, 124)
+//   x     = q * scale + min   (separate multiply and add)            (quantize.rs:210, 223)
+// with IEEE round-to-nearest intrinsics so nvcc cannot contract or
+// approximate any of it. min/max ignore NaN (Rust f32::min/max) and treat
+// -0.0 as +0.0 so a parallel reduction gives an order-independent result.
+//
+// Memory layout: x [H, T, D] row-major; codes are one byte per element
+// (flat index), INT4 packing into nibbles is a separate pass.
+#include <algorithm>
+#include <cmath>
+
+#include "kvf_internal.cuh"
+
+namespace kvf {
+namespace {
+
+constexpr int kSMs = 148;
+
+__device__ __forceinline__ float canon0(float v) { return v == 0.0f ? 0.0f : v; }
+
+__device__ __forceinline__ void mm_update(float v, float& mn, float& mx) {
+  if (!isnan(v)) {
+    v = canon0(v);
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+}
+
+__device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+}
+
+__device__ __forceinline__ float make_scale(float mn, float mx, float levels) {
+  const float range = __fsub_rn(mx, mn);
+  return (range < 1e-10f) ? 1.0f : __fdiv_rn(range, levels);
+}
+
+__device__ __forceinline__ uint32_t qcode(float v, float mn, float scale, float levels) {
+  const float y = __fdiv_rn(__fsub_rn(v, mn), scale);
+  float r = roundf(y);  // half away from zero, as Rust f32::round
+  if (isnan(r)) return 0u;  // NaN.clamp() stays NaN; `as u8` maps it to 0
+  r = fminf(fmaxf(r, 0.0f), levels);
+  return (uint32_t)r;
+}
+
+__device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
+  return __fadd_rn(__fmul_rn((float)q, scale), mn);
+}
+
+// order-preserving int image of a (non-NaN, canonical) float, for atomicMin/Max
+__device__ __forceinline__ int fkey(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float kfloat(int k) { return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF)); }
+
+__device__ __forceinline__ float ldf(const float* p, size_t i) { return __ldg(p + i); }
+__device__ __forceinline__ float ldf(const __half* p, size_t i) { return __half2float(__ldg(p + i)); }
+__device__ __forceinline__ float4 ld4(const float* p, size_t i) {
+  return __ldg(reinterpret_cast<const float4*>(p + i));
+}
+__device__ __forceinline__ float4 ld4(const __half* p, size_t i) {
+  uint2 u = __ldg(reinterpret_cast<const uint2*>(p + i));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+inline unsigned grid_warps(size_t rows, int warps_per_block) {
+  size_t b = (rows + warps_per_block - 1) / warps_per_block;
+  const size_t cap = (size_t)kSMs * 32;
+  if (b > cap) b = cap;
+  return (unsigned)(b ? b : 1);
+}
+
+// ---- per-token: one warp per (head, token) row (quantize.rs:102-130) -------
+template <typename TIn, int NV>
+__global__ void __launch_bounds__(256) k_quant_token_v4(const TIn* __restrict__ x, size_t rows,
+                                                        int D, float levels,
+                                                        uint8_t* __restrict__ codes,
+                                                        float* __restrict__ scales,
+                                                        float* __restrict__ mins) {
+  const int lane = threadIdx.x & 31;
+  const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const int nq = D >> 2;
+  for (size_t g = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < rows; g += nwarps) {
+    const size_t base = g * (size_t)D;
+    float4 v[NV];
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int q = lane + 32 * k;
+      if (q < nq) {
+        v[k] = ld4(x, base + 4 * (size_t)q);
+        mm_update(v[k].x, mn, mx);
+        mm_update(v[k].y, mn, mx);
+        mm_update(v[k].z, mn, mx);
+        mm_update(v[k].w, mn, mx);
+      }
+    }
+    warp_minmax(mn, mx);
+    const float scale = make_scale(mn, mx, levels);
+    if (lane == 0) {
+      scales[g] = scale;
+      mins[g] = mn;
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int q = lane + 32 * k;
+      if (q < nq) {
+        const uint32_t c = qcode(v[k].x, mn, scale, levels) | (qcode(v[k].y, mn, scale, levels) << 8) |
+                           (qcode(v[k].z, mn, scale, levels) << 16) |
+                           (qcode(v[k].w, mn, scale, levels) << 24);
+        *reinterpret_cast<uint32_t*>(codes + base + 4 * (size_t)q) = c;
+      }
+    }
+  }
+}
+
+template <typename TIn>
+__global__ void __launch_bounds__(256) k_quant_token_scalar(const TIn* __restrict__ x, size_t rows,
+                                                            int D, float levels,
+                                                            uint8_t* __restrict__ codes,
+                                                            float* __restrict__ scales,
+                                                            float* __restrict__ mins) {
+  const int lane = threadIdx.x & 31;
+  const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t g = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < rows; g += nwarps) {
+    const size_t base = g * (size_t)D;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int c = lane; c < D; c += 32) mm_update(ldf(x, base + c), mn, mx);
+    warp_minmax(mn, mx);
+    const float scale = make_scale(mn, mx, levels);
+    if (lane == 0) {
+      scales[g] = scale;
+      mins[g] = mn;
+    }
+    for (int c = lane; c < D; c += 32) codes[base + c] = (uint8_t)qcode(ldf(x, base + c), mn, scale, levels);
+  }
+}
+
+// ---- per-channel (quantize.rs:67-101): column min/max over all tokens -------
+__global__ void k_minmax_init(int* __restrict__ kmin, int* __restrict__ kmax, size_t np) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < np; i += (size_t)gridDim.x * blockDim.x) {
+    kmin[i] = fkey(INFINITY);
+    kmax[i] = fkey(-INFINITY);
+  }
+}
+
+// grid (token tiles, H); 8 warps stride over the tile's tokens, each lane owns
+// a channel of a 32-channel block; partials meet in shared memory, then one
+// atomicMin/atomicMax per (head, channel) and block.
+template <typename TIn>
+__global__ void __launch_bounds__(256) k_colminmax(const TIn* __restrict__ x, size_t T, int D,
+                                                   int tpb, int* __restrict__ kmin,
+                                                   int* __restrict__ kmax) {
+  extern __shared__ float sred[];  // [8][D] minima, then [8][D] maxima
+  const int h = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t t0 = (size_t)blockIdx.x * tpb;
+  const size_t t1 = (t0 + tpb < T) ? t0 + tpb : T;
+  const TIn* xh = x + (size_t)h * T * D;
+  for (int cb = 0; cb < D; cb += 32) {
+    const int c = cb + lane;
+    float mn = INFINITY, mx = -INFINITY;
+    if (c < D)
+      for (size_t t = t0 + w; t < t1; t += 8) mm_update(ldf(xh, t * D + c), mn, mx);
+    if (c < D) {
+      sred[w * D + c] = mn;
+      sred[8 * D + w * D + c] = mx;
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float mn = sred[c], mx = sred[8 * D + c];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+      mn = fminf(mn, sred[k * D + c]);
+      mx = fmaxf(mx, sred[8 * D + k * D + c]);
+    }
+    atomicMin(&kmin[(size_t)h * D + c], fkey(mn));
+    atomicMax(&kmax[(size_t)h * D + c], fkey(mx));
+  }
+}
+
+__global__ void k_params_from_keys(const int* __restrict__ kmin, const int* __restrict__ kmax,
+                                   size_t np, float levels, float* __restrict__ scales,
+                                   float* __restrict__ mins) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < np; i += (size_t)gridDim.x * blockDim.x) {
+    const float mn = kfloat(kmin[i]), mx = kfloat(kmax[i]);
+    scales[i] = make_scale(mn, mx, levels);
+    mins[i] = mn;
+  }
+}
+
+template <typename TIn, bool V4>
+__global__ void __launch_bounds__(256) k_quant_channel(const TIn* __restrict__ x, size_t rows, size_t T,
+                                                       int D, float levels,
+                                                       const float* __restrict__ scales,
+                                                       const float* __restrict__ mins,
+                                                       uint8_t* __restrict__ codes) {
+  const int lane = threadIdx.x & 31;
+  const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t g = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < rows; g += nwarps) {
+    const size_t base = g * (size_t)D;
+    const size_t pb = (g / T) * (size_t)D;
+    if (V4) {
+      for (int q = lane; q < (D >> 2); q += 32) {
+        const float4 v = ld4(x, base + 4 * (size_t)q);
+        const float4 s = __ldg(reinterpret_cast<const float4*>(scales + pb) + q);
+        const float4 m = __ldg(reinterpret_cast<const float4*>(mins + pb) + q);
+        const uint32_t c = qcode(v.x, m.x, s.x, levels) | (qcode(v.y, m.y, s.y, levels) << 8) |
+                           (qcode(v.z, m.z, s.z, levels) << 16) | (qcode(v.w, m.w, s.w, levels) << 24);
+        *reinterpret_cast<uint32_t*>(codes + base + 4 * (size_t)q) = c;
+      }
+    } else {
+      for (int c = lane; c < D; c += 32)
+        codes[base + c] = (uint8_t)qcode(ldf(x, base + c), __ldg(mins + pb + c), __ldg(scales + pb + c), levels);
+    }
+  }
+}
+
+// ---- INT4 nibble packing over the flat index (quantize.rs:136-150) ----------
+// 32 codes -> 16 packed bytes per thread step; optional 256-bin histogram of
+// the packed bytes (entropy.rs:24-31) in per-warp shared sub-histograms.
+__device__ __forceinline__ uint32_t pack4(uint32_t w) {
+  return (w & 0xFu) | (((w >> 8) & 0xFu) << 4) | (((w >> 16) & 0xFu) << 8) | (((w >> 24) & 0xFu) << 12);
+}
+
+__device__ __forceinline__ void hist_word(uint32_t* sh, uint32_t w) {
+  atomicAdd(&sh[w & 0xFF], 1u);
+  atomicAdd(&sh[(w >> 8) & 0xFF], 1u);
+  atomicAdd(&sh[(w >> 16) & 0xFF], 1u);
+  atomicAdd(&sh[w >> 24], 1u);
+}
+
+template <bool HIST>
+__global__ void __launch_bounds__(256) k_pack_int4(const uint8_t* __restrict__ codes, size_t n,
+                                                   uint8_t* __restrict__ packed,
+                                                   uint32_t* __restrict__ hist, bool vec) {
+  __shared__ uint32_t sh[8][256];
+  const int w = threadIdx.x >> 5;
+  if (HIST) {
+    for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) (&sh[0][0])[i] = 0;
+    __syncthreads();
+  }
+  const size_t n32 = vec ? n / 32 : 0;
+  for (size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x; j < n32; j += (size_t)gridDim.x * blockDim.x) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(codes + 32 * j));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(codes + 32 * j + 16));
+    uint4 o;
+    o.x = pack4(a.x) | (pack4(a.y) << 16);
+    o.y = pack4(a.z) | (pack4(a.w) << 16);
+    o.z = pack4(b.x) | (pack4(b.y) << 16);
+    o.w = pack4(b.z) | (pack4(b.w) << 16);
+    *reinterpret_cast<uint4*>(packed + 16 * j) = o;
+    if (HIST) {
+      hist_word(sh[w], o.x);
+      hist_word(sh[w], o.y);
+      hist_word(sh[w], o.z);
+      hist_word(sh[w], o.w);
+    }
+  }
+  {
+    const size_t np = (n + 1) / 2;
+    for (size_t p = 16 * n32 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; p < np;
+         p += (size_t)gridDim.x * blockDim.x) {
+      const uint32_t lo = codes[2 * p] & 0xFu;
+      const uint32_t hi = (2 * p + 1 < n) ? (codes[2 * p + 1] & 0xFu) : 0u;
+      const uint32_t byte = lo | (hi << 4);
+      packed[p] = (uint8_t)byte;
+      if (HIST) atomicAdd(&sh[w][byte], 1u);
+    }
+  }
+  if (HIST) {
+    __syncthreads();
+    for (int s = threadIdx.x; s < 256; s += blockDim.x) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += sh[k][s];
+      if (t) atomicAdd(&hist[s], t);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) k_histogram(const uint8_t* __restrict__ data, size_t n,
+                                                   uint32_t* __restrict__ hist, bool vec) {
+  __shared__ uint32_t sh[8][256];
+  const int w = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) (&sh[0][0])[i] = 0;
+  __syncthreads();
+  const size_t n16 = vec ? n / 16 : 0;
+  for (size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x; j < n16; j += (size_t)gridDim.x * blockDim.x) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(data + 16 * j));
+    hist_word(sh[w], a.x);
+    hist_word(sh[w], a.y);
+    hist_word(sh[w], a.z);
+    hist_word(sh[w], a.w);
+  }
+  for (size_t i = 16 * n16 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    atomicAdd(&sh[w][data[i]], 1u);
+  __syncthreads();
+  for (int s = threadIdx.x; s < 256; s += blockDim.x) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sh[k][s];
+    if (t) atomicAdd(&hist[s], t);
+  }
+}
+
+// ---- dequantize without projection (quantize.rs:165-231) --------------------
+template <bool INT4, bool V4>
+__global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ packed,
+                                                 const float* __restrict__ scales,
+                                                 const float* __restrict__ mins, int axis,
+                                                 size_t rows, size_t T, int D,
+                                                 float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t g = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < rows; g += nwarps) {
+    const size_t base = g * (size_t)D;
+    const bool per_channel = (axis == KVF_PER_CHANNEL);
+    const size_t pb = per_channel ? (g / T) * (size_t)D : g;
+    const float ts = per_channel ? 0.0f : __ldg(scales + g);
+    const float tm = per_channel ? 0.0f : __ldg(mins + g);
+    if (V4) {
+      for (int q = lane; q < (D >> 2); q += 32) {
+        const size_t i = base + 4 * (size_t)q;
+        uint32_t c0, c1, c2, c3;
+        if (INT4) {
+          const uint32_t b = *reinterpret_cast<const uint16_t*>(packed + (i >> 1));
+          c0 = b & 0xF; c1 = (b >> 4) & 0xF; c2 = (b >> 8) & 0xF; c3 = (b >> 12) & 0xF;
+        } else {
+          const uint32_t b = *reinterpret_cast<const uint32_t*>(packed + i);
+          c0 = b & 0xFF; c1 = (b >> 8) & 0xFF; c2 = (b >> 16) & 0xFF; c3 = b >> 24;
+        }
+        float4 s, m;
+        if (per_channel) {
+          s = __ldg(reinterpret_cast<const float4*>(scales + pb) + q);
+          m = __ldg(reinterpret_cast<const float4*>(mins + pb) + q);
+        } else {
+          s = make_float4(ts, ts, ts, ts);
+          m = make_float4(tm, tm, tm, tm);
+        }
+        const float4 o = make_float4(dq(c0, s.x, m.x), dq(c1, s.y, m.y), dq(c2, s.z, m.z), dq(c3, s.w, m.w));
+        __stcs(reinterpret_cast<float4*>(out + i), o);
+      }
+    } else {
+      for (int c = lane; c < D; c += 32) {
+        const size_t i = base + c;
+        const uint32_t b = packed[INT4 ? (i >> 1) : i];
+        const uint32_t q = INT4 ? ((i & 1) ? (b >> 4) & 0xF : b & 0xF) : b;
+        const float s = per_channel ? __ldg(scales + pb + c) : ts;
+        const float m = per_channel ? __ldg(mins + pb + c) : tm;
+        out[i] = dq(q, s, m);
+      }
+    }
+  }
+}
+
+template <typename TIn>
+cudaError_t quantize_typed(const TIn* x, size_t H, size_t T, size_t D, int dt, int axis,
+                           uint8_t* codes, float* scales, float* mins, int* keys,
+                           cudaStream_t st) {
+  const float levels = quant_levels(dt);
+  const size_t rows = H * T;
+  const int Di = (int)D;
+  const bool xal = aligned(x, sizeof(TIn) * 4) && aligned(codes, 4);
+  if (axis == KVF_PER_TOKEN) {
+    if (rows == 0) return cudaSuccess;
+    const unsigned grid = grid_warps(rows, 8);
+    if (!xal)
+      k_quant_token_scalar<TIn><<<grid, 256, 0, st>>>(x, rows, Di, levels, codes, scales, mins);
+    else if (D % 4 == 0 && D > 0 && D <= 128)
+      k_quant_token_v4<TIn, 1><<<grid, 256, 0, st>>>(x, rows, Di, levels, codes, scales, mins);
+    else if (D % 4 == 0 && D > 0 && D <= 256)
+      k_quant_token_v4<TIn, 2><<<grid, 256, 0, st>>>(x, rows, Di, levels, codes, scales, mins);
+    else if (D % 4 == 0 && D > 0 && D <= 512)
+      k_quant_token_v4<TIn, 4><<<grid, 256, 0, st>>>(x, rows, Di, levels, codes, scales, mins);
+    else
+      k_quant_token_scalar<TIn><<<grid, 256, 0, st>>>(x, rows, Di, levels, codes, scales, mins);
+    note_launches(1);
+    return cudaGetLastError();
+  }
+  // per-channel
+  const size_t np = H * D;
+  if (np == 0) return cudaSuccess;
+  int* kmin = keys;
+  int* kmax = keys + np;
+  const unsigned ig = (unsigned)std::min<size_t>((np + 255) / 256, 4096);
+  k_minmax_init<<<ig, 256, 0, st>>>(kmin, kmax, np);
+  if (T > 0) {
+    const int tpb = 256;
+    const dim3 grid((unsigned)((T + tpb - 1) / tpb), (unsigned)H);
+    const size_t smem = 2 * 8 * D * sizeof(float);
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(k_colminmax<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    k_colminmax<TIn><<<grid, 256, smem, st>>>(x, T, Di, tpb, kmin, kmax);
+  }
+  k_params_from_keys<<<ig, 256, 0, st>>>(kmin, kmax, np, levels, scales, mins);
+  note_launches(2 + (T > 0 ? 1 : 0) + (rows > 0 ? 1 : 0));
+  if (rows > 0) {
+    const unsigned grid = grid_warps(rows, 8);
+    if (D % 4 == 0 && xal && aligned(scales, 16) && aligned(mins, 16))
+      k_quant_channel<TIn, true><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, codes);
+    else
+      k_quant_channel<TIn, false><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, codes);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                                  int data_type, int axis, uint8_t* codes, float* scales,
+                                  float* mins, int* keys, cudaStream_t st) {
+  if (in_dtype == KVF_IN_F16)
+    return quantize_typed(static_cast<const __half*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
+  return quantize_typed(static_cast<const float*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
+}
+
+cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,
+                             cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  size_t work = n / 32;
+  unsigned grid = (unsigned)std::min<size_t>((work + 255) / 256, (size_t)kSMs * 8);
+  if (grid == 0) grid = 1;
+  const bool vec = aligned(codes, 16) && aligned(packed, 16);
+  if (!vec) grid = (unsigned)std::min<size_t>((n / 2 + 255) / 256 + 1, (size_t)kSMs * 8);
+  if (hist)
+    k_pack_int4<true><<<grid, 256, 0, st>>>(codes, n, packed, hist, vec);
+  else
+    k_pack_int4<false><<<grid, 256, 0, st>>>(codes, n, packed, nullptr, vec);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_histogram(const uint8_t* data, size_t n, uint32_t* hist, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  size_t work = n / 16;
+  unsigned grid = (unsigned)std::min<size_t>((work + 255) / 256, (size_t)kSMs * 8);
+  if (grid == 0) grid = 1;
+  const bool vec = aligned(data, 16);
+  if (!vec) grid = (unsigned)std::min<size_t>((n + 255) / 256, (size_t)kSMs * 8);
+  k_histogram<<<grid, 256, 0, st>>>(data, n, hist, vec);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, const float* mins,
+                              int data_type, int axis, size_t H, size_t T, size_t D, float* out,
+                              cudaStream_t st) {
+  const size_t rows = H * T;
+  if (rows == 0 || D == 0) return cudaSuccess;
+  const unsigned grid = grid_warps(rows, 8);
+  const bool v4 = (D % 4 == 0) && aligned(out, 16) && aligned(packed, data_type == KVF_INT4 ? 2 : 4) &&
+                  (axis != KVF_PER_CHANNEL || (aligned(scales, 16) && aligned(mins, 16)));
+  const int Di = (int)D;
+  if (data_type == KVF_INT4) {
+    if (v4) k_dequant<true, true><<<grid, 256, 0, st>>>(packed, scales, mins, axis, rows, T, Di, out);
+    else k_dequant<true, false><<<grid, 256, 0, st>>>(packed, scales, mins, axis, rows, T, Di, out);
+  } else {
+    if (v4) k_dequant<false, true><<<grid, 256, 0, st>>>(packed, scales, mins, axis, rows, T, Di, out);
+    else k_dequant<false, false><<<grid, 256, 0, st>>>(packed, scales, mins, axis, rows, T, Di, out);
+  }
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace kvf

@@ -1,0 +1,353 @@
+// Chunked, 32-lane interleaved rANS (sm_100a).
+//
+// The reference codes one serial stream with constriction's stack ANS
+// (crates/kvforge-cpu/src/entropy.rs:42-123). That stream cannot be split, so
+// this library defines its own container, mirrored bit for bit by the CPU
+// oracle so that each side decodes the other's output:
+//
+//   state x in [2^16, 2^32), 16-bit renormalisation words, 15-bit model.
+//   header (32 B): u32 magic "KVR1", u32 prob_bits = 15, u32 lanes = 32,
+//                  u32 chunk_symbols, u64 original_len, u32 num_chunks,
+//                  u32 header_bytes = 32 + 4 * (num_chunks + 1)
+//   u32 chunk_offset[num_chunks + 1]: byte offset of each chunk payload from
+//                  the container start; the last entry is the total length
+//   chunk payload: u32 nwords; u32 final_state[32]; u16 words[nwords];
+//                  one zero u16 when nwords is odd (4-byte alignment)
+//
+// One warp codes one chunk; symbol i of a chunk belongs to lane i % 32, step
+// i / 32. The encoder runs steps backwards; in each step the active lanes
+// renormalise (emitters ordered by descending lane, found with a ballot) and
+// then encode. The decoder runs steps forwards and serves consuming lanes in
+// ascending order, so it reads the word array front to back.
+//
+// Model: counts -> q[s] = max(1, floor(count * 2^15 / N)) for seen symbols,
+// 0 for unseen; the deficit goes to the most frequent symbol, an excess is
+// removed from the largest entries. Integer only, identical on both sides.
+//
+// Every read of the decoder is bounds-checked against the container; a
+// malformed container sets a status bit instead of faulting, and there are no
+// waits, so no kernel here can hang.
+#include <algorithm>
+
+#include "kvf_internal.cuh"
+
+namespace kvf {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+
+__global__ void __launch_bounds__(256) k_rans_normalize(const uint32_t* __restrict__ freq,
+                                                        RansTables* __restrict__ tab,
+                                                        unsigned* __restrict__ status) {
+  __shared__ unsigned long long sN;
+  __shared__ uint32_t f[256], q[256], cum[256];
+  __shared__ int bad;
+  const int s = threadIdx.x;
+  f[s] = freq[s];
+  if (s == 0) { sN = 0ull; bad = 0; }
+  __syncthreads();
+  atomicAdd(&sN, (unsigned long long)f[s]);
+  __syncthreads();
+  const unsigned long long N = sN;
+  if (N == 0ull) {
+    if (s == 0) atomicOr(status, kDevErrEntropy);
+    return;
+  }
+  if (f[s] == 0) {
+    q[s] = 0;
+  } else {
+    const unsigned long long v = ((unsigned long long)f[s] * kRansM) / N;
+    q[s] = (uint32_t)(v < 1ull ? 1ull : v);
+  }
+  __syncthreads();
+  if (s == 0) {
+    unsigned long long S = 0;
+    int argmax = 0;
+    for (int k = 0; k < 256; ++k) {
+      S += q[k];
+      if (f[k] > f[argmax]) argmax = k;
+    }
+    if (S < kRansM) {
+      q[argmax] += (uint32_t)(kRansM - S);
+    } else {
+      while (S > kRansM) {
+        int best = -1;
+        for (int k = 0; k < 256; ++k)
+          if (q[k] > 1 && (best < 0 || q[k] > q[best])) best = k;
+        if (best < 0) { bad = 1; break; }
+        unsigned long long d = S - kRansM;
+        if (d > q[best] - 1) d = q[best] - 1;
+        q[best] -= (uint32_t)d;
+        S -= d;
+      }
+    }
+    uint32_t c = 0;
+    for (int k = 0; k < 256; ++k) { cum[k] = c; c += q[k]; }
+  }
+  __syncthreads();
+  if (bad) {
+    if (s == 0) atomicOr(status, kDevErrEntropy);
+    return;
+  }
+  tab->q[s] = q[s];
+  tab->cum[s] = cum[s];
+  tab->rcp[s] = q[s] ? 0xFFFFFFFFu / q[s] : 0u;
+  // slot -> symbol: the last symbol whose cum <= slot (unseen symbols share
+  // the cum of the next seen one and therefore never win)
+  for (uint32_t k = s; k < kRansM; k += blockDim.x) {
+    int lo = 0, hi = 255;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cum[mid] <= k) lo = mid; else hi = mid - 1;
+    }
+    tab->slot2sym[k] = (uint8_t)lo;
+  }
+}
+
+// one warp per chunk; the chunk's symbols are staged in shared memory first
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8_t* __restrict__ data,
+                                                                   uint64_t n, uint32_t chunk,
+                                                                   const RansTables* __restrict__ tab,
+                                                                   uint8_t* __restrict__ slots,
+                                                                   uint64_t nchunks) {
+  extern __shared__ __align__(16) uint8_t sbuf[];  // [warps][chunk]
+  __shared__ uint32_t q[256], cum[256], rcp[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    q[i] = tab->q[i];
+    cum[i] = tab->cum[i];
+    rcp[i] = tab->rcp[i];
+  }
+  __syncthreads();
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w;
+  if (c >= nchunks) return;
+  const uint64_t start = c * chunk;
+  const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
+  uint8_t* buf = sbuf + (size_t)w * chunk;
+  // stage symbols (start is a multiple of chunk, itself a multiple of 32)
+  const uint32_t n16 = (reinterpret_cast<uintptr_t>(data + start) & 15u) == 0 ? nsym / 16 : 0;
+  for (uint32_t j = lane; j < n16; j += 32)
+    reinterpret_cast<uint4*>(buf)[j] = __ldg(reinterpret_cast<const uint4*>(data + start) + j);
+  for (uint32_t j = 16 * n16 + lane; j < nsym; j += 32) buf[j] = data[start + j];
+  __syncwarp();
+
+  uint8_t* slot = slots + c * rans_slot_bytes(chunk);
+  uint16_t* words = reinterpret_cast<uint16_t*>(slot + kRansChunkHeader);
+  const uint32_t capw = chunk + 2;
+  uint32_t pos = capw;  // words are written backwards, ending at capw
+  uint32_t x = kRansL;
+  const uint32_t steps = (nsym + 31) / 32;
+  for (uint32_t st = steps; st-- > 0;) {
+    const uint32_t i = st * 32 + lane;
+    const bool active = i < nsym;
+    const uint32_t s = active ? buf[i] : 0u;
+    const uint32_t f = q[s];
+    const bool need = active && ((uint64_t)x >= ((uint64_t)f << 17));
+    const unsigned mask = __ballot_sync(0xffffffffu, need);
+    if (need) {
+      const unsigned above = mask & ~((2u << lane) - 1u);  // emitting lanes above this one
+      words[pos - 1 - __popc(above)] = (uint16_t)(x & 0xFFFFu);
+      x >>= 16;
+    }
+    pos -= __popc(mask);
+    if (active) {
+      uint32_t qq = __umulhi(x, rcp[s]);
+      uint32_t r = x - qq * f;
+      if (r >= f) { ++qq; r -= f; }
+      x = (qq << kRansProbBits) + r + cum[s];
+    }
+  }
+  uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
+  hdr[1 + lane] = x;
+  if (lane == 0) hdr[0] = capw - pos;
+}
+
+// header + offsets: one block scans the chunk sizes
+__global__ void __launch_bounds__(1024) k_rans_offsets(const uint8_t* __restrict__ slots, uint64_t n,
+                                                       uint32_t chunk, uint64_t nchunks,
+                                                       uint8_t* __restrict__ out,
+                                                       uint64_t* __restrict__ out_len) {
+  __shared__ uint64_t part[1024];
+  const uint64_t per = (nchunks + blockDim.x - 1) / blockDim.x;
+  const uint64_t c0 = threadIdx.x * per;
+  const uint64_t c1 = (c0 + per < nchunks) ? c0 + per : nchunks;
+  const size_t sb = rans_slot_bytes(chunk);
+  uint64_t local = 0;
+  for (uint64_t c = c0; c < c1; ++c) {
+    const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
+    local += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
+  }
+  part[threadIdx.x] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t run = 0;
+    for (int k = 0; k < (int)blockDim.x; ++k) {
+      const uint64_t v = part[k];
+      part[k] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  const uint64_t hdr = kRansHeader + 4ull * (nchunks + 1);
+  uint32_t* off = reinterpret_cast<uint32_t*>(out + kRansHeader);
+  uint64_t run = hdr + part[threadIdx.x];
+  for (uint64_t c = c0; c < c1; ++c) {
+    off[c] = (uint32_t)run;
+    const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
+    run += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
+  }
+  if (threadIdx.x == blockDim.x - 1) {
+    // last thread's run ends at the total
+    off[nchunks] = (uint32_t)run;
+    *out_len = run;
+    uint32_t* h = reinterpret_cast<uint32_t*>(out);
+    h[0] = kRansMagic;
+    h[1] = kRansProbBits;
+    h[2] = kRansLanes;
+    h[3] = chunk;
+    h[4] = (uint32_t)(n & 0xFFFFFFFFull);
+    h[5] = (uint32_t)(n >> 32);
+    h[6] = (uint32_t)nchunks;
+    h[7] = (uint32_t)hdr;
+  }
+}
+
+// one block per chunk: copy nwords, states and words into place
+__global__ void __launch_bounds__(128) k_rans_compact(const uint8_t* __restrict__ slots, uint32_t chunk,
+                                                      uint8_t* __restrict__ out) {
+  const uint64_t c = blockIdx.x;
+  const uint8_t* slot = slots + c * rans_slot_bytes(chunk);
+  const uint32_t* off = reinterpret_cast<const uint32_t*>(out + kRansHeader);
+  uint8_t* dst = out + off[c];
+  const uint32_t* shdr = reinterpret_cast<const uint32_t*>(slot);
+  const uint32_t nw = shdr[0];
+  uint32_t* dhdr = reinterpret_cast<uint32_t*>(dst);
+  for (int i = threadIdx.x; i < 1 + (int)kRansLanes; i += blockDim.x) dhdr[i] = shdr[i];
+  const uint16_t* sw = reinterpret_cast<const uint16_t*>(slot + kRansChunkHeader) + (chunk + 2 - nw);
+  uint16_t* dw = reinterpret_cast<uint16_t*>(dst + kRansChunkHeader);
+  for (uint32_t i = threadIdx.x; i < nw; i += blockDim.x) dw[i] = sw[i];
+  if ((nw & 1u) && threadIdx.x == 0) dw[nw] = 0;
+}
+
+__device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// one warp per chunk; slot table and model in shared memory
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_decode(const uint8_t* __restrict__ comp,
+                                                                   uint64_t comp_len_host,
+                                                                   const uint64_t* __restrict__ comp_len_dev,
+                                                                   const RansTables* __restrict__ tab,
+                                                                   uint64_t n, uint8_t* __restrict__ out,
+                                                                   unsigned* __restrict__ status) {
+  __shared__ __align__(16) uint8_t sym[kRansM];
+  __shared__ uint32_t qc[256];  // q | cum << 16
+  for (int i = threadIdx.x; i < (int)(kRansM / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(sym)[i] = reinterpret_cast<const uint4*>(tab->slot2sym)[i];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) qc[i] = tab->q[i] | (tab->cum[i] << 16);
+  __syncthreads();
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t comp_len = comp_len_dev ? *comp_len_dev : comp_len_host;
+  // header checks (every warp reads the same 32 bytes)
+  if (comp_len < kRansHeader) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
+  const uint32_t chunk = rd32(comp + 12);
+  const uint64_t nn = (uint64_t)rd32(comp + 16) | ((uint64_t)rd32(comp + 20) << 32);
+  const uint64_t nchunks = rd32(comp + 24);
+  const uint64_t hdr = kRansHeader + 4ull * (nchunks + 1);
+  const bool hdr_ok = rd32(comp) == kRansMagic && rd32(comp + 4) == kRansProbBits &&
+                      rd32(comp + 8) == kRansLanes && chunk != 0 && (chunk % 32) == 0 && nn == n &&
+                      nchunks == (n + chunk - 1) / chunk && rd32(comp + 28) == hdr && hdr <= comp_len &&
+                      rd32(comp + kRansHeader + 4 * nchunks) == comp_len;
+  if (!hdr_ok) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
+  const uint64_t nwarps = (uint64_t)gridDim.x * kWarpsPerBlock;
+  for (uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w; c < nchunks; c += nwarps) {
+    const uint64_t off = rd32(comp + kRansHeader + 4 * c);
+    const uint64_t end = rd32(comp + kRansHeader + 4 * (c + 1));
+    if (off < hdr || end > comp_len || end < off + kRansChunkHeader || (off & 3u)) {
+      if (lane == 0) atomicOr(status, kDevErrCorrupt);
+      continue;
+    }
+    const uint32_t nw = rd32(comp + off);
+    if (off + kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u) != end) {
+      if (lane == 0) atomicOr(status, kDevErrCorrupt);
+      continue;
+    }
+    uint32_t x = rd32(comp + off + 4 + 4 * lane);
+    bool bad = x < kRansL;
+    const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
+    const uint64_t start = c * chunk;
+    const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
+    const uint32_t steps = (nsym + 31) / 32;
+    uint32_t p = 0;
+    for (uint32_t st = 0; st < steps; ++st) {
+      const uint32_t i = st * 32 + lane;
+      const bool active = i < nsym;
+      if (active) {
+        const uint32_t slot = x & (kRansM - 1);
+        const uint32_t s = sym[slot];
+        const uint32_t e = qc[s];
+        x = (e & 0xFFFFu) * (x >> kRansProbBits) + slot - (e >> 16);
+        out[start + i] = (uint8_t)s;
+      }
+      const bool need = active && x < kRansL;
+      const unsigned mask = __ballot_sync(0xffffffffu, need);
+      if (need) {
+        const uint32_t idx = p + __popc(mask & ((1u << lane) - 1u));
+        if (idx < nw) x = (x << 16) | words[idx];
+        else { bad = true; x = kRansL; }
+      }
+      p += __popc(mask);
+    }
+    bad = bad || x != kRansL || p != nw;
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, kDevErrCorrupt);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_rans_normalize(const uint32_t* freq, RansTables* tab, unsigned* status,
+                                  cudaStream_t st) {
+  k_rans_normalize<<<1, 256, 0, st>>>(freq, tab, status);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const RansTables* tab,
+                               uint8_t* slots, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  const size_t nc = rans_num_chunks(n, chunk);
+  const size_t smem = (size_t)kWarpsPerBlock * chunk;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_rans_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const unsigned grid = (unsigned)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
+  k_rans_encode<<<grid, kWarpsPerBlock * 32, smem, st>>>(data, n, chunk, tab, slots, nc);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk, uint8_t* out,
+                                 uint64_t* out_len, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  const size_t nc = rans_num_chunks(n, chunk);
+  k_rans_offsets<<<1, 1024, 0, st>>>(slots, n, chunk, nc, out, out_len);
+  k_rans_compact<<<(unsigned)nc, 128, 0, st>>>(slots, chunk, out);
+  note_launches(2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
+                               const RansTables* tab, size_t n, uint8_t* out, unsigned* status,
+                               cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  // the grid is sized for the encoder's default chunk size; warps loop over
+  // chunks, so a container with any chunk size named in its header decodes
+  const size_t nc = rans_num_chunks(n, kRansChunk);
+  const unsigned grid = (unsigned)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
+  k_rans_decode<<<grid, kWarpsPerBlock * 32, 0, st>>>(comp, comp_len, comp_len_dev, tab, n, out, status);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace kvf
