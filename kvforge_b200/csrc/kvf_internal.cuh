@@ -21,6 +21,10 @@ constexpr uint32_t kRansMagic = 0x3152564Bu;  // "KVR1"
 constexpr size_t kRansHeader = 32;
 constexpr size_t kRansChunkHeader = 4 + 4 * kRansLanes;  // nwords + 32 lane states
 
+// dynamic shared memory above this opts in to the larger per-block limit;
+// the margin below 48 KB leaves room for a kernel's static shared memory
+constexpr size_t kSmemOptIn = 40 * 1024;
+
 // device status bits (ctx->d_status); mapped to kvf_status by the host
 constexpr unsigned kDevErrCorrupt = 1u;
 constexpr unsigned kDevErrEntropy = 2u;

@@ -189,12 +189,12 @@ cudaError_t project_rg(const TIn* x, size_t H, size_t T, size_t D, const float* 
   cudaError_t e;
   if (cpart) {
     auto kern = k_project<TIn, RG, VEC, true>;
-    if (smem > 48 * 1024 && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+    if (smem > kSmemOptIn && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
     kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, P, cpart);
   } else {
     auto kern = k_project<TIn, RG, VEC, false>;
-    if (smem > 48 * 1024 && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+    if (smem > kSmemOptIn && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
     kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, P, nullptr);
   }
@@ -383,7 +383,7 @@ cudaError_t dequant_reconstruct_mode(const uint8_t* codes, const float* raw, con
   const size_t smem = ((size_t)R * D + (size_t)R * kRecRows) * sizeof(float);
   if (D % 4 == 0 && smem <= 200 * 1024 && aligned(out, 16)) {
     auto kern = k_dequant_reconstruct<MODE, EXACT>;
-    if (smem > 48 * 1024) {
+    if (smem > kSmemOptIn) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }
@@ -515,7 +515,7 @@ cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t til
                                   size_t D, float* scores, cudaStream_t st) {
   if (H == 0) return cudaSuccess;
   const size_t smem = H * sizeof(double);
-  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  if (smem > kSmemOptIn) return cudaErrorInvalidValue;
   k_calib_finalize<<<1, 256, smem, st>>>(calib_part, (int)H, (int)tiles, (double)(T * D), scores);
   note_launches(1);
   return cudaGetLastError();

@@ -400,7 +400,7 @@ cudaError_t quantize_typed(const TIn* x, size_t H, size_t T, size_t D, int dt, i
     const int tpb = 256;
     const dim3 grid((unsigned)((T + tpb - 1) / tpb), (unsigned)H);
     const size_t smem = 2 * 8 * D * sizeof(float);
-    if (smem > 48 * 1024) {
+    if (smem > kSmemOptIn) {
       cudaError_t e = cudaFuncSetAttribute(k_colminmax<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }

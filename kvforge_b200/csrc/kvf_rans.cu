@@ -317,7 +317,7 @@ cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, co
   if (n == 0) return cudaSuccess;
   const size_t nc = rans_num_chunks(n, chunk);
   const size_t smem = (size_t)kWarpsPerBlock * chunk;
-  if (smem > 48 * 1024) {
+  if (smem > kSmemOptIn) {
     cudaError_t e = cudaFuncSetAttribute(k_rans_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }

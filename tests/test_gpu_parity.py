@@ -28,7 +28,13 @@ def host(t):
 
 
 def bits(a):
-    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+    """f32 bit patterns with every NaN mapped to one value: IEEE 754 leaves NaN
+    payloads unspecified (x86 yields 0xFFC00000 for 0 * inf, the GPU 0x7FFFFFFF),
+    so NaN positions must match but their payloads are not compared."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = a.view(np.uint32).copy()
+    b[np.isnan(a)] = 0x7FC00000
+    return b
 
 
 def rel(a, b):
