@@ -127,6 +127,27 @@ kvf_status kvf_pipeline_config_from_preset(int32_t preset, kvf_pipeline_config* 
 kvf_status kvf_calibrate(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_t H, size_t T,
                          size_t D, size_t min_tokens, float* scores, void* stream);
 
+/* kvf_calibrate without any device allocation. It has no counterpart in the
+ * reference. It is for callers that cannot allocate device memory: a serving
+ * engine that reserves all device memory up front and forbids later
+ * allocations, or a latency-critical path that cannot afford cudaMalloc's
+ * implicit device synchronisation. Results match kvf_calibrate.
+ * - Scratch: a file-scope device array of 65536 (head, tile) slots (1 MiB),
+ *   loaded with the library and held by every GPU that loads it until the
+ *   process exits. A tile is 65536 elements of one head, so the call needs
+ *   H * ceil(T * D / 65536) <= 65536 and returns KVF_ERR_INVALID_CONFIG
+ *   beyond that, before touching the device.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress, once per device per process); make that first call
+ *   before any stream capture begins.
+ * - All calls share the one array and each overwrites it: calls that overlap
+ *   on the GPU (two streams, or two threads) race and give wrong scores.
+ *   Every slot a call reads is written by that call first, so nothing has to
+ *   be cleared between calls.
+ * It calls no cudaMalloc, cudaFree or allocating library routine. */
+kvf_status kvf_calibrate_noalloc(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_t H, size_t T,
+                                 size_t D, size_t min_tokens, float* scores, void* stream);
+
 /* Quantizer::quantize (codec.rs:105-111; quantize.rs:47-163).
  * packed: INT8 -> H*T*D bytes, INT4 -> ceil(H*T*D/2) bytes (low nibble first,
  * pairs over the flat index). scales/mins: H*D (per-channel) or H*T (per-token). */

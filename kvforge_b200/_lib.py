@@ -47,7 +47,7 @@ EXPORTS = [
     "kvf_compressed_shape", "kvf_compressed_size_bytes", "kvf_original_size_bytes", "kvf_compression_ratio",
     "kvf_compressed_tensor_info", "kvf_compressed_tensor_views", "kvf_compressed_calibration",
     "kvf_compressed_serialize", "kvf_compressed_deserialize", "kvf_compressed_free",
-    "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read",
+    "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read", "kvf_calibrate_noalloc",
 ]
 
 NUM_STAGES = 8
@@ -129,6 +129,7 @@ def _declare(L):
         "kvf_stage_name": (C.c_char_p, [i32]),
         "kvf_profile_enable": (st, [p, C.c_int]),
         "kvf_profile_read": (st, [p, p, p, p]),
+        "kvf_calibrate_noalloc": (st, [p, p, i32, sz, sz, sz, sz, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -789,6 +789,31 @@ kvf_status kvf_calibrate(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_
   return KVF_OK;
 }
 
+// Same computation as kvf_calibrate; the per-block partials go to a
+// file-scope device array instead of the stream-ordered pool (contract in
+// include/kvforge.h). No cudaMalloc/cudaFree on this path.
+kvf_status kvf_calibrate_noalloc(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_t H, size_t T, size_t D,
+                                 size_t min_tokens, float* scores, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (T < min_tokens)
+    return fail(KVF_ERR_INVALID_CONFIG, "Need at least " + std::to_string(min_tokens) +
+                                            " tokens for calibration, got " + std::to_string(T));
+  const size_t tiles = calib_partial_tiles(T, D);
+  if (H * tiles > kCalibStaticSlots)
+    return fail(KVF_ERR_INVALID_CONFIG, "num_heads * ceil(seq_len * head_dim / 65536) = " +
+                                            std::to_string(H * tiles) + " exceeds the " +
+                                            std::to_string(kCalibStaticSlots) + " static scratch slots");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(KVF_ERR_CUDA, "cudaSetDevice failed");
+  double* cpart = nullptr;
+  KVF_CUDA(calib_static_scratch(ctx->device, &cpart));
+  KVF_CUDA(launch_calib_partials(keys, in_dtype, H, T, D, cpart, S(stream)));
+  KVF_CUDA(launch_calib_finalize(cpart, H, tiles, T, D, scores, S(stream)));
+  return KVF_OK;
+}
+
 kvf_status kvf_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
                         int32_t data_type, int32_t axis, uint8_t* packed, float* scales, float* mins,
                         void* stream) {

@@ -80,6 +80,10 @@ cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size
 size_t calib_partial_tiles(size_t T, size_t D);
 cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                                   double* calib_part, cudaStream_t st);
+// no-allocation calibration: partials for up to kCalibStaticSlots (head, tile)
+// pairs in a file-scope device array; its address for `device` (current)
+constexpr size_t kCalibStaticSlots = 65536;
+cudaError_t calib_static_scratch(int device, double** out);
 cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t tiles, size_t T,
                                   size_t D, float* scores, cudaStream_t st);
 // packed codes (or raw f32 when data_type == KVF_F32) + params + basis -> f32 [H,T,D]

@@ -17,6 +17,7 @@
 // in fp64 rounding order).
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "kvf_internal.cuh"
 
@@ -481,6 +482,33 @@ __global__ void k_gram_reduce(const float* __restrict__ partial, int tiles, int 
 }
 
 }  // namespace
+
+// ---- calibration scratch that needs no allocation ------------------------------
+// For callers that cannot allocate device memory (see kvf_calibrate_noalloc in
+// include/kvforge.h): the per-block partial sums live in this file-scope array,
+// loaded with the library and held by every GPU that loads it until the process
+// exits. Host code cannot use the name as a device address; it asks the runtime
+// for the address once per device (calib_static_scratch below).
+static __device__ __align__(256) double g_calib_static[2 * kCalibStaticSlots];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+double* g_static_ptr[kMaxDevices] = {};
+}  // namespace
+
+cudaError_t calib_static_scratch(int device, double** out) {
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_calib_static);  // device `device` is current
+    if (e != cudaSuccess) return e;
+    g_static_ptr[device] = static_cast<double*>(p);
+  }
+  *out = g_static_ptr[device];
+  return cudaSuccess;
+}
 
 size_t project_num_tiles(size_t T) { return (T + kProjTile - 1) / kProjTile; }
 
