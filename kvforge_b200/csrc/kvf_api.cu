@@ -118,6 +118,7 @@ struct TensorC {
   float* d_scales = nullptr;
   float* d_mins = nullptr;
   uint32_t* d_freq = nullptr;
+  RansTables* d_tab = nullptr;       // model built from d_freq (kept for decoding)
   std::shared_ptr<BasisData> basis;  // projection state, when projected
 };
 
@@ -127,6 +128,10 @@ struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
   unsigned* d_status = nullptr;
+  // a layer's value tensor runs on `side` while its key tensor runs on the
+  // caller's stream; fork/join events order the two
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
   // stage timing (kvf_profile_enable / kvf_profile_read)
   struct Rec {
     int stage;
@@ -185,12 +190,18 @@ struct kvf_compressed {
   float* d_scores = nullptr;
   std::vector<void*> owned;
 
+  // owned buffers are allocated in the order of the stream that first uses
+  // them (a layer's value tensor is built on the context's side stream)
   template <class T>
-  T* alloc(size_t count) {
+  T* alloc(size_t count, cudaStream_t on) {
     void* p = nullptr;
-    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), stream) != cudaSuccess) return nullptr;
+    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), on) != cudaSuccess) return nullptr;
     owned.push_back(p);
     return static_cast<T*>(p);
+  }
+  template <class T>
+  T* alloc(size_t count) {
+    return alloc<T>(count, stream);
   }
 };
 
@@ -242,10 +253,9 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
   return KVF_OK;
 }
 
-// histogram -> model -> chunk coding -> container in `out` (length -> d_len)
+// model (into `tab`) -> chunk coding -> container in `out` (length -> d_len)
 kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, size_t plen,
-                            const uint32_t* freq, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
-  RansTables* tab = sc.get<RansTables>(1);
+                            const uint32_t* freq, RansTables* tab, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
   const size_t nc = rans_num_chunks(plen, kRansChunk);
   uint8_t* slots = sc.get<uint8_t>(nc * rans_slot_bytes(kRansChunk));
   if (!tab || !slots) return fail(KVF_ERR_CUDA, "scratch allocation failed");
@@ -256,6 +266,11 @@ kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, si
 }
 
 // compress_tensor (crates/kvforge-cpu/src/pipeline.rs:38-72)
+//
+// With projection the quantizer reads the projection kernel's epilogue:
+// keys (per channel) get P plus per-(head, r) min/max from the projection
+// kernel, then one quantize + pack + histogram kernel; values (per token) are
+// quantized row by row inside the projection kernel, then packed.
 kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, int in_dtype, size_t H,
                            size_t T, size_t D, int dt, int axis, const std::shared_ptr<BasisData>& basis,
                            bool entropy, bool calib, float* d_scores, TensorC* out, cudaStream_t st) {
@@ -268,69 +283,107 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
   out->D = D;
   out->entropy = entropy;
   out->basis = basis;
-  const void* qin = x;
-  int qdt = in_dtype;
-  size_t qcols = D;
-  double* cpart = nullptr;
-  size_t ctiles = 0;
-  const bool do_calib = calib && d_scores && T >= 64;  // CalibrationConfig::default().min_tokens
   if (basis) {
     if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
     if (basis->H != H || basis->D != D)
       return fail(KVF_ERR_SHAPE_MISMATCH, "basis shape does not match the tensor");
-    qcols = basis->R;
-    float* P = sc.get<float>(H * T * qcols);
-    if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-    if (do_calib) {
-      ctiles = project_num_tiles(T);
-      cpart = sc.get<double>(2 * H * ctiles);
-      if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-    }
-    {
-      StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4) + (double)H * T * qcols * 4, st);
-      KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, P, cpart, st));
-    }
-    qin = P;
-    qdt = KVF_IN_F32;
-  } else if (do_calib) {
-    ctiles = calib_partial_tiles(T, D);
-    cpart = sc.get<double>(2 * H * ctiles);
-    if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-    StageTimer tm(ctx, KVF_STAGE_CALIBRATE, (double)H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4), st);
-    KVF_CUDA(launch_calib_partials(x, in_dtype, H, T, D, cpart, st));
   }
-  if (cpart) KVF_CUDA(launch_calib_finalize(cpart, H, ctiles, T, D, d_scores, st));
-
-  out->qcols = qcols;
+  const size_t qcols = basis ? basis->R : D;
   const size_t n = H * T * qcols;
   const size_t plen = packed_len(n, dt);
   const size_t np = num_params(H, T, qcols, axis);
+  const size_t in_bytes = H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4);
+  out->qcols = qcols;
   out->packed_len = plen;
   out->num_params = np;
-  out->d_scales = owner->alloc<float>(np);
-  out->d_mins = owner->alloc<float>(np);
+  out->d_scales = owner->alloc<float>(np, st);
+  out->d_mins = owner->alloc<float>(np, st);
   if (!out->d_scales || !out->d_mins) return fail(KVF_ERR_CUDA, "allocation failed");
   const bool do_ent = entropy && plen > 0;
   out->has_freq = do_ent;
-  uint8_t* packed = do_ent ? sc.get<uint8_t>(plen) : owner->alloc<uint8_t>(plen);
+  uint8_t* packed = do_ent ? sc.get<uint8_t>(plen) : owner->alloc<uint8_t>(plen, st);
   if (!packed) return fail(KVF_ERR_CUDA, "allocation failed");
+  uint32_t* hist = nullptr;
   if (do_ent) {
-    out->d_freq = owner->alloc<uint32_t>(256);
+    out->d_freq = owner->alloc<uint32_t>(256, st);
     if (!out->d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
     KVF_CUDA(cudaMemsetAsync(out->d_freq, 0, 256 * sizeof(uint32_t), st));
+    hist = out->d_freq;
   }
-  {
-    StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n * (qdt == KVF_IN_F16 ? 2 : 4) + (double)plen + 8.0 * np, st);
-    KVF_TRY(quantize_into(sc, qin, qdt, H, T, qcols, dt, axis, packed, out->d_scales, out->d_mins,
-                          do_ent ? out->d_freq : nullptr, st));
+
+  const bool do_calib = calib && d_scores && T >= 64;  // CalibrationConfig::default().min_tokens
+  double* cpart = nullptr;
+  size_t ctiles = 0;
+  if (do_calib) {
+    ctiles = basis ? project_num_tiles(T) : calib_partial_tiles(T, D);
+    cpart = sc.get<double>(2 * H * ctiles);
+    if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   }
+
+  if (basis) {
+    ProjectOut po;
+    po.cpart = cpart;
+    po.levels = quant_levels(dt);
+    if (axis == KVF_PER_CHANNEL) {
+      float* P = sc.get<float>(n);
+      int* keys = sc.get<int>(2 * H * qcols);
+      if (!P || !keys) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+      KVF_CUDA(launch_minmax_init(keys, keys + H * qcols, H * qcols, st));
+      po.mode = 1;
+      po.P = P;
+      po.kmin = keys;
+      po.kmax = keys + H * qcols;
+      {
+        StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + 4.0 * n, st);
+        KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
+      }
+      StageTimer tm(ctx, KVF_STAGE_QUANTIZE, 4.0 * n + (double)plen + 8.0 * np, st);
+      KVF_CUDA(launch_quantpack_channel(P, H, T, qcols, po.kmin, po.kmax, dt, out->d_scales, out->d_mins, packed,
+                                        hist, st));
+    } else if (qcols <= 32) {
+      uint8_t* codes = (dt == KVF_INT8) ? packed : sc.get<uint8_t>(n);
+      if (!codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+      po.mode = 2;
+      po.codes = codes;
+      po.scales = out->d_scales;
+      po.mins = out->d_mins;
+      {
+        StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + (double)n + 8.0 * np, st);
+        KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
+      }
+      StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n + (double)plen, st);
+      if (dt == KVF_INT4) KVF_CUDA(launch_pack_int4(codes, n, packed, hist, st));
+      else if (hist) KVF_CUDA(launch_histogram(packed, n, hist, st));
+    } else {
+      float* P = sc.get<float>(n);
+      if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+      po.mode = 0;
+      po.P = P;
+      {
+        StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + 4.0 * n, st);
+        KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
+      }
+      StageTimer tm(ctx, KVF_STAGE_QUANTIZE, 4.0 * n + (double)plen + 8.0 * np, st);
+      KVF_TRY(quantize_into(sc, P, KVF_IN_F32, H, T, qcols, dt, axis, packed, out->d_scales, out->d_mins, hist, st));
+    }
+  } else {
+    if (do_calib) {
+      StageTimer tm(ctx, KVF_STAGE_CALIBRATE, (double)in_bytes, st);
+      KVF_CUDA(launch_calib_partials(x, in_dtype, H, T, D, cpart, st));
+    }
+    StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)in_bytes + (double)plen + 8.0 * np, st);
+    KVF_TRY(quantize_into(sc, x, in_dtype, H, T, D, dt, axis, packed, out->d_scales, out->d_mins, hist, st));
+  }
+  if (cpart) KVF_CUDA(launch_calib_finalize(cpart, H, ctiles, T, D, d_scores, st));
+
   if (do_ent) {
     out->data_cap = rans_max_len(plen, kRansChunk);
-    out->d_data = owner->alloc<uint8_t>(out->data_cap);
-    out->d_len = owner->alloc<uint64_t>(1);
-    if (!out->d_data || !out->d_len) return fail(KVF_ERR_CUDA, "allocation failed");
+    out->d_data = owner->alloc<uint8_t>(out->data_cap, st);
+    out->d_len = owner->alloc<uint64_t>(1, st);
+    out->d_tab = owner->alloc<RansTables>(1, st);
+    if (!out->d_data || !out->d_len || !out->d_tab) return fail(KVF_ERR_CUDA, "allocation failed");
     StageTimer tm(ctx, KVF_STAGE_ENTROPY_ENCODE, (double)plen, st);
-    KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_data, out->d_len, st));
+    KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_tab, out->d_data, out->d_len, st));
     out->len_known = false;
   } else {
     out->d_data = packed;
@@ -346,11 +399,11 @@ kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStr
   Scratch sc(st);
   const uint8_t* codes = t.d_data;
   if (t.has_freq) {
-    RansTables* tab = sc.get<RansTables>(1);
+    RansTables* tab = t.d_tab ? t.d_tab : sc.get<RansTables>(1);
     uint8_t* dec = sc.get<uint8_t>(t.packed_len);
     if (!tab || !dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
     StageTimer tm(ctx, KVF_STAGE_ENTROPY_DECODE, 2.0 * t.packed_len, st);
-    KVF_CUDA(launch_rans_normalize(t.d_freq, tab, ctx->d_status, st));
+    if (!t.d_tab) KVF_CUDA(launch_rans_normalize(t.d_freq, tab, ctx->d_status, st));
     KVF_CUDA(launch_rans_decode(t.d_data, t.data_len, t.len_known ? nullptr : t.d_len, tab, t.packed_len,
                                 dec, ctx->d_status, st));
     codes = dec;
@@ -623,6 +676,9 @@ kvf_status deser_tensor(kvf_compressed* c, TensorC& t, Reader& r, cudaStream_t s
     t.d_freq = c->alloc<uint32_t>(256);
     if (!t.d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
     KVF_TRY(up(t.d_freq, 256 * 4));
+    t.d_tab = c->alloc<RansTables>(1);
+    if (!t.d_tab) return fail(KVF_ERR_CUDA, "allocation failed");
+    KVF_CUDA(launch_rans_normalize(t.d_freq, t.d_tab, c->ctx->d_status, st));
   }
   t.data_cap = t.data_len;
   t.d_data = c->alloc<uint8_t>(t.data_len);
@@ -672,6 +728,9 @@ kvf_status kvf_init(int device, kvf_ctx** out) {
   }
   cudaError_t e = cudaMalloc(&ctx->d_status, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     delete ctx;
     return fail(KVF_ERR_CUDA, std::string("context allocation: ") + cudaGetErrorString(e));
@@ -688,6 +747,12 @@ kvf_status kvf_destroy(kvf_ctx* ctx) {
     cudaEventDestroy(r.b);
   }
   for (auto e : ctx->spare) cudaEventDestroy(e);
+  if (ctx->side) {
+    cudaStreamSynchronize(ctx->side);
+    cudaStreamDestroy(ctx->side);
+  }
+  if (ctx->fork) cudaEventDestroy(ctx->fork);
+  if (ctx->join) cudaEventDestroy(ctx->join);
   cudaFree(ctx->d_status);
   delete ctx;
   return KVF_OK;
@@ -853,7 +918,9 @@ kvf_status kvf_project(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t 
   if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
-  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, projected, nullptr, S(stream)));
+  ProjectOut po;
+  po.P = projected;
+  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, S(stream)));
   return KVF_OK;
 }
 
@@ -880,10 +947,39 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
   Scratch sc(S(stream));
-  float* P = sc.get<float>(H * T * R);
+  cudaStream_t st = S(stream);
+  const size_t n = H * T * R;
+  ProjectOut po;
+  po.levels = quant_levels(data_type);
+  if (axis == KVF_PER_CHANNEL) {
+    float* P = sc.get<float>(n);
+    int* keys = sc.get<int>(2 * H * R);
+    if (!P || !keys) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    KVF_CUDA(launch_minmax_init(keys, keys + H * R, H * R, st));
+    po.mode = 1;
+    po.P = P;
+    po.kmin = keys;
+    po.kmax = keys + H * R;
+    KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
+    KVF_CUDA(launch_quantpack_channel(P, H, T, R, po.kmin, po.kmax, data_type, scales, mins, packed, nullptr, st));
+    return KVF_OK;
+  }
+  if (R <= 32) {
+    uint8_t* codes = (data_type == KVF_INT8) ? packed : sc.get<uint8_t>(n);
+    if (!codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    po.mode = 2;
+    po.codes = codes;
+    po.scales = scales;
+    po.mins = mins;
+    KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
+    if (data_type == KVF_INT4) KVF_CUDA(launch_pack_int4(codes, n, packed, nullptr, st));
+    return KVF_OK;
+  }
+  float* P = sc.get<float>(n);
   if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, P, nullptr, S(stream)));
-  return quantize_into(sc, P, KVF_IN_F32, H, T, R, data_type, axis, packed, scales, mins, nullptr, S(stream));
+  po.P = P;
+  KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
+  return quantize_into(sc, P, KVF_IN_F32, H, T, R, data_type, axis, packed, scales, mins, nullptr, st);
 }
 
 size_t kvf_rans_max_encoded_len(size_t n) { return rans_max_len(n, kRansChunk); }
@@ -904,8 +1000,10 @@ kvf_status kvf_rans_encode(kvf_ctx* ctx, const uint8_t* data, size_t n, uint8_t*
   Scratch sc(st);
   uint64_t* d_len = sc.get<uint64_t>(1);
   if (!d_len) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  RansTables* tab = sc.get<RansTables>(1);
+  if (!tab) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   KVF_CUDA(launch_histogram(data, n, freq, st));
-  KVF_TRY(rans_encode_into(ctx, sc, data, n, freq, out, d_len, st));
+  KVF_TRY(rans_encode_into(ctx, sc, data, n, freq, tab, out, d_len, st));
   uint64_t len = 0;
   KVF_CUDA(cudaMemcpyAsync(&len, d_len, sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
   KVF_TRY(read_status(ctx, st));
@@ -1041,12 +1139,18 @@ kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values
     c->d_scores = c->alloc<float>(H);
     if (!c->d_scores) return fail(KVF_ERR_CUDA, "allocation failed");
   }
+  // keys on the caller's stream, values on the side stream, joined before return
+  KVF_CUDA(cudaEventRecord(ctx->fork, st));
+  KVF_CUDA(cudaStreamWaitEvent(ctx->side, ctx->fork, 0));
   kvf_status s = compress_tensor(ctx, c.get(), keys, in_dtype, H, T, D, cfg->key_data_type, KVF_PER_CHANNEL, kb,
                                  cfg->enable_entropy_coding != 0, cfg->enable_calibration != 0, c->d_scores,
                                  &c->key, st);
   if (s == KVF_OK)
     s = compress_tensor(ctx, c.get(), values, in_dtype, H, T, D, cfg->value_data_type, KVF_PER_TOKEN, vb,
-                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, st);
+                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, ctx->side);
+  cudaError_t je = cudaEventRecord(ctx->join, ctx->side);
+  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, ctx->join, 0);
+  if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   if (s != KVF_OK) {
     std::string msg = g_err;
     kvf_compressed_free(c.release());
@@ -1062,9 +1166,15 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
   KVF_TRY(check_ctx(ctx));
   if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
   DeviceGuard g(ctx->device);
-  KVF_TRY(decompress_tensor(ctx, c->key, keys_out, S(stream)));
-  KVF_TRY(decompress_tensor(ctx, c->value, values_out, S(stream)));
-  return KVF_OK;
+  cudaStream_t st = S(stream);
+  KVF_CUDA(cudaEventRecord(ctx->fork, st));
+  KVF_CUDA(cudaStreamWaitEvent(ctx->side, ctx->fork, 0));
+  kvf_status s = decompress_tensor(ctx, c->key, keys_out, st);
+  if (s == KVF_OK) s = decompress_tensor(ctx, c->value, values_out, ctx->side);
+  cudaError_t je = cudaEventRecord(ctx->join, ctx->side);
+  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, ctx->join, 0);
+  if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
+  return s;
 }
 
 kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host, int32_t in_dtype,

@@ -60,6 +60,53 @@ inline size_t num_params(size_t H, size_t T, size_t D, int axis) {
 // process-wide count of kernels launched by this library (kvf_launch_count)
 void note_launches(unsigned n);
 
+
+#ifdef __CUDACC__
+// ---- KIVI arithmetic shared by every kernel that quantizes (quantize.rs) ----
+__device__ __forceinline__ float canon0(float v) { return v == 0.0f ? 0.0f : v; }
+
+__device__ __forceinline__ void mm_update(float v, float& mn, float& mx) {
+  if (!isnan(v)) {
+    v = canon0(v);
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+}
+
+__device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+}
+
+__device__ __forceinline__ float make_scale(float mn, float mx, float levels) {
+  const float range = __fsub_rn(mx, mn);
+  return (range < 1e-10f) ? 1.0f : __fdiv_rn(range, levels);
+}
+
+__device__ __forceinline__ uint32_t qcode(float v, float mn, float scale, float levels) {
+  const float y = __fdiv_rn(__fsub_rn(v, mn), scale);
+  float r = roundf(y);  // half away from zero, as Rust f32::round
+  if (isnan(r)) return 0u;  // NaN.clamp() stays NaN; `as u8` maps it to 0
+  r = fminf(fmaxf(r, 0.0f), levels);
+  return (uint32_t)r;
+}
+
+__device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
+  return __fadd_rn(__fmul_rn((float)q, scale), mn);
+}
+
+// order-preserving int image of a (non-NaN, canonical) float, for atomicMin/Max
+__device__ __forceinline__ int fkey(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float kfloat(int k) { return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF)); }
+
+#endif  // __CUDACC__
+
 // ---- kernel launchers (return the launch error, if any) -------------------
 // quantization (kvf_quant.cu)
 cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t T, size_t D,
@@ -67,6 +114,13 @@ cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t 
                                   float* mins, int* minmax_keys, cudaStream_t st);
 cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,
                              cudaStream_t st);
+// kmin/kmax <- keys of +inf / -inf
+cudaError_t launch_minmax_init(int* kmin, int* kmax, size_t np, cudaStream_t st);
+// codes (+ INT4 packing, + optional histogram) of projected keys P [H,T,R]
+// whose per-(head, r) min/max keys are final; also writes scales/mins [H,R]
+cudaError_t launch_quantpack_channel(const float* P, size_t H, size_t T, size_t R, const int* kmin,
+                                     const int* kmax, int data_type, float* scales, float* mins,
+                                     uint8_t* out, uint32_t* hist, cudaStream_t st);
 cudaError_t launch_histogram(const uint8_t* data, size_t n, uint32_t* hist, cudaStream_t st);
 cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, const float* mins,
                               int data_type, int axis, size_t H, size_t T, size_t D, float* out,
@@ -74,9 +128,24 @@ cudaError_t launch_dequantize(const uint8_t* packed, const float* scales, const 
 
 // projection / calibration / gram (kvf_project.cu)
 size_t project_num_tiles(size_t T);
+// outputs of the projection kernel; mode 0: P; mode 1: P + per-(head, r)
+// min/max keys (kmin/kmax, initialised to +inf/-inf keys); mode 2: per-token
+// codes + scales/mins (R <= 32). cpart (optional): key calibration partials,
+// project_num_tiles(T) per head.
+struct ProjectOut {
+  int mode = 0;
+  float* P = nullptr;
+  double* cpart = nullptr;
+  int* kmin = nullptr;
+  int* kmax = nullptr;
+  uint8_t* codes = nullptr;
+  float* scales = nullptr;
+  float* mins = nullptr;
+  float levels = 15.0f;
+};
 cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
-                           const float* basis_vt, const uint64_t* ranks, size_t R, float* P,
-                           double* calib_part, cudaStream_t st);
+                           const float* basis_vt, const uint64_t* ranks, size_t R, const ProjectOut& o,
+                           cudaStream_t st);
 size_t calib_partial_tiles(size_t T, size_t D);
 cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                                   double* calib_part, cudaStream_t st);

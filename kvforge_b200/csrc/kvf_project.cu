@@ -25,8 +25,6 @@ namespace kvf {
 namespace {
 
 constexpr int kProjThreads = 128;
-constexpr int kProjTok = 2;                      // tokens per thread
-constexpr int kProjTile = kProjThreads * kProjTok;  // tokens per block
 constexpr int kRecRows = 128;                    // token rows per reconstruct block
 constexpr int kCalibTile = 1 << 16;              // elements per calibration block
 constexpr int kGramTile = 512;                   // tokens per Gram block
@@ -83,16 +81,48 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 }
 
 // ---- projection -------------------------------------------------------------
-// grid (ceil(T / 256), H), 128 threads; each thread owns two token rows, reads
-// them from global memory with 16-byte loads and keeps RG coefficients per row
-// in registers. The basis of head h sits transposed in shared memory, vT[c][r],
-// so the RG basis values of one c are a broadcast float4 load.
-template <typename TIn, int RG, bool VEC, bool CALIB>
+// grid (ceil(T / 128), H), 128 threads, one token row per thread. The row is
+// read in 256-byte segments whose sixteen 16-byte loads are issued together, so
+// a whole segment is in flight at once (the kernel is bound by HBM latency
+// otherwise). The basis of head h sits transposed in shared memory, vT[c][r],
+// so the RG basis values of one c are a broadcast float4 load. Epilogues:
+//   MODE 0: write P [H,T,R];
+//   MODE 1: write P and fold each column into per-(head, r) min/max with
+//           order-preserving integer atomics (keys: per-channel parameters
+//           need every token before any code can be formed);
+//   MODE 2: quantize the row per token at once -- codes [H,T,R] bytes plus a
+//           scale/min per token; P never reaches memory (values; R <= RG).
+template <typename TIn>
+struct Seg;
+template <>
+struct Seg<__half> {
+  static constexpr int PV = 8;  // elements per 16-byte vector
+  __device__ static void unpack(const uint4& u, float* o) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      o[2 * k] = f.x;
+      o[2 * k + 1] = f.y;
+    }
+  }
+};
+template <>
+struct Seg<float> {
+  static constexpr int PV = 4;
+  __device__ static void unpack(const uint4& u, float* o) {
+    o[0] = __uint_as_float(u.x);
+    o[1] = __uint_as_float(u.y);
+    o[2] = __uint_as_float(u.z);
+    o[3] = __uint_as_float(u.w);
+  }
+};
+
+template <typename TIn, int RG, bool VEC, bool CALIB, int MODE>
 __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict__ x, int T, int D,
                                                         const float* __restrict__ bvt,
                                                         const uint64_t* __restrict__ ranks, int R,
-                                                        int Rpad, float* __restrict__ P,
-                                                        double* __restrict__ cpart) {
+                                                        int Rpad, ProjectOut o) {
   extern __shared__ __align__(16) float vT[];  // [D][Rpad]
   const int h = blockIdx.y;
   const uint64_t rk = ranks[h];
@@ -104,70 +134,105 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
   }
   __syncthreads();
 
-  const size_t t_first = (size_t)blockIdx.x * kProjTile + threadIdx.x;
-  const TIn* xr[kProjTok];
-  bool ok[kProjTok];
-#pragma unroll
-  for (int k = 0; k < kProjTok; ++k) {
-    const size_t t = t_first + (size_t)k * kProjThreads;
-    ok[k] = t < (size_t)T;
-    xr[k] = x + ((size_t)h * T + (ok[k] ? t : 0)) * D;
-  }
+  const int t = blockIdx.x * kProjThreads + threadIdx.x;
+  const bool ok = t < T;
+  const size_t g = (size_t)h * T + (ok ? t : 0);
+  const TIn* xr = x + g * D;
   double s1 = 0.0, s2 = 0.0;
-  constexpr int CV = VEC ? Vec<TIn>::N : 1;
   for (int rg = 0; rg < R; rg += RG) {
-    float acc[kProjTok][RG];
+    float acc[RG];
 #pragma unroll
-    for (int k = 0; k < kProjTok; ++k)
+    for (int r = 0; r < RG; ++r) acc[r] = 0.0f;
+    if (VEC) {
+      constexpr int PV = Seg<TIn>::PV;
+      for (int c0 = 0; c0 < D; c0 += 16 * PV) {
+        const int nv = min(16, (D - c0) / PV);
+        uint4 raw[16];
 #pragma unroll
-      for (int r = 0; r < RG; ++r) acc[k][r] = 0.0f;
-    for (int c0 = 0; c0 < D; c0 += CV) {
-      float xv[kProjTok][CV];
+        for (int j = 0; j < 16; ++j)
+          raw[j] = (ok && j < nv) ? __ldg(reinterpret_cast<const uint4*>(xr + c0) + j) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int k = 0; k < kProjTok; ++k) {
-        if (ok[k]) {
-          if (VEC) Vec<TIn>::load(xr[k] + c0, xv[k]);
-          else xv[k][0] = ldf(xr[k], c0);
-        } else {
+        for (int j = 0; j < 16; ++j) {
+          if (j < nv) {
+            float xv[PV];
+            Seg<TIn>::unpack(raw[j], xv);
+            if (CALIB && rg == 0) {
 #pragma unroll
-          for (int j = 0; j < CV; ++j) xv[k][j] = 0.0f;
+              for (int k = 0; k < PV; ++k) {
+                const double v = (double)xv[k];
+                s1 += v;
+                s2 += v * v;
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < PV; ++k) {
+              const float4* vr = reinterpret_cast<const float4*>(vT + (size_t)(c0 + j * PV + k) * Rpad + rg);
+#pragma unroll
+              for (int q = 0; q < RG / 4; ++q) {
+                const float4 v = vr[q];
+                acc[4 * q + 0] = __fmaf_rn(xv[k], v.x, acc[4 * q + 0]);
+                acc[4 * q + 1] = __fmaf_rn(xv[k], v.y, acc[4 * q + 1]);
+                acc[4 * q + 2] = __fmaf_rn(xv[k], v.z, acc[4 * q + 2]);
+                acc[4 * q + 3] = __fmaf_rn(xv[k], v.w, acc[4 * q + 3]);
+              }
+            }
+          }
         }
       }
-      if (CALIB && rg == 0) {
-#pragma unroll
-        for (int k = 0; k < kProjTok; ++k)
-#pragma unroll
-          for (int j = 0; j < CV; ++j) {
-            const double v = (double)xv[k][j];
-            s1 += v;
-            s2 += v * v;
-          }
-      }
-#pragma unroll
-      for (int j = 0; j < CV; ++j) {
-        const float4* vr = reinterpret_cast<const float4*>(vT + (size_t)(c0 + j) * Rpad + rg);
+    } else {
+      for (int c = 0; c < D; ++c) {
+        const float xv = ok ? ldf(xr, c) : 0.0f;
+        if (CALIB && rg == 0) {
+          const double v = (double)xv;
+          s1 += v;
+          s2 += v * v;
+        }
+        const float4* vr = reinterpret_cast<const float4*>(vT + (size_t)c * Rpad + rg);
 #pragma unroll
         for (int q = 0; q < RG / 4; ++q) {
           const float4 v = vr[q];
-#pragma unroll
-          for (int k = 0; k < kProjTok; ++k) {
-            acc[k][4 * q + 0] = __fmaf_rn(xv[k][j], v.x, acc[k][4 * q + 0]);
-            acc[k][4 * q + 1] = __fmaf_rn(xv[k][j], v.y, acc[k][4 * q + 1]);
-            acc[k][4 * q + 2] = __fmaf_rn(xv[k][j], v.z, acc[k][4 * q + 2]);
-            acc[k][4 * q + 3] = __fmaf_rn(xv[k][j], v.w, acc[k][4 * q + 3]);
-          }
+          acc[4 * q + 0] = __fmaf_rn(xv, v.x, acc[4 * q + 0]);
+          acc[4 * q + 1] = __fmaf_rn(xv, v.y, acc[4 * q + 1]);
+          acc[4 * q + 2] = __fmaf_rn(xv, v.z, acc[4 * q + 2]);
+          acc[4 * q + 3] = __fmaf_rn(xv, v.w, acc[4 * q + 3]);
         }
       }
     }
+    // coefficients r >= rank_h are +0.0 (projection.rs:96)
 #pragma unroll
-    for (int k = 0; k < kProjTok; ++k) {
-      if (!ok[k]) continue;
-      const size_t t = t_first + (size_t)k * kProjThreads;
-      float* pr = P + ((size_t)h * T + t) * R;
+    for (int r = 0; r < RG; ++r)
+      if (rg + r >= rank) acc[r] = 0.0f;
+    if (MODE == 0 || MODE == 1) {
+      float* pr = o.P + g * R;
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
         const int rr = rg + r;
-        if (rr < R) pr[rr] = (rr < rank) ? acc[k][r] : 0.0f;
+        if (rr < R) {  // warp-uniform
+          if (ok) pr[rr] = acc[r];
+          if (MODE == 1) {
+            float mn = INFINITY, mx = -INFINITY;
+            if (ok) mm_update(acc[r], mn, mx);
+            warp_minmax(mn, mx);
+            if ((threadIdx.x & 31) == 0) {
+              atomicMin(&o.kmin[(size_t)h * R + rr], fkey(mn));
+              atomicMax(&o.kmax[(size_t)h * R + rr], fkey(mx));
+            }
+          }
+        }
+      }
+    } else {  // MODE 2: per-token quantization of the whole row (R <= RG)
+      float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < RG; ++r)
+        if (r < R) mm_update(acc[r], mn, mx);
+      const float scale = make_scale(mn, mx, o.levels);
+      if (ok) {
+        o.scales[g] = scale;
+        o.mins[g] = mn;
+        uint8_t* cr = o.codes + g * R;
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+          if (r < R) cr[r] = (uint8_t)qcode(acc[r], mn, scale, o.levels);
       }
     }
   }
@@ -175,48 +240,61 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
     block_sum2(s1, s2);
     if (threadIdx.x == 0) {
       const size_t slot = (size_t)h * gridDim.x + blockIdx.x;
-      cpart[2 * slot] = s1;
-      cpart[2 * slot + 1] = s2;
+      o.cpart[2 * slot] = s1;
+      o.cpart[2 * slot + 1] = s2;
     }
   }
 }
 
-template <typename TIn, int RG, bool VEC>
-cudaError_t project_rg(const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
-                       const uint64_t* ranks, size_t R, float* P, double* cpart, cudaStream_t st) {
+template <typename TIn, int RG, bool VEC, bool CALIB, int MODE>
+cudaError_t project_launch(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
+                           size_t R, const ProjectOut& o, cudaStream_t st) {
   const int Rpad = (int)(((R + RG - 1) / RG) * RG);
   const size_t smem = (size_t)D * Rpad * sizeof(float);
-  const dim3 grid((unsigned)((T + kProjTile - 1) / kProjTile), (unsigned)H);
-  cudaError_t e;
-  if (cpart) {
-    auto kern = k_project<TIn, RG, VEC, true>;
-    if (smem > kSmemOptIn && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
-      return e;
-    kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, P, cpart);
-  } else {
-    auto kern = k_project<TIn, RG, VEC, false>;
-    if (smem > kSmemOptIn && (e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
-      return e;
-    kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, P, nullptr);
+  const dim3 grid((unsigned)((T + kProjThreads - 1) / kProjThreads), (unsigned)H);
+  auto kern = k_project<TIn, RG, VEC, CALIB, MODE>;
+  if (smem > kSmemOptIn) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
   }
+  kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, o);
   note_launches(1);
   return cudaGetLastError();
 }
 
+template <typename TIn, int RG, bool VEC>
+cudaError_t project_mode(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
+                         size_t R, const ProjectOut& o, cudaStream_t st) {
+  const bool calib = o.cpart != nullptr;
+#define KVF_PL(C, M) return project_launch<TIn, RG, VEC, C, M>(x, H, T, D, bvt, ranks, R, o, st)
+  if (o.mode == 1) {
+    if (calib) KVF_PL(true, 1);
+    KVF_PL(false, 1);
+  }
+  if (o.mode == 2) {
+    if (calib) KVF_PL(true, 2);
+    KVF_PL(false, 2);
+  }
+  if (calib) KVF_PL(true, 0);
+  KVF_PL(false, 0);
+#undef KVF_PL
+}
+
 template <typename TIn, bool VEC>
-cudaError_t project_vec(const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
-                        const uint64_t* ranks, size_t R, float* P, double* cpart, cudaStream_t st) {
-  if (R <= 4) return project_rg<TIn, 4, VEC>(x, H, T, D, bvt, ranks, R, P, cpart, st);
-  if (R <= 8) return project_rg<TIn, 8, VEC>(x, H, T, D, bvt, ranks, R, P, cpart, st);
-  if (R <= 16) return project_rg<TIn, 16, VEC>(x, H, T, D, bvt, ranks, R, P, cpart, st);
-  return project_rg<TIn, 32, VEC>(x, H, T, D, bvt, ranks, R, P, cpart, st);
+cudaError_t project_vec(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
+                        size_t R, const ProjectOut& o, cudaStream_t st) {
+  if (R <= 4) return project_mode<TIn, 4, VEC>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 8) return project_mode<TIn, 8, VEC>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 16) return project_mode<TIn, 16, VEC>(x, H, T, D, bvt, ranks, R, o, st);
+  if (o.mode == 2 && R > 32) return cudaErrorInvalidValue;
+  return project_mode<TIn, 32, VEC>(x, H, T, D, bvt, ranks, R, o, st);
 }
 
 template <typename TIn>
-cudaError_t project_typed(const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
-                          const uint64_t* ranks, size_t R, float* P, double* cpart, cudaStream_t st) {
-  if (D % Vec<TIn>::N == 0 && aligned(x, 16)) return project_vec<TIn, true>(x, H, T, D, bvt, ranks, R, P, cpart, st);
-  return project_vec<TIn, false>(x, H, T, D, bvt, ranks, R, P, cpart, st);
+cudaError_t project_typed(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
+                          size_t R, const ProjectOut& o, cudaStream_t st) {
+  if (D % Seg<TIn>::PV == 0 && aligned(x, 16)) return project_vec<TIn, true>(x, H, T, D, bvt, ranks, R, o, st);
+  return project_vec<TIn, false>(x, H, T, D, bvt, ranks, R, o, st);
 }
 
 // ---- calibration partials without projection ----------------------------------
@@ -510,15 +588,15 @@ cudaError_t calib_static_scratch(int device, double** out) {
   return cudaSuccess;
 }
 
-size_t project_num_tiles(size_t T) { return (T + kProjTile - 1) / kProjTile; }
+size_t project_num_tiles(size_t T) { return (T + kProjThreads - 1) / kProjThreads; }
 
 cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
-                           const float* basis_vt, const uint64_t* ranks, size_t R, float* P,
-                           double* calib_part, cudaStream_t st) {
+                           const float* basis_vt, const uint64_t* ranks, size_t R, const ProjectOut& o,
+                           cudaStream_t st) {
   if (H == 0 || T == 0) return cudaSuccess;
   if (in_dtype == KVF_IN_F16)
-    return project_typed(static_cast<const __half*>(x), H, T, D, basis_vt, ranks, R, P, calib_part, st);
-  return project_typed(static_cast<const float*>(x), H, T, D, basis_vt, ranks, R, P, calib_part, st);
+    return project_typed(static_cast<const __half*>(x), H, T, D, basis_vt, ranks, R, o, st);
+  return project_typed(static_cast<const float*>(x), H, T, D, basis_vt, ranks, R, o, st);
 }
 
 size_t calib_partial_tiles(size_t T, size_t D) {

@@ -20,48 +20,6 @@ namespace {
 
 constexpr int kSMs = 148;
 
-__device__ __forceinline__ float canon0(float v) { return v == 0.0f ? 0.0f : v; }
-
-__device__ __forceinline__ void mm_update(float v, float& mn, float& mx) {
-  if (!isnan(v)) {
-    v = canon0(v);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
-  }
-}
-
-__device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  }
-}
-
-__device__ __forceinline__ float make_scale(float mn, float mx, float levels) {
-  const float range = __fsub_rn(mx, mn);
-  return (range < 1e-10f) ? 1.0f : __fdiv_rn(range, levels);
-}
-
-__device__ __forceinline__ uint32_t qcode(float v, float mn, float scale, float levels) {
-  const float y = __fdiv_rn(__fsub_rn(v, mn), scale);
-  float r = roundf(y);  // half away from zero, as Rust f32::round
-  if (isnan(r)) return 0u;  // NaN.clamp() stays NaN; `as u8` maps it to 0
-  r = fminf(fmaxf(r, 0.0f), levels);
-  return (uint32_t)r;
-}
-
-__device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
-  return __fadd_rn(__fmul_rn((float)q, scale), mn);
-}
-
-// order-preserving int image of a (non-NaN, canonical) float, for atomicMin/Max
-__device__ __forceinline__ int fkey(float f) {
-  const int i = __float_as_int(f);
-  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
-}
-__device__ __forceinline__ float kfloat(int k) { return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF)); }
-
 __device__ __forceinline__ float ldf(const float* p, size_t i) { return __ldg(p + i); }
 __device__ __forceinline__ float ldf(const __half* p, size_t i) { return __half2float(__ldg(p + i)); }
 __device__ __forceinline__ float4 ld4(const float* p, size_t i) {
@@ -365,6 +323,57 @@ __global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ pac
   }
 }
 
+// ---- per-channel codes from projected coefficients ---------------------------
+// P [H,T,R] f32 with its per-(head, r) min/max already folded into kmin/kmax
+// by the projection kernel: one thread per output byte forms the code(s),
+// packs INT4 nibbles over the flat index and counts the packed byte. The
+// first np threads also write the (scale, min) parameters.
+template <bool INT4, bool HIST>
+__global__ void __launch_bounds__(256) k_quantpack_channel(const float* __restrict__ P, uint64_t n, uint64_t T,
+                                                           uint64_t R, const int* __restrict__ kmin,
+                                                           const int* __restrict__ kmax, float levels,
+                                                           float* __restrict__ scales, float* __restrict__ mins,
+                                                           uint64_t np, uint8_t* __restrict__ out,
+                                                           uint32_t* __restrict__ hist) {
+  __shared__ uint32_t sh[8][256];
+  const int w = threadIdx.x >> 5;
+  if (HIST) {
+    for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) (&sh[0][0])[i] = 0;
+    __syncthreads();
+  }
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = tid; i < np; i += stride) {
+    const float mn = kfloat(kmin[i]), mx = kfloat(kmax[i]);
+    scales[i] = make_scale(mn, mx, levels);
+    mins[i] = mn;
+  }
+  auto code = [&](uint64_t i) -> uint32_t {
+    const uint64_t g = i / R;
+    const uint64_t c = i - g * R;
+    const uint64_t p = (g / T) * R + c;
+    const float mn = kfloat(__ldg(kmin + p)), mx = kfloat(__ldg(kmax + p));
+    return qcode(__ldg(P + i), mn, make_scale(mn, mx, levels), levels);
+  };
+  const uint64_t nb = INT4 ? (n + 1) / 2 : n;
+  for (uint64_t b = tid; b < nb; b += stride) {
+    uint32_t byte;
+    if (INT4) byte = code(2 * b) | ((2 * b + 1 < n) ? (code(2 * b + 1) << 4) : 0u);
+    else byte = code(b);
+    out[b] = (uint8_t)byte;
+    if (HIST) atomicAdd(&sh[w][byte], 1u);
+  }
+  if (HIST) {
+    __syncthreads();
+    for (int s = threadIdx.x; s < 256; s += blockDim.x) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += sh[k][s];
+      if (t) atomicAdd(&hist[s], t);
+    }
+  }
+}
+
 template <typename TIn>
 cudaError_t quantize_typed(const TIn* x, size_t H, size_t T, size_t D, int dt, int axis,
                            uint8_t* codes, float* scales, float* mins, int* keys,
@@ -426,6 +435,34 @@ cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t 
   if (in_dtype == KVF_IN_F16)
     return quantize_typed(static_cast<const __half*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
   return quantize_typed(static_cast<const float*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
+}
+
+cudaError_t launch_minmax_init(int* kmin, int* kmax, size_t np, cudaStream_t st) {
+  if (np == 0) return cudaSuccess;
+  const unsigned ig = (unsigned)std::min<size_t>((np + 255) / 256, 4096);
+  k_minmax_init<<<ig, 256, 0, st>>>(kmin, kmax, np);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantpack_channel(const float* P, size_t H, size_t T, size_t R, const int* kmin,
+                                     const int* kmax, int data_type, float* scales, float* mins,
+                                     uint8_t* out, uint32_t* hist, cudaStream_t st) {
+  const size_t n = H * T * R;
+  const size_t np = H * R;
+  const size_t nb = std::max(packed_len(n, data_type), np);
+  if (nb == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)std::min<size_t>((nb + 255) / 256, (size_t)kSMs * 16);
+  const float levels = quant_levels(data_type);
+  if (data_type == KVF_INT4) {
+    if (hist) k_quantpack_channel<true, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist);
+    else k_quantpack_channel<true, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr);
+  } else {
+    if (hist) k_quantpack_channel<false, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist);
+    else k_quantpack_channel<false, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr);
+  }
+  note_launches(1);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,

@@ -34,43 +34,95 @@
 namespace kvf {
 namespace {
 
-constexpr int kWarpsPerBlock = 4;
+constexpr int kWarpsPerBlock = 4;  // encoder: chunks per block
+constexpr int kDecWarps = 2;       // decoder: chunks per block
+constexpr uint32_t kDecWcap = kRansChunk + 2;  // renormalisation words staged per decoding warp
+
+// cp.async helpers: asynchronous global -> shared copies, many in flight per thread
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n" ::);
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// exclusive prefix sum of one value per thread over a block of blockDim.x threads
+template <typename T>
+__device__ __forceinline__ T block_exclusive_scan(T v, T* warp_tot, T* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  T incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    T t = (lane < nw) ? warp_tot[lane] : T(0);
+    T ti = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T u = __shfl_up_sync(0xffffffffu, ti, o);
+      if (lane >= o) ti += u;
+    }
+    if (lane < nw) warp_tot[lane] = ti - t;
+    if (lane == nw - 1) *total = ti;
+  }
+  __syncthreads();
+  return warp_tot[w] + incl - v;
+}
 
 __global__ void __launch_bounds__(256) k_rans_normalize(const uint32_t* __restrict__ freq,
                                                         RansTables* __restrict__ tab,
                                                         unsigned* __restrict__ status) {
   __shared__ unsigned long long sN;
-  __shared__ uint32_t f[256], q[256], cum[256];
-  __shared__ int bad;
-  const int s = threadIdx.x;
-  f[s] = freq[s];
-  if (s == 0) { sN = 0ull; bad = 0; }
+  __shared__ uint32_t q[256], cum[256];
+  __shared__ uint32_t sS, wtot[8], total;
+  __shared__ unsigned long long wbest[8];
+  __shared__ int bad, argmax;
+  const int s = threadIdx.x, lane = s & 31, w = s >> 5;
+  const uint32_t f = freq[s];
+  if (s == 0) { sN = 0ull; sS = 0u; bad = 0; }
   __syncthreads();
-  atomicAdd(&sN, (unsigned long long)f[s]);
+  atomicAdd(&sN, (unsigned long long)f);
   __syncthreads();
   const unsigned long long N = sN;
   if (N == 0ull) {
     if (s == 0) atomicOr(status, kDevErrEntropy);
     return;
   }
-  if (f[s] == 0) {
-    q[s] = 0;
-  } else {
-    const unsigned long long v = ((unsigned long long)f[s] * kRansM) / N;
-    q[s] = (uint32_t)(v < 1ull ? 1ull : v);
+  uint32_t qs = 0;
+  if (f) {
+    const unsigned long long v = ((unsigned long long)f * kRansM) / N;
+    qs = (uint32_t)(v < 1ull ? 1ull : v);
   }
+  q[s] = qs;
+  atomicAdd(&sS, qs);
+  // most frequent symbol, lowest index on ties
+  unsigned long long key = ((unsigned long long)f << 8) | (unsigned long long)(255 - s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long u = __shfl_xor_sync(0xffffffffu, key, o);
+    key = u > key ? u : key;
+  }
+  if (lane == 0) wbest[w] = key;
   __syncthreads();
   if (s == 0) {
-    unsigned long long S = 0;
-    int argmax = 0;
-    for (int k = 0; k < 256; ++k) {
-      S += q[k];
-      if (f[k] > f[argmax]) argmax = k;
-    }
+    unsigned long long b = wbest[0];
+    for (int k = 1; k < 8; ++k) b = wbest[k] > b ? wbest[k] : b;
+    argmax = 255 - (int)(b & 0xFF);
+    unsigned long long S = sS;
     if (S < kRansM) {
       q[argmax] += (uint32_t)(kRansM - S);
     } else {
-      while (S > kRansM) {
+      while (S > kRansM) {  // rare: many symbols lifted to 1
         int best = -1;
         for (int k = 0; k < 256; ++k)
           if (q[k] > 1 && (best < 0 || q[k] > q[best])) best = k;
@@ -81,30 +133,44 @@ __global__ void __launch_bounds__(256) k_rans_normalize(const uint32_t* __restri
         S -= d;
       }
     }
-    uint32_t c = 0;
-    for (int k = 0; k < 256; ++k) { cum[k] = c; c += q[k]; }
   }
   __syncthreads();
   if (bad) {
     if (s == 0) atomicOr(status, kDevErrEntropy);
     return;
   }
-  tab->q[s] = q[s];
+  const uint32_t qf = q[s];
+  cum[s] = block_exclusive_scan<uint32_t>(qf, wtot, &total);
+  __syncthreads();
+  tab->q[s] = qf;
   tab->cum[s] = cum[s];
-  tab->rcp[s] = q[s] ? 0xFFFFFFFFu / q[s] : 0u;
-  // slot -> symbol: the last symbol whose cum <= slot (unseen symbols share
-  // the cum of the next seen one and therefore never win)
-  for (uint32_t k = s; k < kRansM; k += blockDim.x) {
-    int lo = 0, hi = 255;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (cum[mid] <= k) lo = mid; else hi = mid - 1;
+  tab->rcp[s] = qf ? 0xFFFFFFFFu / qf : 0u;
+  // slot -> symbol: thread s fills slots [128 s, 128 s + 128), starting from the
+  // last symbol whose cum <= 128 s and walking forward (unseen symbols share the
+  // cum of the next seen one and are skipped by the walk)
+  const uint32_t k0 = (uint32_t)s * (kRansM / 256);
+  int lo = 0, hi = 255;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cum[mid] <= k0) lo = mid; else hi = mid - 1;
+  }
+  int sym = lo;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(tab->slot2sym + k0);
+  for (uint32_t j = 0; j < kRansM / 256; j += 4) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t k = k0 + j + b;
+      while (cum[sym] + q[sym] <= k) ++sym;
+      word |= (uint32_t)sym << (8 * b);
     }
-    tab->slot2sym[k] = (uint8_t)lo;
+    dst[j / 4] = word;
   }
 }
 
-// one warp per chunk; the chunk's symbols are staged in shared memory first
+// One warp per chunk. The chunk's symbols are staged in shared memory with
+// asynchronous copies; the loop is software-pipelined so that the next step's
+// symbol and model entries are loaded while the current state is updated.
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8_t* __restrict__ data,
                                                                    uint64_t n, uint32_t chunk,
                                                                    const RansTables* __restrict__ tab,
@@ -117,19 +183,21 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
     cum[i] = tab->cum[i];
     rcp[i] = tab->rcp[i];
   }
-  __syncthreads();
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w;
-  if (c >= nchunks) return;
-  const uint64_t start = c * chunk;
-  const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
+  const bool live = c < nchunks;
+  const uint64_t start = live ? c * chunk : 0;
+  const uint32_t nsym = live ? (uint32_t)((n - start < chunk) ? (n - start) : chunk) : 0;
   uint8_t* buf = sbuf + (size_t)w * chunk;
-  // stage symbols (start is a multiple of chunk, itself a multiple of 32)
-  const uint32_t n16 = (reinterpret_cast<uintptr_t>(data + start) & 15u) == 0 ? nsym / 16 : 0;
-  for (uint32_t j = lane; j < n16; j += 32)
-    reinterpret_cast<uint4*>(buf)[j] = __ldg(reinterpret_cast<const uint4*>(data + start) + j);
-  for (uint32_t j = 16 * n16 + lane; j < nsym; j += 32) buf[j] = data[start + j];
-  __syncwarp();
+  if (live) {
+    const bool vec = (reinterpret_cast<uintptr_t>(data + start) & 15u) == 0;
+    const uint32_t n16 = vec ? nsym / 16 : 0;
+    for (uint32_t j = lane; j < n16; j += 32) cp_async16(buf + 16 * j, data + start + 16 * j);
+    for (uint32_t j = 16 * n16 + lane; j < nsym; j += 32) buf[j] = data[start + j];
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (!live) return;
 
   uint8_t* slot = slots + c * rans_slot_bytes(chunk);
   uint16_t* words = reinterpret_cast<uint16_t*>(slot + kRansChunkHeader);
@@ -137,12 +205,22 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
   uint32_t pos = capw;  // words are written backwards, ending at capw
   uint32_t x = kRansL;
   const uint32_t steps = (nsym + 31) / 32;
+  // preload the last step (the only one that may be partial)
+  uint32_t i = (steps - 1) * 32 + lane;
+  bool act = i < nsym;
+  uint32_t s = act ? buf[i] : 0u;
+  uint32_t f = q[s], cu = cum[s], rc = rcp[s];
   for (uint32_t st = steps; st-- > 0;) {
-    const uint32_t i = st * 32 + lane;
-    const bool active = i < nsym;
-    const uint32_t s = active ? buf[i] : 0u;
-    const uint32_t f = q[s];
-    const bool need = active && ((uint64_t)x >= ((uint64_t)f << 17));
+    const bool a0 = act;
+    const uint32_t f0 = f, c0 = cu, r0 = rc;
+    if (st > 0) {  // next step (st - 1) is always full
+      s = buf[(st - 1) * 32 + lane];
+      act = true;
+      f = q[s];
+      cu = cum[s];
+      rc = rcp[s];
+    }
+    const bool need = a0 && ((uint64_t)x >= ((uint64_t)f0 << 17));
     const unsigned mask = __ballot_sync(0xffffffffu, need);
     if (need) {
       const unsigned above = mask & ~((2u << lane) - 1u);  // emitting lanes above this one
@@ -150,11 +228,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
       x >>= 16;
     }
     pos -= __popc(mask);
-    if (active) {
-      uint32_t qq = __umulhi(x, rcp[s]);
-      uint32_t r = x - qq * f;
-      if (r >= f) { ++qq; r -= f; }
-      x = (qq << kRansProbBits) + r + cum[s];
+    if (a0) {
+      uint32_t qq = __umulhi(x, r0);
+      uint32_t r = x - qq * f0;
+      if (r >= f0) { ++qq; r -= f0; }
+      x = (qq << kRansProbBits) + r + c0;
     }
   }
   uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
@@ -162,44 +240,34 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
   if (lane == 0) hdr[0] = capw - pos;
 }
 
-// header + offsets: one block scans the chunk sizes
+// header + offsets: one block scans the chunk payload sizes
 __global__ void __launch_bounds__(1024) k_rans_offsets(const uint8_t* __restrict__ slots, uint64_t n,
                                                        uint32_t chunk, uint64_t nchunks,
                                                        uint8_t* __restrict__ out,
                                                        uint64_t* __restrict__ out_len) {
-  __shared__ uint64_t part[1024];
+  __shared__ unsigned long long wtot[32], total;
   const uint64_t per = (nchunks + blockDim.x - 1) / blockDim.x;
   const uint64_t c0 = threadIdx.x * per;
   const uint64_t c1 = (c0 + per < nchunks) ? c0 + per : nchunks;
   const size_t sb = rans_slot_bytes(chunk);
-  uint64_t local = 0;
+  unsigned long long local = 0;
   for (uint64_t c = c0; c < c1; ++c) {
     const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
     local += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
   }
-  part[threadIdx.x] = local;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint64_t run = 0;
-    for (int k = 0; k < (int)blockDim.x; ++k) {
-      const uint64_t v = part[k];
-      part[k] = run;
-      run += v;
-    }
-  }
-  __syncthreads();
+  const unsigned long long excl = block_exclusive_scan<unsigned long long>(local, wtot, &total);
   const uint64_t hdr = kRansHeader + 4ull * (nchunks + 1);
   uint32_t* off = reinterpret_cast<uint32_t*>(out + kRansHeader);
-  uint64_t run = hdr + part[threadIdx.x];
+  uint64_t run = hdr + excl;
   for (uint64_t c = c0; c < c1; ++c) {
     off[c] = (uint32_t)run;
     const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
     run += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
   }
-  if (threadIdx.x == blockDim.x - 1) {
-    // last thread's run ends at the total
-    off[nchunks] = (uint32_t)run;
-    *out_len = run;
+  if (threadIdx.x == 0) {
+    const uint64_t len = hdr + total;
+    off[nchunks] = (uint32_t)len;
+    *out_len = len;
     uint32_t* h = reinterpret_cast<uint32_t*>(out);
     h[0] = kRansMagic;
     h[1] = kRansProbBits;
@@ -233,18 +301,24 @@ __device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
   return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// one warp per chunk; slot table and model in shared memory
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_decode(const uint8_t* __restrict__ comp,
-                                                                   uint64_t comp_len_host,
-                                                                   const uint64_t* __restrict__ comp_len_dev,
-                                                                   const RansTables* __restrict__ tab,
-                                                                   uint64_t n, uint8_t* __restrict__ out,
-                                                                   unsigned* __restrict__ status) {
-  __shared__ __align__(16) uint8_t sym[kRansM];
-  __shared__ uint32_t qc[256];  // q | cum << 16
+// One warp per chunk. The slot table and model sit in shared memory; the
+// chunk's renormalisation words are copied into shared memory with
+// asynchronous 4-byte copies before decoding starts (chunks whose word count
+// exceeds the staging buffer are read from global memory instead).
+__global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
+                                                              uint64_t comp_len_host,
+                                                              const uint64_t* __restrict__ comp_len_dev,
+                                                              const RansTables* __restrict__ tab,
+                                                              uint64_t n, uint8_t* __restrict__ out,
+                                                              unsigned* __restrict__ status) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  uint8_t* sym = dsm;                                               // [2^15]
+  uint32_t* qc = reinterpret_cast<uint32_t*>(dsm + kRansM);         // [256] q | cum << 16
+  uint16_t* wstage = reinterpret_cast<uint16_t*>(dsm + kRansM + 1024);  // [kDecWarps][kDecWcap]
   for (int i = threadIdx.x; i < (int)(kRansM / 16); i += blockDim.x)
-    reinterpret_cast<uint4*>(sym)[i] = reinterpret_cast<const uint4*>(tab->slot2sym)[i];
+    cp_async16(sym + 16 * i, tab->slot2sym + 16 * i);
   for (int i = threadIdx.x; i < 256; i += blockDim.x) qc[i] = tab->q[i] | (tab->cum[i] << 16);
+  cp_async_wait_all();
   __syncthreads();
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t comp_len = comp_len_dev ? *comp_len_dev : comp_len_host;
@@ -259,8 +333,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_decode(const uint8
                       nchunks == (n + chunk - 1) / chunk && rd32(comp + 28) == hdr && hdr <= comp_len &&
                       rd32(comp + kRansHeader + 4 * nchunks) == comp_len;
   if (!hdr_ok) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
-  const uint64_t nwarps = (uint64_t)gridDim.x * kWarpsPerBlock;
-  for (uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w; c < nchunks; c += nwarps) {
+  uint16_t* stage = wstage + (size_t)w * kDecWcap;
+  const uint64_t nwarps = (uint64_t)gridDim.x * kDecWarps;
+  for (uint64_t c = (uint64_t)blockIdx.x * kDecWarps + w; c < nchunks; c += nwarps) {
     const uint64_t off = rd32(comp + kRansHeader + 4 * c);
     const uint64_t end = rd32(comp + kRansHeader + 4 * (c + 1));
     if (off < hdr || end > comp_len || end < off + kRansChunkHeader || (off & 3u)) {
@@ -274,7 +349,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_decode(const uint8
     }
     uint32_t x = rd32(comp + off + 4 + 4 * lane);
     bool bad = x < kRansL;
-    const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
+    const uint16_t* gwords = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
+    const uint16_t* words = gwords;
+    if (nw <= kDecWcap) {  // stage pairs of words (the payload is padded to 4 bytes)
+      const uint32_t npair = (nw + 1) / 2;
+      const uint8_t* src = comp + off + kRansChunkHeader;
+      for (uint32_t j = lane; j < npair; j += 32) cp_async4(stage + 2 * j, src + 4 * j);
+      cp_async_wait_all();
+      __syncwarp();
+      words = stage;
+    }
     const uint64_t start = c * chunk;
     const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
     const uint32_t steps = (nsym + 31) / 32;
@@ -300,6 +384,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_decode(const uint8
     }
     bad = bad || x != kRansL || p != nw;
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, kDevErrCorrupt);
+    __syncwarp();
   }
 }
 
@@ -344,10 +429,12 @@ cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint6
   // the grid is sized for the encoder's default chunk size; warps loop over
   // chunks, so a container with any chunk size named in its header decodes
   const size_t nc = rans_num_chunks(n, kRansChunk);
-  const unsigned grid = (unsigned)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  k_rans_decode<<<grid, kWarpsPerBlock * 32, 0, st>>>(comp, comp_len, comp_len_dev, tab, n, out, status);
+  const unsigned grid = (unsigned)((nc + kDecWarps - 1) / kDecWarps);
+  const size_t smem = kRansM + 1024 + (size_t)kDecWarps * kDecWcap * 2;
+  const cudaError_t e = cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k_rans_decode<<<grid, kDecWarps * 32, smem, st>>>(comp, comp_len, comp_len_dev, tab, n, out, status);
   note_launches(1);
   return cudaGetLastError();
 }
-
 }  // namespace kvf
