@@ -196,7 +196,8 @@ def _config(args, w):
     return {"workload": args.workload, "preset": w["preset"], "layers": args.layers or w.get("layers", 1),
             "heads": w["H"], "tokens": w["T"], "head_dim": w["D"], "input_dtype": w["dtype"],
             "output_dtype": "f32", "basis": "calibrated per layer, computed before the timed region",
-            "l2": "inputs larger than L2 (no flush)", "parallelism": f"layer-sharded x{args.gpus}"}
+            "l2": "inputs larger than L2 (no flush)", "parallelism": f"layer-sharded x{args.gpus}",
+            "streams_per_gpu": getattr(args, "streams", 1)}
 
 
 # ---------------------------------------------------------------------------
@@ -238,25 +239,43 @@ def gpu_arm(args):
             t_basis += time.perf_counter() - t0
         layers.append((l, k, v, kb, vb))
     torch.cuda.synchronize()
-    ko = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
-    vo = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
     stream = torch.cuda.current_stream(dev)
     sptr = C.c_void_p(stream.cuda_stream)
+    # layers are issued round-robin on several streams, each with its own output
+    # buffers, so one layer's latency-bound entropy coding overlaps another
+    # layer's bandwidth-bound projection and reconstruction
+    nstreams = max(1, min(args.streams, len(layers)))
+    workers = [torch.cuda.Stream(device=dev) for _ in range(nstreams)]
+    wptr = [C.c_void_p(s.cuda_stream) for s in workers]
+    outs = [(torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}"),
+             torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")) for _ in range(nstreams)]
+    ko, vo = outs[0]
 
-    def run_layer(l, k, v, kb, vb, keep=False):
+    def run_layer(l, k, v, kb, vb, keep=False, wi=0):
         h = C.c_void_p()
+        sp = wptr[wi]
         L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), in_code, H, T, D, l,
                                        C.byref(cfg), kb.handle if kb else None, vb.handle if vb else None,
-                                       C.byref(h), sptr))
-        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sptr))
+                                       C.byref(h), sp))
+        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(outs[wi][0].data_ptr()),
+                                         C.c_void_p(outs[wi][1].data_ptr()), sp))
         if keep:
             return h
         lib.kvf_compressed_free(h)
         return None
 
+    start_ev = torch.cuda.Event()
+    done_ev = [torch.cuda.Event() for _ in workers]
+
     def step():
-        for lay in layers:
-            run_layer(*lay)
+        start_ev.record(stream)
+        for w in workers:
+            w.wait_event(start_ev)
+        for i, lay in enumerate(layers):
+            run_layer(*lay, wi=i % nstreams)
+        for w, e in zip(workers, done_ev):
+            e.record(w)
+            stream.wait_event(e)
 
     for _ in range(args.warmup):
         step()
@@ -267,6 +286,7 @@ def gpu_arm(args):
     err = {"err2_k": 0.0, "ref2_k": 0.0, "err2_v": 0.0, "ref2_v": 0.0}
     for lay in layers:
         h = run_layer(*lay, keep=True)
+        torch.cuda.synchronize()
         n = C.c_size_t()
         L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
         comp_bytes += n.value
@@ -276,6 +296,7 @@ def gpu_arm(args):
         err["err2_v"] += float(((vo - vf) ** 2).sum())
         err["ref2_v"] += float((vf ** 2).sum())
         lib.kvf_compressed_free(h)
+    torch.cuda.synchronize()
     L.check(lib.kvf_sync(ctx, sptr))
     in_bytes = sum(lay[1].numel() * lay[1].element_size() * 2 for lay in layers)
     orig_bytes = len(layers) * 2 * H * T * D * 4
@@ -413,6 +434,7 @@ def main():
     ap.add_argument("--workload", default="llama3_8b_32k")
     ap.add_argument("--layers", type=int, default=0, help="number of layers (default: the workload's)")
     ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

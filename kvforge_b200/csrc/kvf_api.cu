@@ -118,7 +118,6 @@ struct TensorC {
   float* d_scales = nullptr;
   float* d_mins = nullptr;
   uint32_t* d_freq = nullptr;
-  RansTables* d_tab = nullptr;       // model built from d_freq (kept for decoding)
   std::shared_ptr<BasisData> basis;  // projection state, when projected
 };
 
@@ -128,10 +127,30 @@ struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
   unsigned* d_status = nullptr;
-  // a layer's value tensor runs on `side` while its key tensor runs on the
-  // caller's stream; fork/join events order the two
-  cudaStream_t side = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
+  // a layer's value tensor runs on a side stream paired with the caller's
+  // stream while its key tensor runs on the caller's stream; fork/join events
+  // order the two. One side stream per caller stream, made on first use, so
+  // layers issued on different caller streams stay independent.
+  struct Side {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+  };
+  std::vector<std::pair<cudaStream_t, Side>> sides;
+  cudaError_t side_for(cudaStream_t st, Side** out) {
+    for (auto& kv : sides)
+      if (kv.first == st) {
+        *out = &kv.second;
+        return cudaSuccess;
+      }
+    Side sd;
+    cudaError_t e = cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sd.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return e;
+    sides.emplace_back(st, sd);
+    *out = &sides.back().second;
+    return cudaSuccess;
+  }
   // stage timing (kvf_profile_enable / kvf_profile_read)
   struct Rec {
     int stage;
@@ -238,7 +257,7 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
   const size_t n = H * T * D;
   int* keys = nullptr;
   if (axis == KVF_PER_CHANNEL) {
-    keys = sc.get<int>(2 * H * D);
+    keys = sc.get<int>(3 * H * D);  // min keys, max keys, reciprocal scales
     if (!keys) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   }
   if (dt == KVF_INT8) {
@@ -253,14 +272,14 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
   return KVF_OK;
 }
 
-// model (into `tab`) -> chunk coding -> container in `out` (length -> d_len)
+// chunk coding (the model is built from `freq` inside the kernel) -> container
+// in `out`, its length in d_len
 kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, size_t plen,
-                            const uint32_t* freq, RansTables* tab, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
+                            const uint32_t* freq, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
   const size_t nc = rans_num_chunks(plen, kRansChunk);
   uint8_t* slots = sc.get<uint8_t>(nc * rans_slot_bytes(kRansChunk));
-  if (!tab || !slots) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
-  KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, tab, slots, st));
+  if (!slots) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, freq, slots, ctx->d_status, st));
   KVF_CUDA(launch_rans_assemble(slots, plen, kRansChunk, out, d_len, st));
   return KVF_OK;
 }
@@ -341,19 +360,25 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
       KVF_CUDA(launch_quantpack_channel(P, H, T, qcols, po.kmin, po.kmax, dt, out->d_scales, out->d_mins, packed,
                                         hist, st));
     } else if (qcols <= 32) {
-      uint8_t* codes = (dt == KVF_INT8) ? packed : sc.get<uint8_t>(n);
-      if (!codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+      // INT4 bytes are packed inside the projection kernel when every
+      // 128-token tile starts at an even flat index (R or T even)
+      const bool fuse_pack = dt == KVF_INT4 && (qcols % 2 == 0 || T % 2 == 0);
+      uint8_t* codes = (dt == KVF_INT8) ? packed : (fuse_pack ? nullptr : sc.get<uint8_t>(n));
+      if (dt == KVF_INT4 && !fuse_pack && !codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
       po.mode = 2;
       po.codes = codes;
+      po.packed = fuse_pack ? packed : nullptr;
+      po.hist = (dt == KVF_INT8 || fuse_pack) ? hist : nullptr;
       po.scales = out->d_scales;
       po.mins = out->d_mins;
       {
-        StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + (double)n + 8.0 * np, st);
+        StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + (double)plen + 8.0 * np, st);
         KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
       }
-      StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n + (double)plen, st);
-      if (dt == KVF_INT4) KVF_CUDA(launch_pack_int4(codes, n, packed, hist, st));
-      else if (hist) KVF_CUDA(launch_histogram(packed, n, hist, st));
+      if (dt == KVF_INT4 && !fuse_pack) {
+        StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n + (double)plen, st);
+        KVF_CUDA(launch_pack_int4(codes, n, packed, hist, st));
+      }
     } else {
       float* P = sc.get<float>(n);
       if (!P) return fail(KVF_ERR_CUDA, "scratch allocation failed");
@@ -380,10 +405,9 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
     out->data_cap = rans_max_len(plen, kRansChunk);
     out->d_data = owner->alloc<uint8_t>(out->data_cap, st);
     out->d_len = owner->alloc<uint64_t>(1, st);
-    out->d_tab = owner->alloc<RansTables>(1, st);
-    if (!out->d_data || !out->d_len || !out->d_tab) return fail(KVF_ERR_CUDA, "allocation failed");
+    if (!out->d_data || !out->d_len) return fail(KVF_ERR_CUDA, "allocation failed");
     StageTimer tm(ctx, KVF_STAGE_ENTROPY_ENCODE, (double)plen, st);
-    KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_tab, out->d_data, out->d_len, st));
+    KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_data, out->d_len, st));
     out->len_known = false;
   } else {
     out->d_data = packed;
@@ -399,12 +423,10 @@ kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStr
   Scratch sc(st);
   const uint8_t* codes = t.d_data;
   if (t.has_freq) {
-    RansTables* tab = t.d_tab ? t.d_tab : sc.get<RansTables>(1);
     uint8_t* dec = sc.get<uint8_t>(t.packed_len);
-    if (!tab || !dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    if (!dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
     StageTimer tm(ctx, KVF_STAGE_ENTROPY_DECODE, 2.0 * t.packed_len, st);
-    if (!t.d_tab) KVF_CUDA(launch_rans_normalize(t.d_freq, tab, ctx->d_status, st));
-    KVF_CUDA(launch_rans_decode(t.d_data, t.data_len, t.len_known ? nullptr : t.d_len, tab, t.packed_len,
+    KVF_CUDA(launch_rans_decode(t.d_data, t.data_len, t.len_known ? nullptr : t.d_len, t.d_freq, t.packed_len,
                                 dec, ctx->d_status, st));
     codes = dec;
   }
@@ -676,9 +698,6 @@ kvf_status deser_tensor(kvf_compressed* c, TensorC& t, Reader& r, cudaStream_t s
     t.d_freq = c->alloc<uint32_t>(256);
     if (!t.d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
     KVF_TRY(up(t.d_freq, 256 * 4));
-    t.d_tab = c->alloc<RansTables>(1);
-    if (!t.d_tab) return fail(KVF_ERR_CUDA, "allocation failed");
-    KVF_CUDA(launch_rans_normalize(t.d_freq, t.d_tab, c->ctx->d_status, st));
   }
   t.data_cap = t.data_len;
   t.d_data = c->alloc<uint8_t>(t.data_len);
@@ -728,9 +747,6 @@ kvf_status kvf_init(int device, kvf_ctx** out) {
   }
   cudaError_t e = cudaMalloc(&ctx->d_status, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     delete ctx;
     return fail(KVF_ERR_CUDA, std::string("context allocation: ") + cudaGetErrorString(e));
@@ -747,12 +763,12 @@ kvf_status kvf_destroy(kvf_ctx* ctx) {
     cudaEventDestroy(r.b);
   }
   for (auto e : ctx->spare) cudaEventDestroy(e);
-  if (ctx->side) {
-    cudaStreamSynchronize(ctx->side);
-    cudaStreamDestroy(ctx->side);
+  for (auto& kv : ctx->sides) {
+    cudaStreamSynchronize(kv.second.s);
+    cudaStreamDestroy(kv.second.s);
+    cudaEventDestroy(kv.second.fork);
+    cudaEventDestroy(kv.second.join);
   }
-  if (ctx->fork) cudaEventDestroy(ctx->fork);
-  if (ctx->join) cudaEventDestroy(ctx->join);
   cudaFree(ctx->d_status);
   delete ctx;
   return KVF_OK;
@@ -965,14 +981,16 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
     return KVF_OK;
   }
   if (R <= 32) {
-    uint8_t* codes = (data_type == KVF_INT8) ? packed : sc.get<uint8_t>(n);
-    if (!codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    const bool fuse_pack = data_type == KVF_INT4 && (R % 2 == 0 || T % 2 == 0);
+    uint8_t* codes = (data_type == KVF_INT8) ? packed : (fuse_pack ? nullptr : sc.get<uint8_t>(n));
+    if (data_type == KVF_INT4 && !fuse_pack && !codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
     po.mode = 2;
     po.codes = codes;
+    po.packed = fuse_pack ? packed : nullptr;
     po.scales = scales;
     po.mins = mins;
     KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
-    if (data_type == KVF_INT4) KVF_CUDA(launch_pack_int4(codes, n, packed, nullptr, st));
+    if (data_type == KVF_INT4 && !fuse_pack) KVF_CUDA(launch_pack_int4(codes, n, packed, nullptr, st));
     return KVF_OK;
   }
   float* P = sc.get<float>(n);
@@ -1000,10 +1018,8 @@ kvf_status kvf_rans_encode(kvf_ctx* ctx, const uint8_t* data, size_t n, uint8_t*
   Scratch sc(st);
   uint64_t* d_len = sc.get<uint64_t>(1);
   if (!d_len) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  RansTables* tab = sc.get<RansTables>(1);
-  if (!tab) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   KVF_CUDA(launch_histogram(data, n, freq, st));
-  KVF_TRY(rans_encode_into(ctx, sc, data, n, freq, tab, out, d_len, st));
+  KVF_TRY(rans_encode_into(ctx, sc, data, n, freq, out, d_len, st));
   uint64_t len = 0;
   KVF_CUDA(cudaMemcpyAsync(&len, d_len, sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
   KVF_TRY(read_status(ctx, st));
@@ -1020,10 +1036,7 @@ kvf_status kvf_rans_decode(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len, c
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
   Scratch sc(st);
-  RansTables* tab = sc.get<RansTables>(1);
-  if (!tab) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
-  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, tab, original_len, out, ctx->d_status, st));
+  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, freq, original_len, out, ctx->d_status, st));
   return read_status(ctx, st);
 }
 
@@ -1041,11 +1054,9 @@ kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t 
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
   Scratch sc(st);
-  RansTables* tab = sc.get<RansTables>(1);
   uint8_t* dec = sc.get<uint8_t>(plen);
-  if (!tab || !dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  KVF_CUDA(launch_rans_normalize(freq, tab, ctx->d_status, st));
-  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, tab, plen, dec, ctx->d_status, st));
+  if (!dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, freq, plen, dec, ctx->d_status, st));
   KVF_CUDA(launch_dequantize(dec, scales, mins, data_type, axis, H, T, D, out, st));
   return KVF_OK;
 }
@@ -1139,17 +1150,19 @@ kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values
     c->d_scores = c->alloc<float>(H);
     if (!c->d_scores) return fail(KVF_ERR_CUDA, "allocation failed");
   }
-  // keys on the caller's stream, values on the side stream, joined before return
-  KVF_CUDA(cudaEventRecord(ctx->fork, st));
-  KVF_CUDA(cudaStreamWaitEvent(ctx->side, ctx->fork, 0));
+  // keys on the caller's stream, values on its side stream, joined before return
+  kvf_ctx::Side* sd = nullptr;
+  KVF_CUDA(ctx->side_for(st, &sd));
+  KVF_CUDA(cudaEventRecord(sd->fork, st));
+  KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
   kvf_status s = compress_tensor(ctx, c.get(), keys, in_dtype, H, T, D, cfg->key_data_type, KVF_PER_CHANNEL, kb,
                                  cfg->enable_entropy_coding != 0, cfg->enable_calibration != 0, c->d_scores,
                                  &c->key, st);
   if (s == KVF_OK)
     s = compress_tensor(ctx, c.get(), values, in_dtype, H, T, D, cfg->value_data_type, KVF_PER_TOKEN, vb,
-                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, ctx->side);
-  cudaError_t je = cudaEventRecord(ctx->join, ctx->side);
-  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, ctx->join, 0);
+                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, sd->s);
+  cudaError_t je = cudaEventRecord(sd->join, sd->s);
+  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   if (s != KVF_OK) {
     std::string msg = g_err;
@@ -1167,12 +1180,14 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
   if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
-  KVF_CUDA(cudaEventRecord(ctx->fork, st));
-  KVF_CUDA(cudaStreamWaitEvent(ctx->side, ctx->fork, 0));
+  kvf_ctx::Side* sd = nullptr;
+  KVF_CUDA(ctx->side_for(st, &sd));
+  KVF_CUDA(cudaEventRecord(sd->fork, st));
+  KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
   kvf_status s = decompress_tensor(ctx, c->key, keys_out, st);
-  if (s == KVF_OK) s = decompress_tensor(ctx, c->value, values_out, ctx->side);
-  cudaError_t je = cudaEventRecord(ctx->join, ctx->side);
-  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, ctx->join, 0);
+  if (s == KVF_OK) s = decompress_tensor(ctx, c->value, values_out, sd->s);
+  cudaError_t je = cudaEventRecord(sd->join, sd->s);
+  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   return s;
 }

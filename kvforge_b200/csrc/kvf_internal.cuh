@@ -30,14 +30,6 @@ constexpr unsigned kDevErrCorrupt = 1u;
 constexpr unsigned kDevErrEntropy = 2u;
 constexpr unsigned kDevErrTimeout = 4u;
 
-// normalised model + decode table built on the device from 256 counts
-struct RansTables {
-  uint32_t q[256];     // quantised frequencies, sum 2^15
-  uint32_t cum[256];   // exclusive prefix of q
-  uint32_t rcp[256];   // 0xFFFFFFFF / q  (exact division with one correction)
-  uint8_t slot2sym[kRansM];
-};
-
 __host__ __device__ inline size_t rans_num_chunks(size_t n, uint32_t chunk) { return (n + chunk - 1) / chunk; }
 __host__ __device__ inline size_t rans_slot_words(uint32_t chunk) { return chunk + 2; }
 __host__ __device__ inline size_t rans_slot_bytes(uint32_t chunk) {
@@ -65,12 +57,13 @@ void note_launches(unsigned n);
 // ---- KIVI arithmetic shared by every kernel that quantizes (quantize.rs) ----
 __device__ __forceinline__ float canon0(float v) { return v == 0.0f ? 0.0f : v; }
 
+// NaN-ignoring min/max with -0.0 canonicalised to +0.0: fminf/fmaxf already
+// return the other operand for a NaN, and v + 0.0 (IEEE, round to nearest)
+// maps -0.0 to +0.0 and leaves every other value unchanged
 __device__ __forceinline__ void mm_update(float v, float& mn, float& mx) {
-  if (!isnan(v)) {
-    v = canon0(v);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
-  }
+  v = __fadd_rn(v, 0.0f);
+  mn = fminf(mn, v);
+  mx = fmaxf(mx, v);
 }
 
 __device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
@@ -94,6 +87,41 @@ __device__ __forceinline__ uint32_t qcode(float v, float mn, float scale, float 
   return (uint32_t)r;
 }
 
+// The same code without a division per element. With inv = RN(1/scale), the
+// product y = RN(n * inv) is within 1.5 * 2^-23 * y of RN(n / scale); codes need
+// y <= 255.5, so |y - RN(n/scale)| < 2^-14.4. Rounding to an integer can only
+// differ when y lies within that distance of a half-integer, and then the
+// exact IEEE quotient is computed. NaN and +-inf take the same paths as qcode.
+__device__ __forceinline__ uint32_t qcode_fast(float v, float mn, float scale, float inv, float levels) {
+  const float n = __fsub_rn(v, mn);
+  const float y = __fmul_rn(n, inv);
+  const float fl = floorf(y);
+  const float fr = __fsub_rn(y, fl);
+  float r;
+  if (fabsf(__fsub_rn(fr, 0.5f)) < 1.220703125e-4f) {  // within 2^-13 of a half-integer
+    r = roundf(__fdiv_rn(n, scale));
+  } else {
+    // away from the half-integers round-half-away-from-zero is floor + (frac > 1/2);
+    // NaN and -inf fall to 0, +inf to levels through the clamp
+    r = __fadd_rn(fl, fr > 0.5f ? 1.0f : 0.0f);
+  }
+  r = fminf(fmaxf(r, 0.0f), levels);  // fmaxf maps NaN to 0 (`as u8` of NaN)
+  return (uint32_t)r;
+}
+
+// two independent fused multiply-adds in one instruction (fma.rn.f32x2,
+// sm_100); each element is rounded once, exactly as __fmaf_rn
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long A, B, Cc, Dd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(B) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(Cc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(Dd) : "l"(A), "l"(B), "l"(Cc));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(Dd));
+  return d;
+}
+
 __device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
   return __fadd_rn(__fmul_rn((float)q, scale), mn);
 }
@@ -109,6 +137,7 @@ __device__ __forceinline__ float kfloat(int k) { return __int_as_float(k >= 0 ? 
 
 // ---- kernel launchers (return the launch error, if any) -------------------
 // quantization (kvf_quant.cu)
+// minmax_keys: scratch of 3 * H * D ints for per-channel (unused per-token)
 cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                                   int data_type, int axis, uint8_t* codes, float* scales,
                                   float* mins, int* minmax_keys, cudaStream_t st);
@@ -132,6 +161,10 @@ size_t project_num_tiles(size_t T);
 // min/max keys (kmin/kmax, initialised to +inf/-inf keys); mode 2: per-token
 // codes + scales/mins (R <= 32). cpart (optional): key calibration partials,
 // project_num_tiles(T) per head.
+// mode 2 writes either unpacked codes (`codes`) or, when `packed` is set,
+// INT4 bytes packed over the flat index (callers set it only when every
+// 128-token tile starts at an even flat index: R or T even); `hist`, when
+// set, counts the bytes written (packed bytes, or INT8 codes).
 struct ProjectOut {
   int mode = 0;
   float* P = nullptr;
@@ -139,6 +172,8 @@ struct ProjectOut {
   int* kmin = nullptr;
   int* kmax = nullptr;
   uint8_t* codes = nullptr;
+  uint8_t* packed = nullptr;
+  uint32_t* hist = nullptr;
   float* scales = nullptr;
   float* mins = nullptr;
   float levels = 15.0f;
@@ -166,15 +201,14 @@ cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t 
                         float* partial, double* gram, cudaStream_t st);
 
 // rANS (kvf_rans.cu)
-cudaError_t launch_rans_normalize(const uint32_t* freq, RansTables* tab, unsigned* status,
-                                  cudaStream_t st);
-cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk,
-                               const RansTables* tab, uint8_t* slots, cudaStream_t st);
+// encode and decode build the model from the 256 counts themselves
+cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
+                               uint8_t* slots, unsigned* status, cudaStream_t st);
 cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk, uint8_t* out,
                                  uint64_t* out_len, cudaStream_t st);
 // comp_len_dev (when not NULL) supplies the container length from device memory
 cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
-                               const RansTables* tab, size_t n, uint8_t* out, unsigned* status,
+                               const uint32_t* freq, size_t n, uint8_t* out, unsigned* status,
                                cudaStream_t st);
 
 }  // namespace kvf

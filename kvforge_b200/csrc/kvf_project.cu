@@ -29,31 +29,6 @@ constexpr int kRecRows = 128;                    // token rows per reconstruct b
 constexpr int kCalibTile = 1 << 16;              // elements per calibration block
 constexpr int kGramTile = 512;                   // tokens per Gram block
 
-template <typename TIn>
-struct Vec;
-template <>
-struct Vec<float> {
-  static constexpr int N = 4;
-  __device__ static void load(const float* p, float* o) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(p));
-    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-  }
-};
-template <>
-struct Vec<__half> {
-  static constexpr int N = 8;
-  __device__ static void load(const __half* p, float* o) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-      o[2 * k] = f.x;
-      o[2 * k + 1] = f.y;
-    }
-  }
-};
-
 __device__ __forceinline__ float ldf(const float* p, size_t i) { return __ldg(p + i); }
 __device__ __forceinline__ float ldf(const __half* p, size_t i) { return __half2float(__ldg(p + i)); }
 
@@ -81,17 +56,26 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 }
 
 // ---- projection -------------------------------------------------------------
-// grid (ceil(T / 128), H), 128 threads, one token row per thread. The row is
-// read in 256-byte segments whose sixteen 16-byte loads are issued together, so
-// a whole segment is in flight at once (the kernel is bound by HBM latency
-// otherwise). The basis of head h sits transposed in shared memory, vT[c][r],
-// so the RG basis values of one c are a broadcast float4 load. Epilogues:
-//   MODE 0: write P [H,T,R];
-//   MODE 1: write P and fold each column into per-(head, r) min/max with
-//           order-preserving integer atomics (keys: per-channel parameters
-//           need every token before any code can be formed);
-//   MODE 2: quantize the row per token at once -- codes [H,T,R] bytes plus a
-//           scale/min per token; P never reaches memory (values; R <= RG).
+// One persistent kernel. The grid walks (head, 128-token tile) items in
+// contiguous ranges; thread t owns row t of every tile. PIPE variant (rows a
+// multiple of 16 bytes, 16-byte aligned input): each thread streams its own
+// row into shared memory with asynchronous 16-byte copies (cp.async), two
+// stages deep, so the next tile's row is in flight while the current one is
+// computed; 16-byte chunks are XOR-swizzled by row so the rows a warp reads
+// fall on distinct banks (or rows are padded by 16 bytes where the swizzle
+// does not apply). Generic variant: scalar loads from global memory.
+//
+// Each coefficient is a fused multiply-add chain over c = 0..D-1 from +0.0;
+// two chains advance per fma.rn.f32x2 (each element rounded once), so values
+// are identical to the CPU oracle's fmaf chain. The basis of head h sits
+// transposed in shared memory, vT[c][r], read with broadcast float4 loads.
+//
+// Epilogues (outputs staged in shared memory, stored coalesced):
+//   MODE 0: P [H,T,R];
+//   MODE 1: P and per-(head, r) min/max folded into block-local keys,
+//           flushed with one global atomic per (block, head, r);
+//   MODE 2: per-token quantization: scale/min per token, codes as bytes or
+//           INT4-packed bytes, plus an optional byte histogram.
 template <typename TIn>
 struct Seg;
 template <>
@@ -118,183 +102,371 @@ struct Seg<float> {
   }
 };
 
-template <typename TIn, int RG, bool VEC, bool CALIB, int MODE>
-__global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict__ x, int T, int D,
-                                                        const float* __restrict__ bvt,
-                                                        const uint64_t* __restrict__ ranks, int R,
-                                                        int Rpad, ProjectOut o) {
-  extern __shared__ __align__(16) float vT[];  // [D][Rpad]
-  const int h = blockIdx.y;
-  const uint64_t rk = ranks[h];
-  const int rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
-  const float* B = bvt + (size_t)h * R * D;
-  for (int i = threadIdx.x; i < D * Rpad; i += blockDim.x) {
-    const int c = i / Rpad, r = i - c * Rpad;
-    vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
-  }
-  __syncthreads();
+__device__ __forceinline__ void cp16(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-  const int t = blockIdx.x * kProjThreads + threadIdx.x;
-  const bool ok = t < T;
-  const size_t g = (size_t)h * T + (ok ? t : 0);
-  const TIn* xr = x + g * D;
-  double s1 = 0.0, s2 = 0.0;
-  for (int rg = 0; rg < R; rg += RG) {
-    float acc[RG];
+// shared-memory layout (byte offsets, all multiples of 16), computed on the host
+struct ProjSmem {
+  int keys;    // [2 * Rk] int
+  int hist;    // [256] u32
+  int ostage;  // output staging, 128 * R * 4 bytes (or -1: the current row stage)
+  int xbuf;    // [2][128][stride] (PIPE)
+  int stride;  // bytes per staged row
+  int swz;     // 1: XOR-swizzle 16-byte chunks by row
+  int pow2;    // 16-byte chunks per row is a power of two
+  int total;
+};
+
+template <int RG>
+__device__ __forceinline__ void fma_row(float2 (&acc)[RG / 2], float xv, const float* vrow) {
+  const float2 xx = make_float2(xv, xv);
+  const float4* vr = reinterpret_cast<const float4*>(vrow);
 #pragma unroll
-    for (int r = 0; r < RG; ++r) acc[r] = 0.0f;
-    if (VEC) {
-      constexpr int PV = Seg<TIn>::PV;
-      for (int c0 = 0; c0 < D; c0 += 16 * PV) {
-        const int nv = min(16, (D - c0) / PV);
-        uint4 raw[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          raw[j] = (ok && j < nv) ? __ldg(reinterpret_cast<const uint4*>(xr + c0) + j) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < nv) {
-            float xv[PV];
-            Seg<TIn>::unpack(raw[j], xv);
-            if (CALIB && rg == 0) {
-#pragma unroll
-              for (int k = 0; k < PV; ++k) {
-                const double v = (double)xv[k];
-                s1 += v;
-                s2 += v * v;
-              }
-            }
-#pragma unroll
-            for (int k = 0; k < PV; ++k) {
-              const float4* vr = reinterpret_cast<const float4*>(vT + (size_t)(c0 + j * PV + k) * Rpad + rg);
-#pragma unroll
-              for (int q = 0; q < RG / 4; ++q) {
-                const float4 v = vr[q];
-                acc[4 * q + 0] = __fmaf_rn(xv[k], v.x, acc[4 * q + 0]);
-                acc[4 * q + 1] = __fmaf_rn(xv[k], v.y, acc[4 * q + 1]);
-                acc[4 * q + 2] = __fmaf_rn(xv[k], v.z, acc[4 * q + 2]);
-                acc[4 * q + 3] = __fmaf_rn(xv[k], v.w, acc[4 * q + 3]);
-              }
-            }
-          }
-        }
-      }
-    } else {
-      for (int c = 0; c < D; ++c) {
-        const float xv = ok ? ldf(xr, c) : 0.0f;
-        if (CALIB && rg == 0) {
-          const double v = (double)xv;
-          s1 += v;
-          s2 += v * v;
-        }
-        const float4* vr = reinterpret_cast<const float4*>(vT + (size_t)c * Rpad + rg);
-#pragma unroll
-        for (int q = 0; q < RG / 4; ++q) {
-          const float4 v = vr[q];
-          acc[4 * q + 0] = __fmaf_rn(xv, v.x, acc[4 * q + 0]);
-          acc[4 * q + 1] = __fmaf_rn(xv, v.y, acc[4 * q + 1]);
-          acc[4 * q + 2] = __fmaf_rn(xv, v.z, acc[4 * q + 2]);
-          acc[4 * q + 3] = __fmaf_rn(xv, v.w, acc[4 * q + 3]);
-        }
-      }
-    }
-    // coefficients r >= rank_h are +0.0 (projection.rs:96)
-#pragma unroll
-    for (int r = 0; r < RG; ++r)
-      if (rg + r >= rank) acc[r] = 0.0f;
-    if (MODE == 0 || MODE == 1) {
-      float* pr = o.P + g * R;
-#pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        const int rr = rg + r;
-        if (rr < R) {  // warp-uniform
-          if (ok) pr[rr] = acc[r];
-          if (MODE == 1) {
-            float mn = INFINITY, mx = -INFINITY;
-            if (ok) mm_update(acc[r], mn, mx);
-            warp_minmax(mn, mx);
-            if ((threadIdx.x & 31) == 0) {
-              atomicMin(&o.kmin[(size_t)h * R + rr], fkey(mn));
-              atomicMax(&o.kmax[(size_t)h * R + rr], fkey(mx));
-            }
-          }
-        }
-      }
-    } else {  // MODE 2: per-token quantization of the whole row (R <= RG)
-      float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < RG; ++r)
-        if (r < R) mm_update(acc[r], mn, mx);
-      const float scale = make_scale(mn, mx, o.levels);
-      if (ok) {
-        o.scales[g] = scale;
-        o.mins[g] = mn;
-        uint8_t* cr = o.codes + g * R;
-#pragma unroll
-        for (int r = 0; r < RG; ++r)
-          if (r < R) cr[r] = (uint8_t)qcode(acc[r], mn, scale, o.levels);
-      }
-    }
-  }
-  if (CALIB) {
-    block_sum2(s1, s2);
-    if (threadIdx.x == 0) {
-      const size_t slot = (size_t)h * gridDim.x + blockIdx.x;
-      o.cpart[2 * slot] = s1;
-      o.cpart[2 * slot + 1] = s2;
-    }
+  for (int q = 0; q < RG / 4; ++q) {
+    const float4 v = vr[q];
+    acc[2 * q] = ffma2(xx, make_float2(v.x, v.y), acc[2 * q]);
+    acc[2 * q + 1] = ffma2(xx, make_float2(v.z, v.w), acc[2 * q + 1]);
   }
 }
 
-template <typename TIn, int RG, bool VEC, bool CALIB, int MODE>
+template <typename TIn, int RG, bool CALIB, int MODE, bool PIPE>
+__global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict__ x, int H, int T, int D,
+                                                        const float* __restrict__ bvt,
+                                                        const uint64_t* __restrict__ ranks, int R, int Rpad,
+                                                        ProjSmem L, ProjectOut o) {
+  extern __shared__ __align__(16) uint8_t smraw[];
+  float* vT = reinterpret_cast<float*>(smraw);  // [D][Rpad]
+  const int Rk = (R + 3) & ~3;
+  int* skmin = reinterpret_cast<int*>(smraw + L.keys);
+  int* skmax = skmin + Rk;
+  uint32_t* shist = reinterpret_cast<uint32_t*>(smraw + L.hist);
+  uint8_t* xbuf = smraw + L.xbuf;
+  const int tid = threadIdx.x;
+  const int nvec = D * (int)sizeof(TIn) / 16;
+  const int tiles = (T + kProjThreads - 1) / kProjThreads;
+  const long long items = (long long)H * tiles;
+  const long long i0 = items * blockIdx.x / gridDim.x;
+  const long long i1 = items * (blockIdx.x + 1) / gridDim.x;
+  const bool staged = (R <= RG);  // single r-group: outputs go through shared memory
+  const bool hist_on = (MODE == 2) && o.hist != nullptr;
+  if (hist_on)
+    for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
+
+  // the block copies the tile's contiguous rows cooperatively (consecutive
+  // threads take consecutive 16-byte chunks, so global reads coalesce); chunk j
+  // of row r lands at position j ^ (r mod nvec) when swizzling
+  const int lg = 31 - __clz(nvec > 0 ? nvec : 1);
+  auto issue = [&](long long it, int stage) {
+    if (PIPE) {
+      const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+      const int nr = min(kProjThreads, T - tile * kProjThreads);
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(x + ((size_t)h * T + (size_t)tile * kProjThreads) * D);
+      uint8_t* dst = xbuf + (size_t)stage * kProjThreads * L.stride;
+      const int total = nr * nvec;
+      for (int i = tid; i < total; i += blockDim.x) {
+        const int r = L.pow2 ? (i >> lg) : (i / nvec);
+        const int j = i - r * nvec;
+        const int pj = L.swz ? (j ^ (r & (nvec - 1))) : j;
+        cp16(dst + (size_t)r * L.stride + 16 * pj, src + 16 * (size_t)i);
+      }
+      cp_commit();
+    }
+  };
+
+  auto flush_keys = [&](int hh) {
+    if (MODE == 1 && hh >= 0)
+      for (int r = tid; r < R; r += blockDim.x) {
+        atomicMin(&o.kmin[(size_t)hh * R + r], skmin[r]);
+        atomicMax(&o.kmax[(size_t)hh * R + r], skmax[r]);
+      }
+  };
+
+  int cur_h = -1, rank = 0;
+  if (PIPE && i0 < i1) issue(i0, 0);
+  for (long long it = i0; it < i1; ++it) {
+    const int stage = (int)((it - i0) & 1);
+    const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+    if (h != cur_h) {  // block-uniform
+      __syncthreads();
+      flush_keys(cur_h);
+      const uint64_t rk = ranks[h];
+      rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
+      const float* B = bvt + (size_t)h * R * D;
+      for (int i = tid; i < D * Rpad; i += blockDim.x) {
+        const int c = i / Rpad, r = i - c * Rpad;
+        vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
+      }
+      if (MODE == 1)
+        for (int r = tid; r < R; r += blockDim.x) {
+          skmin[r] = fkey(INFINITY);
+          skmax[r] = fkey(-INFINITY);
+        }
+      __syncthreads();
+      cur_h = h;
+    }
+    if (PIPE) {
+      if (it + 1 < i1) {
+        issue(it + 1, stage ^ 1);
+        cp_wait<1>();
+      } else {
+        cp_wait<0>();
+      }
+      __syncthreads();  // rows were copied by other threads
+    }
+    const int t = tile * kProjThreads + tid;
+    const bool ok = t < T;
+    const size_t g = (size_t)h * T + (ok ? t : 0);
+    const size_t g0 = (size_t)h * T + (size_t)tile * kProjThreads;
+    const int nrows = min(kProjThreads, T - tile * kProjThreads);
+    const uint8_t* row = xbuf + ((size_t)stage * kProjThreads + tid) * L.stride;
+    const TIn* xr = x + g * D;
+    uint8_t* ostage = (L.ostage >= 0) ? smraw + L.ostage : xbuf + (size_t)stage * kProjThreads * L.stride;
+    double s1 = 0.0, s2 = 0.0;
+    for (int rg = 0; rg < R; rg += RG) {
+      float2 acc2[RG / 2];
+#pragma unroll
+      for (int r = 0; r < RG / 2; ++r) acc2[r] = make_float2(0.0f, 0.0f);
+      if (PIPE) {
+        constexpr int PV = Seg<TIn>::PV;
+        const int sw = L.swz ? (tid & (nvec - 1)) : 0;
+        for (int j = 0; j < nvec; ++j) {
+          float xv[PV];
+          if (ok) {
+            const uint4 u = *reinterpret_cast<const uint4*>(row + 16 * (j ^ sw));
+            Seg<TIn>::unpack(u, xv);
+          } else {
+#pragma unroll
+            for (int k = 0; k < PV; ++k) xv[k] = 0.0f;
+          }
+          if (CALIB && rg == 0) {
+#pragma unroll
+            for (int k = 0; k < PV; ++k) {
+              const double v = (double)xv[k];
+              s1 += v;
+              s2 += v * v;
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < PV; ++k) fma_row<RG>(acc2, xv[k], vT + (size_t)(j * PV + k) * Rpad + rg);
+        }
+      } else {
+        for (int c = 0; c < D; ++c) {
+          const float xv = ok ? ldf(xr, c) : 0.0f;
+          if (CALIB && rg == 0) {
+            const double v = (double)xv;
+            s1 += v;
+            s2 += v * v;
+          }
+          fma_row<RG>(acc2, xv, vT + (size_t)c * Rpad + rg);
+        }
+      }
+      float acc[RG];
+#pragma unroll
+      for (int r = 0; r < RG / 2; ++r) {
+        acc[2 * r] = acc2[r].x;
+        acc[2 * r + 1] = acc2[r].y;
+      }
+#pragma unroll
+      for (int r = 0; r < RG; ++r)
+        if (rg + r >= rank) acc[r] = 0.0f;  // projection.rs:96
+
+      if (MODE == 1) {  // column min/max of this tile into the block's keys
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+          if (rg + r < R) {  // warp-uniform
+            float mn = INFINITY, mx = -INFINITY;
+            if (ok) mm_update(acc[r], mn, mx);
+            warp_minmax(mn, mx);
+            if ((tid & 31) == 0) {
+              atomicMin(&skmin[rg + r], fkey(mn));
+              atomicMax(&skmax[rg + r], fkey(mx));
+            }
+          }
+        }
+      }
+      if (MODE == 0 || MODE == 1) {
+        if (staged) {
+          if (PIPE && L.ostage < 0) __syncthreads();  // every row of this stage has been read
+          float* ps = reinterpret_cast<float*>(ostage);
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+            if (r < R) ps[tid * R + r] = acc[r];
+          __syncthreads();
+          float* dst = o.P + g0 * R;
+          for (int i = tid; i < nrows * R; i += blockDim.x) dst[i] = ps[i];
+          __syncthreads();
+        } else if (ok) {
+          float* pr = o.P + g * R;
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+            if (rg + r < R) pr[rg + r] = acc[r];
+        }
+      } else {  // MODE 2 (R <= RG)
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+          if (r < R) mm_update(acc[r], mn, mx);
+        const float scale = make_scale(mn, mx, o.levels);
+        const float inv = __frcp_rn(scale);
+        if (ok) {
+          o.scales[g] = scale;
+          o.mins[g] = mn;
+        }
+        if (PIPE && L.ostage < 0) __syncthreads();
+        uint8_t* cs = ostage;
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+          if (r < R) cs[tid * R + r] = (uint8_t)qcode_fast(acc[r], mn, scale, inv, o.levels);
+        __syncthreads();
+        const int cnt = nrows * R;
+        if (o.packed) {
+          uint8_t* dp = o.packed + (g0 * R) / 2;
+          for (int b = tid; b < cnt / 2; b += blockDim.x) {
+            const uint32_t byte = (cs[2 * b] & 0xFu) | ((uint32_t)(cs[2 * b + 1] & 0xFu) << 4);
+            dp[b] = (uint8_t)byte;
+            if (hist_on) atomicAdd(&shist[byte], 1u);
+          }
+        } else {
+          uint8_t* dc = o.codes + g0 * R;
+          for (int i = tid; i < cnt; i += blockDim.x) {
+            const uint8_t c = cs[i];
+            dc[i] = c;
+            if (hist_on) atomicAdd(&shist[c], 1u);
+          }
+        }
+        __syncthreads();
+      }
+    }
+    if (CALIB) {
+      block_sum2(s1, s2);
+      if (tid == 0) {
+        const size_t slot = (size_t)h * tiles + tile;
+        o.cpart[2 * slot] = s1;
+        o.cpart[2 * slot + 1] = s2;
+      }
+      __syncthreads();  // block_sum2's shared slots are reused by the next item
+    }
+  }
+  __syncthreads();
+  flush_keys(cur_h);
+  if (hist_on)
+    for (int i = tid; i < 256; i += blockDim.x)
+      if (shist[i]) atomicAdd(&o.hist[i], shist[i]);
+}
+
+struct LaunchCache {
+  int smem = -1;
+  int per_sm = 0;
+};
+
+template <typename TIn, int RG, bool CALIB, int MODE, bool PIPE>
 cudaError_t project_launch(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
                            size_t R, const ProjectOut& o, cudaStream_t st) {
   const int Rpad = (int)(((R + RG - 1) / RG) * RG);
-  const size_t smem = (size_t)D * Rpad * sizeof(float);
-  const dim3 grid((unsigned)((T + kProjThreads - 1) / kProjThreads), (unsigned)H);
-  auto kern = k_project<TIn, RG, VEC, CALIB, MODE>;
-  if (smem > kSmemOptIn) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  const int Rk = (int)((R + 3) & ~size_t(3));
+  ProjSmem L{};
+  int off = (int)(D * Rpad * sizeof(float));
+  L.keys = off;
+  off += 2 * Rk * 4;
+  off = (off + 15) & ~15;
+  L.hist = off;
+  off += 256 * 4;
+  const int row_bytes = (int)(D * sizeof(TIn));
+  const int nvec = row_bytes / 16;
+  L.pow2 = nvec > 0 && (nvec & (nvec - 1)) == 0;
+  L.swz = PIPE && nvec >= 8 && L.pow2;
+  L.stride = PIPE ? (L.swz ? row_bytes : row_bytes + 16) : 0;
+  L.xbuf = off;
+  if (PIPE) off += 2 * kProjThreads * L.stride;
+  const bool staged = R <= (size_t)RG;
+  const int need_stage = staged ? (int)(kProjThreads * R * 4) : 0;
+  if (PIPE && staged && kProjThreads * L.stride >= need_stage) {
+    L.ostage = -1;  // reuse the current row stage
+  } else {
+    L.ostage = off;
+    off += need_stage;
   }
-  kern<<<grid, kProjThreads, smem, st>>>(x, (int)T, (int)D, bvt, ranks, (int)R, Rpad, o);
+  L.total = (off + 15) & ~15;
+  if (L.total > 200 * 1024) {
+    if (PIPE) return project_launch<TIn, RG, CALIB, MODE, false>(x, H, T, D, bvt, ranks, R, o, st);
+    return cudaErrorInvalidValue;
+  }
+  auto kern = k_project<TIn, RG, CALIB, MODE, PIPE>;
+  // per-device launch facts, looked up once per kernel instantiation
+  constexpr int kDevs = 64;
+  static bool attr_set[kDevs] = {};
+  static int sms[kDevs] = {};
+  static LaunchCache cache[kDevs][4];
+  cudaError_t e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) != cudaSuccess)
+      return e;
+    if ((e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  int per_sm = 0;
+  for (auto& c : cache[dev])
+    if (c.smem == L.total) per_sm = c.per_sm;
+  if (per_sm == 0) {
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, L.total)) != cudaSuccess)
+      return e;
+    per_sm = std::max(per_sm, 1);
+    for (auto& c : cache[dev])
+      if (c.smem < 0) {
+        c.smem = L.total;
+        c.per_sm = per_sm;
+        break;
+      }
+  }
+  const int nsm = sms[dev];
+  const size_t items = H * ((T + kProjThreads - 1) / kProjThreads);
+  const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * nsm));
+  kern<<<(unsigned)grid, kProjThreads, L.total, st>>>(x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
   note_launches(1);
   return cudaGetLastError();
 }
 
-template <typename TIn, int RG, bool VEC>
+template <typename TIn, int RG, bool PIPE>
 cudaError_t project_mode(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
                          size_t R, const ProjectOut& o, cudaStream_t st) {
-  const bool calib = o.cpart != nullptr;
-#define KVF_PL(C, M) return project_launch<TIn, RG, VEC, C, M>(x, H, T, D, bvt, ranks, R, o, st)
   if (o.mode == 1) {
-    if (calib) KVF_PL(true, 1);
-    KVF_PL(false, 1);
+    if (o.cpart) return project_launch<TIn, RG, true, 1, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+    return project_launch<TIn, RG, false, 1, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
   }
+  if (o.cpart) return cudaErrorInvalidValue;  // calibration is fused into the key path only
   if (o.mode == 2) {
-    if (calib) KVF_PL(true, 2);
-    KVF_PL(false, 2);
+    if (R > (size_t)RG) return cudaErrorInvalidValue;
+    return project_launch<TIn, RG, false, 2, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
   }
-  if (calib) KVF_PL(true, 0);
-  KVF_PL(false, 0);
-#undef KVF_PL
+  return project_launch<TIn, RG, false, 0, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
 }
 
-template <typename TIn, bool VEC>
-cudaError_t project_vec(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
-                        size_t R, const ProjectOut& o, cudaStream_t st) {
-  if (R <= 4) return project_mode<TIn, 4, VEC>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 8) return project_mode<TIn, 8, VEC>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 16) return project_mode<TIn, 16, VEC>(x, H, T, D, bvt, ranks, R, o, st);
-  if (o.mode == 2 && R > 32) return cudaErrorInvalidValue;
-  return project_mode<TIn, 32, VEC>(x, H, T, D, bvt, ranks, R, o, st);
+template <typename TIn, bool PIPE>
+cudaError_t project_rg(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
+                       size_t R, const ProjectOut& o, cudaStream_t st) {
+  if (R <= 4) return project_mode<TIn, 4, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 8) return project_mode<TIn, 8, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 12) return project_mode<TIn, 12, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 16) return project_mode<TIn, 16, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 24) return project_mode<TIn, 24, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  return project_mode<TIn, 32, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
 }
 
 template <typename TIn>
 cudaError_t project_typed(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
                           size_t R, const ProjectOut& o, cudaStream_t st) {
-  if (D % Seg<TIn>::PV == 0 && aligned(x, 16)) return project_vec<TIn, true>(x, H, T, D, bvt, ranks, R, o, st);
-  return project_vec<TIn, false>(x, H, T, D, bvt, ranks, R, o, st);
+  const bool pipe = (D * sizeof(TIn)) % 16 == 0 && aligned(x, 16) &&
+                    (D * 32 * 4 + 2 * kProjThreads * (D * sizeof(TIn) + 16) + 16 * 1024) <= 200 * 1024;
+  if (pipe) return project_rg<TIn, true>(x, H, T, D, bvt, ranks, R, o, st);
+  return project_rg<TIn, false>(x, H, T, D, bvt, ranks, R, o, st);
 }
 
 // ---- calibration partials without projection ----------------------------------
@@ -320,22 +492,26 @@ __global__ void __launch_bounds__(256) k_calib_partials(const TIn* __restrict__ 
 }
 
 // calibration.rs:56-71: variance per head, clamped at 0, normalised by the max
-// (uniform 0.5 when the max is below 1e-12). One block; thread h sums its
-// head's partials in block order.
-__global__ void k_calib_finalize(const double* __restrict__ cpart, int H, int tiles, double n,
-                                 float* __restrict__ scores) {
+// (uniform 0.5 when the max is below 1e-12). One block; for each head the
+// threads sum a fixed, strided share of the partials and the block combines
+// them in a fixed order, so the result does not depend on scheduling.
+__global__ void __launch_bounds__(256) k_calib_finalize(const double* __restrict__ cpart, int H, int tiles,
+                                                        double n, float* __restrict__ scores) {
   extern __shared__ double var[];
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+  for (int h = 0; h < H; ++h) {
     double s1 = 0.0, s2 = 0.0;
-    for (int k = 0; k < tiles; ++k) {
+    for (int k = threadIdx.x; k < tiles; k += blockDim.x) {
       s1 += cpart[2 * ((size_t)h * tiles + k)];
       s2 += cpart[2 * ((size_t)h * tiles + k) + 1];
     }
-    const double mean = s1 / n;
-    const double v = (s2 / n) - (mean * mean);
-    var[h] = (isnan(v) || v < 0.0) ? 0.0 : v;  // variance.max(0.0)
+    block_sum2(s1, s2);
+    if (threadIdx.x == 0) {
+      const double mean = s1 / n;
+      const double v = (s2 / n) - (mean * mean);
+      var[h] = (isnan(v) || v < 0.0) ? 0.0 : v;  // variance.max(0.0)
+    }
+    __syncthreads();
   }
-  __syncthreads();
   __shared__ double maxv;
   if (threadIdx.x == 0) {
     double m = 0.0;

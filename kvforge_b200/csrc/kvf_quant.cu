@@ -19,6 +19,7 @@ namespace kvf {
 namespace {
 
 constexpr int kSMs = 148;
+constexpr int kQpTable = 2048;  // (head, r) parameters kept in shared memory
 
 __device__ __forceinline__ float ldf(const float* p, size_t i) { return __ldg(p + i); }
 __device__ __forceinline__ float ldf(const __half* p, size_t i) { return __half2float(__ldg(p + i)); }
@@ -66,6 +67,7 @@ __global__ void __launch_bounds__(256) k_quant_token_v4(const TIn* __restrict__ 
     }
     warp_minmax(mn, mx);
     const float scale = make_scale(mn, mx, levels);
+    const float inv = __frcp_rn(scale);
     if (lane == 0) {
       scales[g] = scale;
       mins[g] = mn;
@@ -74,9 +76,10 @@ __global__ void __launch_bounds__(256) k_quant_token_v4(const TIn* __restrict__ 
     for (int k = 0; k < NV; ++k) {
       const int q = lane + 32 * k;
       if (q < nq) {
-        const uint32_t c = qcode(v[k].x, mn, scale, levels) | (qcode(v[k].y, mn, scale, levels) << 8) |
-                           (qcode(v[k].z, mn, scale, levels) << 16) |
-                           (qcode(v[k].w, mn, scale, levels) << 24);
+        const uint32_t c = qcode_fast(v[k].x, mn, scale, inv, levels) |
+                           (qcode_fast(v[k].y, mn, scale, inv, levels) << 8) |
+                           (qcode_fast(v[k].z, mn, scale, inv, levels) << 16) |
+                           (qcode_fast(v[k].w, mn, scale, inv, levels) << 24);
         *reinterpret_cast<uint32_t*>(codes + base + 4 * (size_t)q) = c;
       }
     }
@@ -97,11 +100,12 @@ __global__ void __launch_bounds__(256) k_quant_token_scalar(const TIn* __restric
     for (int c = lane; c < D; c += 32) mm_update(ldf(x, base + c), mn, mx);
     warp_minmax(mn, mx);
     const float scale = make_scale(mn, mx, levels);
+    const float inv = __frcp_rn(scale);
     if (lane == 0) {
       scales[g] = scale;
       mins[g] = mn;
     }
-    for (int c = lane; c < D; c += 32) codes[base + c] = (uint8_t)qcode(ldf(x, base + c), mn, scale, levels);
+    for (int c = lane; c < D; c += 32) codes[base + c] = (uint8_t)qcode_fast(ldf(x, base + c), mn, scale, inv, levels);
   }
 }
 
@@ -150,11 +154,13 @@ __global__ void __launch_bounds__(256) k_colminmax(const TIn* __restrict__ x, si
 
 __global__ void k_params_from_keys(const int* __restrict__ kmin, const int* __restrict__ kmax,
                                    size_t np, float levels, float* __restrict__ scales,
-                                   float* __restrict__ mins) {
+                                   float* __restrict__ mins, float* __restrict__ inv) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < np; i += (size_t)gridDim.x * blockDim.x) {
     const float mn = kfloat(kmin[i]), mx = kfloat(kmax[i]);
-    scales[i] = make_scale(mn, mx, levels);
+    const float sc = make_scale(mn, mx, levels);
+    scales[i] = sc;
     mins[i] = mn;
+    inv[i] = __frcp_rn(sc);
   }
 }
 
@@ -163,6 +169,7 @@ __global__ void __launch_bounds__(256) k_quant_channel(const TIn* __restrict__ x
                                                        int D, float levels,
                                                        const float* __restrict__ scales,
                                                        const float* __restrict__ mins,
+                                                       const float* __restrict__ invs,
                                                        uint8_t* __restrict__ codes) {
   const int lane = threadIdx.x & 31;
   const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -174,13 +181,16 @@ __global__ void __launch_bounds__(256) k_quant_channel(const TIn* __restrict__ x
         const float4 v = ld4(x, base + 4 * (size_t)q);
         const float4 s = __ldg(reinterpret_cast<const float4*>(scales + pb) + q);
         const float4 m = __ldg(reinterpret_cast<const float4*>(mins + pb) + q);
-        const uint32_t c = qcode(v.x, m.x, s.x, levels) | (qcode(v.y, m.y, s.y, levels) << 8) |
-                           (qcode(v.z, m.z, s.z, levels) << 16) | (qcode(v.w, m.w, s.w, levels) << 24);
+        const float4 iv = __ldg(reinterpret_cast<const float4*>(invs + pb) + q);
+        const uint32_t c = qcode_fast(v.x, m.x, s.x, iv.x, levels) | (qcode_fast(v.y, m.y, s.y, iv.y, levels) << 8) |
+                           (qcode_fast(v.z, m.z, s.z, iv.z, levels) << 16) |
+                           (qcode_fast(v.w, m.w, s.w, iv.w, levels) << 24);
         *reinterpret_cast<uint32_t*>(codes + base + 4 * (size_t)q) = c;
       }
     } else {
       for (int c = lane; c < D; c += 32)
-        codes[base + c] = (uint8_t)qcode(ldf(x, base + c), __ldg(mins + pb + c), __ldg(scales + pb + c), levels);
+        codes[base + c] = (uint8_t)qcode_fast(ldf(x, base + c), __ldg(mins + pb + c), __ldg(scales + pb + c),
+                                              __ldg(invs + pb + c), levels);
     }
   }
 }
@@ -348,12 +358,36 @@ __global__ void __launch_bounds__(256) k_quantpack_channel(const float* __restri
     scales[i] = make_scale(mn, mx, levels);
     mins[i] = mn;
   }
+  // (scale, min, 1/scale) per (head, r) in shared memory when they fit
+  __shared__ float ps[kQpTable], pm[kQpTable], pi[kQpTable];
+  const bool table = np <= (uint64_t)kQpTable;
+  if (table) {
+    for (uint64_t i = threadIdx.x; i < np; i += blockDim.x) {
+      const float mn = kfloat(kmin[i]), mx = kfloat(kmax[i]);
+      const float sc = make_scale(mn, mx, levels);
+      ps[i] = sc;
+      pm[i] = mn;
+      pi[i] = __frcp_rn(sc);
+    }
+    __syncthreads();
+  }
+  const bool small = n < (1ull << 32);
   auto code = [&](uint64_t i) -> uint32_t {
-    const uint64_t g = i / R;
-    const uint64_t c = i - g * R;
-    const uint64_t p = (g / T) * R + c;
+    uint64_t g, c, p;
+    if (small) {
+      const uint32_t i32 = (uint32_t)i, g32 = i32 / (uint32_t)R;
+      g = g32;
+      c = i32 - g32 * (uint32_t)R;
+      p = (uint64_t)(g32 / (uint32_t)T) * R + c;
+    } else {
+      g = i / R;
+      c = i - g * R;
+      p = (g / T) * R + c;
+    }
+    if (table) return qcode_fast(__ldg(P + i), pm[p], ps[p], pi[p], levels);
     const float mn = kfloat(__ldg(kmin + p)), mx = kfloat(__ldg(kmax + p));
-    return qcode(__ldg(P + i), mn, make_scale(mn, mx, levels), levels);
+    const float sc = make_scale(mn, mx, levels);
+    return qcode_fast(__ldg(P + i), mn, sc, __frcp_rn(sc), levels);
   };
   const uint64_t nb = INT4 ? (n + 1) / 2 : n;
   for (uint64_t b = tid; b < nb; b += stride) {
@@ -415,14 +449,15 @@ cudaError_t quantize_typed(const TIn* x, size_t H, size_t T, size_t D, int dt, i
     }
     k_colminmax<TIn><<<grid, 256, smem, st>>>(x, T, Di, tpb, kmin, kmax);
   }
-  k_params_from_keys<<<ig, 256, 0, st>>>(kmin, kmax, np, levels, scales, mins);
+  float* invs = reinterpret_cast<float*>(keys + 2 * np);
+  k_params_from_keys<<<ig, 256, 0, st>>>(kmin, kmax, np, levels, scales, mins, invs);
   note_launches(2 + (T > 0 ? 1 : 0) + (rows > 0 ? 1 : 0));
   if (rows > 0) {
     const unsigned grid = grid_warps(rows, 8);
-    if (D % 4 == 0 && xal && aligned(scales, 16) && aligned(mins, 16))
-      k_quant_channel<TIn, true><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, codes);
+    if (D % 4 == 0 && xal && aligned(scales, 16) && aligned(mins, 16) && aligned(invs, 16))
+      k_quant_channel<TIn, true><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, invs, codes);
     else
-      k_quant_channel<TIn, false><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, codes);
+      k_quant_channel<TIn, false><<<grid, 256, 0, st>>>(x, rows, T, Di, levels, scales, mins, invs, codes);
   }
   return cudaGetLastError();
 }

@@ -22,7 +22,8 @@
 //
 // Model: counts -> q[s] = max(1, floor(count * 2^15 / N)) for seen symbols,
 // 0 for unseen; the deficit goes to the most frequent symbol, an excess is
-// removed from the largest entries. Integer only, identical on both sides.
+// removed from the largest entries. Integer only, identical on both sides;
+// every encode and decode block builds it from the 256 counts it is given.
 //
 // Every read of the decoder is bounds-checked against the container; a
 // malformed container sets a status bit instead of faulting, and there are no
@@ -36,7 +37,6 @@ namespace {
 
 constexpr int kWarpsPerBlock = 4;  // encoder: chunks per block
 constexpr int kDecWarps = 2;       // decoder: chunks per block
-constexpr uint32_t kDecWcap = kRansChunk + 2;  // renormalisation words staged per decoding warp
 
 // cp.async helpers: asynchronous global -> shared copies, many in flight per thread
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
@@ -79,93 +79,91 @@ __device__ __forceinline__ T block_exclusive_scan(T v, T* warp_tot, T* total) {
   return warp_tot[w] + incl - v;
 }
 
-__global__ void __launch_bounds__(256) k_rans_normalize(const uint32_t* __restrict__ freq,
-                                                        RansTables* __restrict__ tab,
-                                                        unsigned* __restrict__ status) {
-  __shared__ unsigned long long sN;
-  __shared__ uint32_t q[256], cum[256];
-  __shared__ uint32_t sS, wtot[8], total;
-  __shared__ unsigned long long wbest[8];
-  __shared__ int bad, argmax;
-  const int s = threadIdx.x, lane = s & 31, w = s >> 5;
-  const uint32_t f = freq[s];
-  if (s == 0) { sN = 0ull; sS = 0u; bad = 0; }
-  __syncthreads();
-  atomicAdd(&sN, (unsigned long long)f);
-  __syncthreads();
-  const unsigned long long N = sN;
-  if (N == 0ull) {
-    if (s == 0) atomicOr(status, kDevErrEntropy);
-    return;
+// The model (q, cum) built by a whole block from the 256 counts, identical to
+// the CPU mirror's: q = max(1, floor(count * 2^15 / N)) for
+// seen symbols; the deficit goes to the most frequent symbol (lowest index on
+// ties); an excess is removed from the largest entries. Returns false (on
+// every thread) when the counts admit no model.
+struct ModelSmem {
+  unsigned long long N, best;
+  uint32_t S;
+  int bad;
+};
+
+__device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint32_t* cum, ModelSmem& ms) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  if (tid == 0) {
+    ms.N = 0ull;
+    ms.best = 0ull;
+    ms.S = 0u;
+    ms.bad = 0;
   }
-  uint32_t qs = 0;
-  if (f) {
-    const unsigned long long v = ((unsigned long long)f * kRansM) / N;
-    qs = (uint32_t)(v < 1ull ? 1ull : v);
-  }
-  q[s] = qs;
-  atomicAdd(&sS, qs);
-  // most frequent symbol, lowest index on ties
-  unsigned long long key = ((unsigned long long)f << 8) | (unsigned long long)(255 - s);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long u = __shfl_xor_sync(0xffffffffu, key, o);
-    key = u > key ? u : key;
-  }
-  if (lane == 0) wbest[w] = key;
   __syncthreads();
-  if (s == 0) {
-    unsigned long long b = wbest[0];
-    for (int k = 1; k < 8; ++k) b = wbest[k] > b ? wbest[k] : b;
-    argmax = 255 - (int)(b & 0xFF);
-    unsigned long long S = sS;
+  unsigned long long n = 0ull, key = 0ull;
+  for (int s = tid; s < 256; s += nt) {
+    const uint32_t f = freq[s];
+    q[s] = f;  // counts for now
+    n += f;
+    const unsigned long long k = ((unsigned long long)f << 8) | (unsigned long long)(255 - s);
+    key = k > key ? k : key;
+  }
+  atomicAdd(&ms.N, n);
+  atomicMax(&ms.best, key);
+  __syncthreads();
+  const unsigned long long N = ms.N;
+  if (N == 0ull) return false;
+  uint32_t ssum = 0;
+  for (int s = tid; s < 256; s += nt) {
+    const uint32_t f = q[s];
+    uint32_t qs = 0;
+    if (f) {
+      const unsigned long long v = ((unsigned long long)f * kRansM) / N;
+      qs = (uint32_t)(v < 1ull ? 1ull : v);
+    }
+    q[s] = qs;
+    ssum += qs;
+  }
+  atomicAdd(&ms.S, ssum);
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long S = ms.S;
+    const int argmax = 255 - (int)(ms.best & 0xFF);
     if (S < kRansM) {
       q[argmax] += (uint32_t)(kRansM - S);
     } else {
       while (S > kRansM) {  // rare: many symbols lifted to 1
-        int best = -1;
+        int b = -1;
         for (int k = 0; k < 256; ++k)
-          if (q[k] > 1 && (best < 0 || q[k] > q[best])) best = k;
-        if (best < 0) { bad = 1; break; }
+          if (q[k] > 1 && (b < 0 || q[k] > q[b])) b = k;
+        if (b < 0) { ms.bad = 1; break; }
         unsigned long long d = S - kRansM;
-        if (d > q[best] - 1) d = q[best] - 1;
-        q[best] -= (uint32_t)d;
+        if (d > q[b] - 1) d = q[b] - 1;
+        q[b] -= (uint32_t)d;
         S -= d;
       }
     }
   }
   __syncthreads();
-  if (bad) {
-    if (s == 0) atomicOr(status, kDevErrEntropy);
-    return;
-  }
-  const uint32_t qf = q[s];
-  cum[s] = block_exclusive_scan<uint32_t>(qf, wtot, &total);
-  __syncthreads();
-  tab->q[s] = qf;
-  tab->cum[s] = cum[s];
-  tab->rcp[s] = qf ? 0xFFFFFFFFu / qf : 0u;
-  // slot -> symbol: thread s fills slots [128 s, 128 s + 128), starting from the
-  // last symbol whose cum <= 128 s and walking forward (unseen symbols share the
-  // cum of the next seen one and are skipped by the walk)
-  const uint32_t k0 = (uint32_t)s * (kRansM / 256);
-  int lo = 0, hi = 255;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (cum[mid] <= k0) lo = mid; else hi = mid - 1;
-  }
-  int sym = lo;
-  uint32_t* dst = reinterpret_cast<uint32_t*>(tab->slot2sym + k0);
-  for (uint32_t j = 0; j < kRansM / 256; j += 4) {
-    uint32_t word = 0;
+  if (ms.bad) return false;
+  if (tid < 32) {  // exclusive prefix over 256 entries: 8 per lane
+    uint32_t loc[8], sum = 0;
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const uint32_t k = k0 + j + b;
-      while (cum[sym] + q[sym] <= k) ++sym;
-      word |= (uint32_t)sym << (8 * b);
+    for (int k = 0; k < 8; ++k) {
+      loc[k] = sum;
+      sum += q[8 * tid + k];
     }
-    dst[j / 4] = word;
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (tid >= o) incl += u;
+    }
+    const uint32_t base = incl - sum;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cum[8 * tid + k] = base + loc[k];
   }
+  __syncthreads();
+  return true;
 }
 
 // One warp per chunk. The chunk's symbols are staged in shared memory with
@@ -173,16 +171,13 @@ __global__ void __launch_bounds__(256) k_rans_normalize(const uint32_t* __restri
 // symbol and model entries are loaded while the current state is updated.
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8_t* __restrict__ data,
                                                                    uint64_t n, uint32_t chunk,
-                                                                   const RansTables* __restrict__ tab,
+                                                                   const uint32_t* __restrict__ freq,
                                                                    uint8_t* __restrict__ slots,
-                                                                   uint64_t nchunks) {
+                                                                   uint64_t nchunks,
+                                                                   unsigned* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t sbuf[];  // [warps][chunk]
   __shared__ uint32_t q[256], cum[256], rcp[256];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    q[i] = tab->q[i];
-    cum[i] = tab->cum[i];
-    rcp[i] = tab->rcp[i];
-  }
+  __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w;
   const bool live = c < nchunks;
@@ -195,8 +190,15 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
     for (uint32_t j = lane; j < n16; j += 32) cp_async16(buf + 16 * j, data + start + 16 * j);
     for (uint32_t j = 16 * n16 + lane; j < nsym; j += 32) buf[j] = data[start + j];
   }
+  // the model is built while the symbols are in flight
+  const bool model_ok = build_model(freq, q, cum, ms);
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) rcp[i] = q[i] ? 0xFFFFFFFFu / q[i] : 0u;
   cp_async_wait_all();
   __syncthreads();
+  if (!model_ok) {
+    if (threadIdx.x == 0) atomicOr(status, kDevErrEntropy);
+    return;
+  }
   if (!live) return;
 
   uint8_t* slot = slots + c * rans_slot_bytes(chunk);
@@ -281,7 +283,7 @@ __global__ void __launch_bounds__(1024) k_rans_offsets(const uint8_t* __restrict
 }
 
 // one block per chunk: copy nwords, states and words into place
-__global__ void __launch_bounds__(128) k_rans_compact(const uint8_t* __restrict__ slots, uint32_t chunk,
+__global__ void __launch_bounds__(256) k_rans_compact(const uint8_t* __restrict__ slots, uint32_t chunk,
                                                       uint8_t* __restrict__ out) {
   const uint64_t c = blockIdx.x;
   const uint8_t* slot = slots + c * rans_slot_bytes(chunk);
@@ -293,7 +295,20 @@ __global__ void __launch_bounds__(128) k_rans_compact(const uint8_t* __restrict_
   for (int i = threadIdx.x; i < 1 + (int)kRansLanes; i += blockDim.x) dhdr[i] = shdr[i];
   const uint16_t* sw = reinterpret_cast<const uint16_t*>(slot + kRansChunkHeader) + (chunk + 2 - nw);
   uint16_t* dw = reinterpret_cast<uint16_t*>(dst + kRansChunkHeader);
-  for (uint32_t i = threadIdx.x; i < nw; i += blockDim.x) dw[i] = sw[i];
+  // eight independent loads in flight per thread
+  for (uint32_t i0 = threadIdx.x; i0 < nw; i0 += blockDim.x * 8) {
+    uint16_t v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t i = i0 + k * blockDim.x;
+      v[k] = (i < nw) ? sw[i] : (uint16_t)0;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t i = i0 + k * blockDim.x;
+      if (i < nw) dw[i] = v[k];
+    }
+  }
   if ((nw & 1u) && threadIdx.x == 0) dw[nw] = 0;
 }
 
@@ -301,26 +316,56 @@ __device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
   return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// One warp per chunk. The slot table and model sit in shared memory; the
-// chunk's renormalisation words are copied into shared memory with
-// asynchronous 4-byte copies before decoding starts (chunks whose word count
-// exceeds the staging buffer are read from global memory instead).
+// One warp per chunk. Each block builds the model from the 256 counts and
+// two per-slot tables in shared memory: ent[slot] = q | (slot - cum) << 16
+// (the only lookup on the state's critical path) and sym[slot] (for the
+// output byte). The chunk's renormalisation words are staged in shared memory
+// with asynchronous 4-byte copies (chunks with more words than the staging
+// buffer read them from global memory instead).
+constexpr uint32_t kDecStage = 12288;  // words staged per decoding warp
+
 __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
                                                               uint64_t comp_len_host,
                                                               const uint64_t* __restrict__ comp_len_dev,
-                                                              const RansTables* __restrict__ tab,
+                                                              const uint32_t* __restrict__ freq,
                                                               uint64_t n, uint8_t* __restrict__ out,
                                                               unsigned* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t dsm[];
-  uint8_t* sym = dsm;                                               // [2^15]
-  uint32_t* qc = reinterpret_cast<uint32_t*>(dsm + kRansM);         // [256] q | cum << 16
-  uint16_t* wstage = reinterpret_cast<uint16_t*>(dsm + kRansM + 1024);  // [kDecWarps][kDecWcap]
-  for (int i = threadIdx.x; i < (int)(kRansM / 16); i += blockDim.x)
-    cp_async16(sym + 16 * i, tab->slot2sym + 16 * i);
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) qc[i] = tab->q[i] | (tab->cum[i] << 16);
-  cp_async_wait_all();
-  __syncthreads();
+  uint32_t* ent = reinterpret_cast<uint32_t*>(dsm);                     // [2^15]
+  uint8_t* sym = dsm + 4 * kRansM;                                      // [2^15]
+  uint16_t* wstage = reinterpret_cast<uint16_t*>(dsm + 5 * kRansM);    // [kDecWarps][kDecStage]
+  __shared__ uint32_t q[256], cum[256];
+  __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (!build_model(freq, q, cum, ms)) {
+    if (threadIdx.x == 0) atomicOr(status, kDevErrEntropy);
+    return;
+  }
+  {  // per-slot tables: each thread fills a contiguous slot range, walking symbols
+    const uint32_t per = kRansM / blockDim.x;
+    const uint32_t k0 = threadIdx.x * per;
+    int lo = 0, hi = 255;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cum[mid] <= k0) lo = mid; else hi = mid - 1;
+    }
+    int s = lo;
+    for (uint32_t k = k0; k < k0 + per; k += 4) {
+      uint32_t sw = 0;
+      uint4 e4;
+      uint32_t* e = &e4.x;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t kk = k + b;
+        while (cum[s] + q[s] <= kk) ++s;
+        e[b] = q[s] | ((kk - cum[s]) << 16);
+        sw |= (uint32_t)s << (8 * b);
+      }
+      *reinterpret_cast<uint4*>(ent + k) = e4;
+      *reinterpret_cast<uint32_t*>(sym + k) = sw;
+    }
+  }
+  __syncthreads();
   const uint64_t comp_len = comp_len_dev ? *comp_len_dev : comp_len_host;
   // header checks (every warp reads the same 32 bytes)
   if (comp_len < kRansHeader) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
@@ -333,7 +378,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
                       nchunks == (n + chunk - 1) / chunk && rd32(comp + 28) == hdr && hdr <= comp_len &&
                       rd32(comp + kRansHeader + 4 * nchunks) == comp_len;
   if (!hdr_ok) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
-  uint16_t* stage = wstage + (size_t)w * kDecWcap;
+  uint16_t* stage = wstage + (size_t)w * kDecStage;
   const uint64_t nwarps = (uint64_t)gridDim.x * kDecWarps;
   for (uint64_t c = (uint64_t)blockIdx.x * kDecWarps + w; c < nchunks; c += nwarps) {
     const uint64_t off = rd32(comp + kRansHeader + 4 * c);
@@ -349,9 +394,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
     }
     uint32_t x = rd32(comp + off + 4 + 4 * lane);
     bool bad = x < kRansL;
-    const uint16_t* gwords = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
-    const uint16_t* words = gwords;
-    if (nw <= kDecWcap) {  // stage pairs of words (the payload is padded to 4 bytes)
+    const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
+    if (nw <= kDecStage) {  // stage pairs of words (the payload is padded to 4 bytes)
       const uint32_t npair = (nw + 1) / 2;
       const uint8_t* src = comp + off + kRansChunkHeader;
       for (uint32_t j = lane; j < npair; j += 32) cp_async4(stage + 2 * j, src + 4 * j);
@@ -362,23 +406,25 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
     const uint64_t start = c * chunk;
     const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
     const uint32_t steps = (nsym + 31) / 32;
+    uint8_t* o = out + start;
+    const uint32_t lt = (1u << lane) - 1u;
     uint32_t p = 0;
     for (uint32_t st = 0; st < steps; ++st) {
       const uint32_t i = st * 32 + lane;
       const bool active = i < nsym;
+      const uint32_t slot = x & (kRansM - 1);
+      const uint32_t e = ent[slot];
       if (active) {
-        const uint32_t slot = x & (kRansM - 1);
-        const uint32_t s = sym[slot];
-        const uint32_t e = qc[s];
-        x = (e & 0xFFFFu) * (x >> kRansProbBits) + slot - (e >> 16);
-        out[start + i] = (uint8_t)s;
+        x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+        o[i] = sym[slot];
       }
       const bool need = active && x < kRansL;
       const unsigned mask = __ballot_sync(0xffffffffu, need);
+      const uint32_t idx = p + __popc(mask & lt);
+      const uint32_t wv = words[idx < nw ? idx : (nw ? nw - 1 : 0)];
       if (need) {
-        const uint32_t idx = p + __popc(mask & ((1u << lane) - 1u));
-        if (idx < nw) x = (x << 16) | words[idx];
-        else { bad = true; x = kRansL; }
+        if (idx >= nw) bad = true;
+        x = (x << 16) | wv;
       }
       p += __popc(mask);
     }
@@ -390,15 +436,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
 
 }  // namespace
 
-cudaError_t launch_rans_normalize(const uint32_t* freq, RansTables* tab, unsigned* status,
-                                  cudaStream_t st) {
-  k_rans_normalize<<<1, 256, 0, st>>>(freq, tab, status);
-  note_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const RansTables* tab,
-                               uint8_t* slots, cudaStream_t st) {
+cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
+                               uint8_t* slots, unsigned* status, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   const size_t nc = rans_num_chunks(n, chunk);
   const size_t smem = (size_t)kWarpsPerBlock * chunk;
@@ -407,7 +446,7 @@ cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, co
     if (e != cudaSuccess) return e;
   }
   const unsigned grid = (unsigned)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  k_rans_encode<<<grid, kWarpsPerBlock * 32, smem, st>>>(data, n, chunk, tab, slots, nc);
+  k_rans_encode<<<grid, kWarpsPerBlock * 32, smem, st>>>(data, n, chunk, freq, slots, nc, status);
   note_launches(1);
   return cudaGetLastError();
 }
@@ -417,23 +456,23 @@ cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk,
   if (n == 0) return cudaSuccess;
   const size_t nc = rans_num_chunks(n, chunk);
   k_rans_offsets<<<1, 1024, 0, st>>>(slots, n, chunk, nc, out, out_len);
-  k_rans_compact<<<(unsigned)nc, 128, 0, st>>>(slots, chunk, out);
+  k_rans_compact<<<(unsigned)nc, 256, 0, st>>>(slots, chunk, out);
   note_launches(2);
   return cudaGetLastError();
 }
 
 cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
-                               const RansTables* tab, size_t n, uint8_t* out, unsigned* status,
+                               const uint32_t* freq, size_t n, uint8_t* out, unsigned* status,
                                cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   // the grid is sized for the encoder's default chunk size; warps loop over
   // chunks, so a container with any chunk size named in its header decodes
   const size_t nc = rans_num_chunks(n, kRansChunk);
   const unsigned grid = (unsigned)((nc + kDecWarps - 1) / kDecWarps);
-  const size_t smem = kRansM + 1024 + (size_t)kDecWarps * kDecWcap * 2;
+  const size_t smem = 5 * (size_t)kRansM + (size_t)kDecWarps * kDecStage * 2;
   const cudaError_t e = cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k_rans_decode<<<grid, kDecWarps * 32, smem, st>>>(comp, comp_len, comp_len_dev, tab, n, out, status);
+  k_rans_decode<<<grid, kDecWarps * 32, smem, st>>>(comp, comp_len, comp_len_dev, freq, n, out, status);
   note_launches(1);
   return cudaGetLastError();
 }

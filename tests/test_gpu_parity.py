@@ -87,6 +87,33 @@ def test_quantize_golden(kvf, golden):
         assert np.array_equal(bits(host(d)), bits(golden[key + "_deq"])), key
 
 
+@pytest.mark.parametrize("dt", [INT4, INT8])
+def test_quantize_half_integer_quotients(kvf, oracle, dt):
+    """Values whose (v - min) / scale falls within a few ulps of k + 0.5: the
+    GPU divides by multiplying with the reciprocal and must fall back to the
+    exact IEEE quotient exactly where rounding could differ."""
+    rng = np.random.default_rng(99)
+    levels = 15 if dt == INT4 else 255
+    H, T, D = 4, 512, 64
+    x = np.zeros((H, T, D), np.float32)
+    for h in range(H):
+        for t in range(T):
+            M = np.float32(rng.uniform(0.01, 100.0))
+            s = np.float32(M / np.float32(levels))
+            k = rng.integers(0, levels, D - 2)
+            base = ((k + 0.5) * s.astype(np.float64)).astype(np.float32)
+            ulp = rng.integers(-3, 4, D - 2).astype(np.int32)
+            vals = (base.view(np.int32) + ulp).view(np.float32)
+            x[h, t, 0], x[h, t, 1] = 0.0, M
+            x[h, t, 2:] = np.clip(vals, 0, M)
+    q = kvf.GpuQuantizer()
+    for ax in (PC, PT):
+        packed, params = q.quantize(dev(x), dt, ax)
+        p, s_, m = oracle.quantize(x, dt, ax)
+        assert np.array_equal(host(packed), p)
+        assert np.array_equal(bits(host(params.scales)), bits(s_))
+
+
 def test_quantize_errors(kvf):
     q = kvf.GpuQuantizer()
     x = dev(np.zeros((2, 4, 4), np.float32))
