@@ -207,34 +207,43 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
   uint32_t pos = capw;  // words are written backwards, ending at capw
   uint32_t x = kRansL;
   const uint32_t steps = (nsym + 31) / 32;
-  // preload the last step (the only one that may be partial)
-  uint32_t i = (steps - 1) * 32 + lane;
-  bool act = i < nsym;
-  uint32_t s = act ? buf[i] : 0u;
-  uint32_t f = q[s], cu = cum[s], rc = rcp[s];
-  for (uint32_t st = steps; st-- > 0;) {
-    const bool a0 = act;
-    const uint32_t f0 = f, c0 = cu, r0 = rc;
-    if (st > 0) {  // next step (st - 1) is always full
-      s = buf[(st - 1) * 32 + lane];
-      act = true;
-      f = q[s];
-      cu = cum[s];
-      rc = rcp[s];
-    }
-    const bool need = a0 && ((uint64_t)x >= ((uint64_t)f0 << 17));
+  const unsigned above_mask = ~((2u << lane) - 1u);  // emitting lanes above this one
+  // one encoding step for a lane holding symbol entry (f, cu, rc); `act`
+  // false leaves the state alone (only the last step can be partial)
+  auto step = [&](bool act, uint32_t f, uint32_t cu, uint32_t rc) {
+    const bool need = act && (x >> 17) >= f;  // x >= f * 2^17
     const unsigned mask = __ballot_sync(0xffffffffu, need);
-    if (need) {
-      const unsigned above = mask & ~((2u << lane) - 1u);  // emitting lanes above this one
-      words[pos - 1 - __popc(above)] = (uint16_t)(x & 0xFFFFu);
-      x >>= 16;
-    }
+    if (need) words[pos - 1 - __popc(mask & above_mask)] = (uint16_t)(x & 0xFFFFu);
     pos -= __popc(mask);
-    if (a0) {
-      uint32_t qq = __umulhi(x, r0);
-      uint32_t r = x - qq * f0;
-      if (r >= f0) { ++qq; r -= f0; }
-      x = (qq << kRansProbBits) + r + c0;
+    const uint32_t xs = need ? (x >> 16) : x;
+    uint32_t qq = __umulhi(xs, rc);
+    uint32_t r = xs - qq * f;
+    const bool fix = r >= f;
+    qq += fix ? 1u : 0u;
+    r -= fix ? f : 0u;
+    x = act ? (qq << kRansProbBits) + r + cu : x;
+  };
+  // last (possibly partial) step
+  {
+    const uint32_t i = (steps - 1) * 32 + lane;
+    const bool act = i < nsym;
+    const uint32_t s = act ? buf[i] : 0u;
+    step(act, q[s], cum[s], rcp[s]);
+  }
+  // full steps, software-pipelined: the next step's model entries load while
+  // the current state updates
+  if (steps >= 2) {
+    uint32_t s = buf[(steps - 2) * 32 + lane];
+    uint32_t f = q[s], cu = cum[s], rc = rcp[s];
+    for (uint32_t st = steps - 1; st-- > 0;) {
+      const uint32_t f0 = f, c0 = cu, r0 = rc;
+      if (st > 0) {
+        s = buf[(st - 1) * 32 + lane];
+        f = q[s];
+        cu = cum[s];
+        rc = rcp[s];
+      }
+      step(true, f0, c0, r0);
     }
   }
   uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
@@ -322,7 +331,7 @@ __device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
 // output byte). The chunk's renormalisation words are staged in shared memory
 // with asynchronous 4-byte copies (chunks with more words than the staging
 // buffer read them from global memory instead).
-constexpr uint32_t kDecStage = 12288;  // words staged per decoding warp
+constexpr uint32_t kDecStage = 16384;  // words staged per decoding warp (a power of two)
 
 __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
                                                               uint64_t comp_len_host,
@@ -394,39 +403,67 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
     }
     uint32_t x = rd32(comp + off + 4 + 4 * lane);
     bool bad = x < kRansL;
-    const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
-    if (nw <= kDecStage) {  // stage pairs of words (the payload is padded to 4 bytes)
+    const uint64_t start = c * chunk;
+    const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
+    const uint32_t full = nsym / 32;  // steps with every lane active
+    uint8_t* o = out + start + lane;
+    const uint32_t lt = (1u << lane) - 1u;
+    uint32_t p = 0;
+    if (nw <= kDecStage) {
+      // stage pairs of words (the payload is padded to 4 bytes); indices are
+      // masked into the staging buffer, so even a corrupt stream reads inside
+      // it, and the end-of-chunk checks reject it
       const uint32_t npair = (nw + 1) / 2;
       const uint8_t* src = comp + off + kRansChunkHeader;
       for (uint32_t j = lane; j < npair; j += 32) cp_async4(stage + 2 * j, src + 4 * j);
       cp_async_wait_all();
       __syncwarp();
-      words = stage;
-    }
-    const uint64_t start = c * chunk;
-    const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
-    const uint32_t steps = (nsym + 31) / 32;
-    uint8_t* o = out + start;
-    const uint32_t lt = (1u << lane) - 1u;
-    uint32_t p = 0;
-    for (uint32_t st = 0; st < steps; ++st) {
-      const uint32_t i = st * 32 + lane;
-      const bool active = i < nsym;
-      const uint32_t slot = x & (kRansM - 1);
-      const uint32_t e = ent[slot];
-      if (active) {
+      for (uint32_t st = 0; st < full; ++st) {
+        const uint32_t slot = x & (kRansM - 1);
+        const uint32_t e = ent[slot];
         x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
-        o[i] = sym[slot];
+        o[32 * st] = sym[slot];
+        const bool need = x < kRansL;
+        const unsigned mask = __ballot_sync(0xffffffffu, need);
+        const uint32_t w16 = stage[(p + __popc(mask & lt)) & (kDecStage - 1)];
+        x = need ? ((x << 16) | w16) : x;
+        p += __popc(mask);
       }
-      const bool need = active && x < kRansL;
-      const unsigned mask = __ballot_sync(0xffffffffu, need);
-      const uint32_t idx = p + __popc(mask & lt);
-      const uint32_t wv = words[idx < nw ? idx : (nw ? nw - 1 : 0)];
-      if (need) {
-        if (idx >= nw) bad = true;
-        x = (x << 16) | wv;
+      if (full * 32 < nsym) {  // last, partial step
+        const bool active = full * 32 + lane < nsym;
+        const uint32_t slot = x & (kRansM - 1);
+        const uint32_t e = ent[slot];
+        if (active) {
+          x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+          o[32 * full] = sym[slot];
+        }
+        const bool need = active && x < kRansL;
+        const unsigned mask = __ballot_sync(0xffffffffu, need);
+        const uint32_t w16 = stage[(p + __popc(mask & lt)) & (kDecStage - 1)];
+        x = need ? ((x << 16) | w16) : x;
+        p += __popc(mask);
       }
-      p += __popc(mask);
+      bad = bad || p > nw;
+    } else {  // words read from global memory, every index checked
+      const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
+      const uint32_t steps = (nsym + 31) / 32;
+      for (uint32_t st = 0; st < steps; ++st) {
+        const bool active = st * 32 + lane < nsym;
+        const uint32_t slot = x & (kRansM - 1);
+        const uint32_t e = ent[slot];
+        if (active) {
+          x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+          o[32 * st] = sym[slot];
+        }
+        const bool need = active && x < kRansL;
+        const unsigned mask = __ballot_sync(0xffffffffu, need);
+        const uint32_t idx = p + __popc(mask & lt);
+        if (need) {
+          if (idx < nw) x = (x << 16) | words[idx];
+          else { bad = true; x = kRansL; }
+        }
+        p += __popc(mask);
+      }
     }
     bad = bad || x != kRansL || p != nw;
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, kDevErrCorrupt);
