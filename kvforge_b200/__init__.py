@@ -164,7 +164,7 @@ class CompressedKV:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h and L._lib is not None:
+        if h and L is not None and L._lib is not None:  # module globals are gone at interpreter exit
             L.lib().kvf_compressed_free(h)
             self._h = None
 
@@ -274,7 +274,7 @@ class Basis:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h and L._lib is not None:
+        if h and L is not None and L._lib is not None:  # module globals are gone at interpreter exit
             L.lib().kvf_basis_free(h)
             self._h = None
 

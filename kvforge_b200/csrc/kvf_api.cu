@@ -277,10 +277,9 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
 kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, size_t plen,
                             const uint32_t* freq, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
   const size_t nc = rans_num_chunks(plen, kRansChunk);
-  uint8_t* slots = sc.get<uint8_t>(nc * rans_slot_bytes(kRansChunk));
-  if (!slots) return fail(KVF_ERR_CUDA, "scratch allocation failed");
-  KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, freq, slots, ctx->d_status, st));
-  KVF_CUDA(launch_rans_assemble(slots, plen, kRansChunk, out, d_len, st));
+  unsigned long long* lookback = sc.get<unsigned long long>(nc);
+  if (!lookback) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, freq, lookback, out, d_len, ctx->d_status, st));
   return KVF_OK;
 }
 
@@ -341,6 +340,7 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
 
   if (basis) {
     ProjectOut po;
+  po.status = ctx->d_status;
     po.cpart = cpart;
     po.levels = quant_levels(dt);
     if (axis == KVF_PER_CHANNEL) {
@@ -935,6 +935,7 @@ kvf_status kvf_project(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t 
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
   ProjectOut po;
+  po.status = ctx->d_status;
   po.P = projected;
   KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, S(stream)));
   return KVF_OK;
@@ -966,6 +967,7 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
   cudaStream_t st = S(stream);
   const size_t n = H * T * R;
   ProjectOut po;
+  po.status = ctx->d_status;
   po.levels = quant_levels(data_type);
   if (axis == KVF_PER_CHANNEL) {
     float* P = sc.get<float>(n);

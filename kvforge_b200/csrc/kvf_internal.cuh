@@ -12,14 +12,15 @@
 namespace kvf {
 
 // ---- rANS container constants (documented in kvf_rans.cu) ----------------
-constexpr uint32_t kRansProbBits = 15;
+constexpr uint32_t kRansProbBits = 13;
 constexpr uint32_t kRansM = 1u << kRansProbBits;
 constexpr uint32_t kRansL = 1u << 16;
 constexpr uint32_t kRansLanes = 32;
-constexpr uint32_t kRansChunk = 16384;       // symbols per chunk (encoder default)
-constexpr uint32_t kRansMagic = 0x3152564Bu;  // "KVR1"
+constexpr uint32_t kRansChunk = 16384;                  // symbols per chunk (encoder default)
+constexpr uint32_t kRansMaxChunk = kRansLanes * 65535u;  // lane word counts are u16
+constexpr uint32_t kRansMagic = 0x3252564Bu;             // "KVR2"
 constexpr size_t kRansHeader = 32;
-constexpr size_t kRansChunkHeader = 4 + 4 * kRansLanes;  // nwords + 32 lane states
+constexpr size_t kRansPayloadHeader = 4 * kRansLanes + 2 * kRansLanes;  // lane states + lane word counts
 
 // dynamic shared memory above this opts in to the larger per-block limit;
 // the margin below 48 KB leaves room for a kernel's static shared memory
@@ -31,14 +32,9 @@ constexpr unsigned kDevErrEntropy = 2u;
 constexpr unsigned kDevErrTimeout = 4u;
 
 __host__ __device__ inline size_t rans_num_chunks(size_t n, uint32_t chunk) { return (n + chunk - 1) / chunk; }
-__host__ __device__ inline size_t rans_slot_words(uint32_t chunk) { return chunk + 2; }
-__host__ __device__ inline size_t rans_slot_bytes(uint32_t chunk) {
-  size_t b = kRansChunkHeader + 2 * rans_slot_words(chunk);
-  return (b + 15) & ~size_t(15);
-}
 inline size_t rans_max_len(size_t n, uint32_t chunk) {
   size_t nc = rans_num_chunks(n, chunk);
-  return kRansHeader + 4 * (nc + 1) + nc * (kRansChunkHeader + 2) + 2 * n;
+  return kRansHeader + 4 * (nc + 1) + nc * (kRansPayloadHeader + 2) + 2 * n;
 }
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -177,6 +173,7 @@ struct ProjectOut {
   float* scales = nullptr;
   float* mins = nullptr;
   float levels = 15.0f;
+  unsigned* status = nullptr;  // device status word: a bounded wait that expires sets kDevErrTimeout
 };
 cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                            const float* basis_vt, const uint64_t* ranks, size_t R, const ProjectOut& o,
@@ -202,11 +199,11 @@ cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t 
 
 // rANS (kvf_rans.cu)
 // encode and decode build the model from the 256 counts themselves
+// container of n symbols into out (capacity rans_max_len), its length into
+// out_len; lookback: one zeroed-here word per chunk
 cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
-                               uint8_t* slots, unsigned* status, cudaStream_t st);
-cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk, uint8_t* out,
-                                 uint64_t* out_len, cudaStream_t st);
-// comp_len_dev (when not NULL) supplies the container length from device memory
+                               unsigned long long* lookback, uint8_t* out, uint64_t* out_len, unsigned* status,
+                               cudaStream_t st);
 cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
                                const uint32_t* freq, size_t n, uint8_t* out, unsigned* status,
                                cudaStream_t st);

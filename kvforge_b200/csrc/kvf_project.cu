@@ -15,6 +15,9 @@
 // of squares per head; partials per block are combined in a fixed order, so
 // the result is deterministic (it differs from the sequential reference only
 // in fp64 rounding order).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
 #include <mutex>
@@ -24,7 +27,6 @@
 namespace kvf {
 namespace {
 
-constexpr int kProjThreads = 128;
 constexpr int kRecRows = 128;                    // token rows per reconstruct block
 constexpr int kCalibTile = 1 << 16;              // elements per calibration block
 constexpr int kGramTile = 512;                   // tokens per Gram block
@@ -57,25 +59,34 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 
 // ---- projection -------------------------------------------------------------
 // One persistent kernel. The grid walks (head, 128-token tile) items in
-// contiguous ranges; thread t owns row t of every tile. PIPE variant (rows a
-// multiple of 16 bytes, 16-byte aligned input): each thread streams its own
-// row into shared memory with asynchronous 16-byte copies (cp.async), two
-// stages deep, so the next tile's row is in flight while the current one is
-// computed; 16-byte chunks are XOR-swizzled by row so the rows a warp reads
-// fall on distinct banks (or rows are padded by 16 bytes where the swizzle
-// does not apply). Generic variant: scalar loads from global memory.
+// contiguous ranges per block; thread t owns row t of every tile and computes
+// its R coefficients. Each coefficient is a fused multiply-add chain over
+// c = 0..D-1 from +0.0; two chains advance per fma.rn.f32x2 (each element
+// rounded once), so values are identical to the CPU oracle's fmaf chain. The
+// basis of head h sits transposed in shared memory, vT[c][RG], read with
+// broadcast 16-byte loads at compile-time offsets.
 //
-// Each coefficient is a fused multiply-add chain over c = 0..D-1 from +0.0;
-// two chains advance per fma.rn.f32x2 (each element rounded once), so values
-// are identical to the CPU oracle's fmaf chain. The basis of head h sits
-// transposed in shared memory, vT[c][r], read with broadcast float4 loads.
+// TMA variant (rows a multiple of 128 bytes, 16-byte aligned input): a tile
+// is streamed as column blocks of 128 rows x 128 bytes (16 KB), each one 2-D
+// tensor copy (cp.async.bulk.tensor, no multicast) with the 128-byte swizzle,
+// several blocks in flight per CTA; the accumulators stay in registers across
+// a tile's column blocks. The swizzle stores 16-byte chunk j of a 128-byte
+// row at j ^ (bits 7-9 of the row's address), so the reads of eight
+// consecutive rows fall on distinct banks. Small stages keep several CTAs resident per SM. Waits are
+// bounded: a wait that expires raises the device timeout status.
+// Generic variant: scalar loads from global memory.
 //
-// Epilogues (outputs staged in shared memory, stored coalesced):
+// Epilogues (each thread stores its own row; consecutive rows are contiguous):
 //   MODE 0: P [H,T,R];
 //   MODE 1: P and per-(head, r) min/max folded into block-local keys,
 //           flushed with one global atomic per (block, head, r);
 //   MODE 2: per-token quantization: scale/min per token, codes as bytes or
 //           INT4-packed bytes, plus an optional byte histogram.
+constexpr int kProjRows = 128;             // token rows per tile = threads per block
+constexpr int kColBytes = 128;             // bytes of each row per streamed column block
+constexpr int kColStage = kProjRows * kColBytes;
+constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before a wait gives up
+
 template <typename TIn>
 struct Seg;
 template <>
@@ -102,82 +113,110 @@ struct Seg<float> {
   }
 };
 
-__device__ __forceinline__ void cp16(void* smem, const void* gmem) {
-  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem));
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// true once the barrier's phase with the given parity has completed; false
+// when the bounded number of polls ran out
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+// 2-D tile copy global -> shared through a tensor map (x: element column, y: row)
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
 
-// shared-memory layout (byte offsets, all multiples of 16), computed on the host
+// shared-memory layout (byte offsets), computed on the host
 struct ProjSmem {
-  int keys;    // [2 * Rk] int
-  int hist;    // [256] u32
-  int ostage;  // output staging, 128 * R * 4 bytes (or -1: the current row stage)
-  int xbuf;    // [2][128][stride] (PIPE)
-  int stride;  // bytes per staged row
-  int swz;     // 1: XOR-swizzle 16-byte chunks by row
-  int pow2;    // 16-byte chunks per row is a power of two
+  int keys;    // [2 * Rk] int (MODE 1)
+  int hist;    // [256] u32 (MODE 2)
+  int cstage;  // [kProjRows][R] code bytes (MODE 2, odd R packing)
+  int bars;    // [stages] u64 (TMA)
+  int xbuf;    // [stages][kColStage] (TMA), 1024-byte aligned
+  int stages;
   int total;
 };
 
+// acc[q] holds coefficients (2q, 2q + 1) as one packed f32x2 register pair;
+// x is broadcast to both halves once, the basis row is read as packed pairs
 template <int RG>
-__device__ __forceinline__ void fma_row(float2 (&acc)[RG / 2], float xv, const float* vrow) {
-  const float2 xx = make_float2(xv, xv);
-  const float4* vr = reinterpret_cast<const float4*>(vrow);
+__device__ __forceinline__ void fma_row(unsigned long long (&acc)[RG / 2], float xv, const float* vrow) {
+  unsigned long long xx;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(xx) : "f"(xv));
+  const ulonglong2* vr = reinterpret_cast<const ulonglong2*>(vrow);
 #pragma unroll
   for (int q = 0; q < RG / 4; ++q) {
-    const float4 v = vr[q];
-    acc[2 * q] = ffma2(xx, make_float2(v.x, v.y), acc[2 * q]);
-    acc[2 * q + 1] = ffma2(xx, make_float2(v.z, v.w), acc[2 * q + 1]);
+    const ulonglong2 v = vr[q];
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[2 * q]) : "l"(xx), "l"(v.x));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[2 * q + 1]) : "l"(xx), "l"(v.y));
   }
 }
 
-template <typename TIn, int RG, bool CALIB, int MODE, bool PIPE>
-__global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict__ x, int H, int T, int D,
-                                                        const float* __restrict__ bvt,
-                                                        const uint64_t* __restrict__ ranks, int R, int Rpad,
-                                                        ProjSmem L, ProjectOut o) {
-  extern __shared__ __align__(16) uint8_t smraw[];
+template <typename TIn, int RG, bool CALIB, int MODE, bool TMA>
+__global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant__ CUtensorMap xmap,
+                                                     const TIn* __restrict__ x, int H, int T, int D,
+                                                     const float* __restrict__ bvt,
+                                                     const uint64_t* __restrict__ ranks, int R, int Rpad,
+                                                     ProjSmem L, ProjectOut o) {
+  extern __shared__ __align__(1024) uint8_t smraw[];
   float* vT = reinterpret_cast<float*>(smraw);  // [D][Rpad]
   const int Rk = (R + 3) & ~3;
   int* skmin = reinterpret_cast<int*>(smraw + L.keys);
   int* skmax = skmin + Rk;
   uint32_t* shist = reinterpret_cast<uint32_t*>(smraw + L.hist);
+  uint8_t* cstage = smraw + L.cstage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smraw + L.bars);
   uint8_t* xbuf = smraw + L.xbuf;
   const int tid = threadIdx.x;
-  const int nvec = D * (int)sizeof(TIn) / 16;
-  const int tiles = (T + kProjThreads - 1) / kProjThreads;
+  const int tiles = (T + kProjRows - 1) / kProjRows;
   const long long items = (long long)H * tiles;
   const long long i0 = items * blockIdx.x / gridDim.x;
   const long long i1 = items * (blockIdx.x + 1) / gridDim.x;
-  const bool staged = (R <= RG);  // single r-group: outputs go through shared memory
+  const long long nit = i1 - i0;
+  constexpr int kColElems = kColBytes / (int)sizeof(TIn);
+  const int ncb = TMA ? D / kColElems : 1;  // column blocks per tile
+  const long long units = nit * ncb;
   const bool hist_on = (MODE == 2) && o.hist != nullptr;
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
+  if (TMA && tid == 0) {
+    for (int s = 0; s < L.stages; ++s) mbar_init(&bars[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
 
-  // the block copies the tile's contiguous rows cooperatively (consecutive
-  // threads take consecutive 16-byte chunks, so global reads coalesce); chunk j
-  // of row r lands at position j ^ (r mod nvec) when swizzling
-  const int lg = 31 - __clz(nvec > 0 ? nvec : 1);
-  auto issue = [&](long long it, int stage) {
-    if (PIPE) {
+  // unit u = column block (u mod ncb) of item (u / ncb), into stage u mod stages
+  long long issued = 0;
+  auto issue = [&](long long u) {
+    if (TMA && tid == 0) {
+      const long long it = i0 + u / ncb;
+      const int cb = (int)(u % ncb);
       const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
-      const int nr = min(kProjThreads, T - tile * kProjThreads);
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(x + ((size_t)h * T + (size_t)tile * kProjThreads) * D);
-      uint8_t* dst = xbuf + (size_t)stage * kProjThreads * L.stride;
-      const int total = nr * nvec;
-      for (int i = tid; i < total; i += blockDim.x) {
-        const int r = L.pow2 ? (i >> lg) : (i / nvec);
-        const int j = i - r * nvec;
-        const int pj = L.swz ? (j ^ (r & (nvec - 1))) : j;
-        cp16(dst + (size_t)r * L.stride + 16 * pj, src + 16 * (size_t)i);
-      }
-      cp_commit();
+      const int s = (int)(u % L.stages);
+      mbar_expect_tx(&bars[s], (uint32_t)kColStage);
+      tma_load_2d(xbuf + (size_t)s * kColStage, &xmap, cb * kColElems, h * T + tile * kProjRows, &bars[s]);
     }
+    issued = u + 1;
   };
-
   auto flush_keys = [&](int hh) {
     if (MODE == 1 && hh >= 0)
       for (int r = tid; r < R; r += blockDim.x) {
@@ -186,91 +225,92 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
       }
   };
 
+  if (TMA)
+    for (long long u = 0; u < L.stages - 1 && u < units; ++u) issue(u);
   int cur_h = -1, rank = 0;
-  if (PIPE && i0 < i1) issue(i0, 0);
-  for (long long it = i0; it < i1; ++it) {
-    const int stage = (int)((it - i0) & 1);
+  long long stuck = -1;  // the unit whose wait expired
+  for (long long li = 0; li < nit; ++li) {
+    const long long it = i0 + li;
     const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
-    if (h != cur_h) {  // block-uniform
-      __syncthreads();
-      flush_keys(cur_h);
-      const uint64_t rk = ranks[h];
-      rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
-      const float* B = bvt + (size_t)h * R * D;
-      for (int i = tid; i < D * Rpad; i += blockDim.x) {
-        const int c = i / Rpad, r = i - c * Rpad;
-        vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
-      }
-      if (MODE == 1)
-        for (int r = tid; r < R; r += blockDim.x) {
-          skmin[r] = fkey(INFINITY);
-          skmax[r] = fkey(-INFINITY);
-        }
-      __syncthreads();
-      cur_h = h;
-    }
-    if (PIPE) {
-      if (it + 1 < i1) {
-        issue(it + 1, stage ^ 1);
-        cp_wait<1>();
-      } else {
-        cp_wait<0>();
-      }
-      __syncthreads();  // rows were copied by other threads
-    }
-    const int t = tile * kProjThreads + tid;
+    const int t = tile * kProjRows + tid;
     const bool ok = t < T;
     const size_t g = (size_t)h * T + (ok ? t : 0);
-    const size_t g0 = (size_t)h * T + (size_t)tile * kProjThreads;
-    const int nrows = min(kProjThreads, T - tile * kProjThreads);
-    const uint8_t* row = xbuf + ((size_t)stage * kProjThreads + tid) * L.stride;
-    const TIn* xr = x + g * D;
-    uint8_t* ostage = (L.ostage >= 0) ? smraw + L.ostage : xbuf + (size_t)stage * kProjThreads * L.stride;
+    const size_t g0 = (size_t)h * T + (size_t)tile * kProjRows;
+    const int nrows = min(kProjRows, T - tile * kProjRows);
     double s1 = 0.0, s2 = 0.0;
     for (int rg = 0; rg < R; rg += RG) {
-      float2 acc2[RG / 2];
+      unsigned long long acc2[RG / 2];
 #pragma unroll
-      for (int r = 0; r < RG / 2; ++r) acc2[r] = make_float2(0.0f, 0.0f);
-      if (PIPE) {
-        constexpr int PV = Seg<TIn>::PV;
-        const int sw = L.swz ? (tid & (nvec - 1)) : 0;
-        for (int j = 0; j < nvec; ++j) {
-          float xv[PV];
-          if (ok) {
-            const uint4 u = *reinterpret_cast<const uint4*>(row + 16 * (j ^ sw));
-            Seg<TIn>::unpack(u, xv);
-          } else {
-#pragma unroll
-            for (int k = 0; k < PV; ++k) xv[k] = 0.0f;
+      for (int r = 0; r < RG / 2; ++r) acc2[r] = 0ull;  // +0.0f in both halves
+      for (int cb = 0; cb < ncb; ++cb) {
+        const long long u = li * ncb + cb;
+        if (TMA) {
+          const int s = (int)(u % L.stages);
+          const bool ok_wait = mbar_wait(&bars[s], (uint32_t)((u / L.stages) & 1));
+          // also: every thread is done with unit u - 1, whose stage is refilled next
+          if (__syncthreads_or(!ok_wait)) {
+            stuck = u;
+            break;
           }
-          if (CALIB && rg == 0) {
+          if (u + L.stages - 1 < units) issue(u + L.stages - 1);
+        } else if (cb == 0) {
+          __syncthreads();
+        }
+        if (cb == 0 && rg == 0 && h != cur_h) {  // block-uniform: this head's basis
+          flush_keys(cur_h);
+          const uint64_t rk = ranks[h];
+          rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
+          const float* B = bvt + (size_t)h * R * D;
+          for (int i = tid; i < D * Rpad; i += blockDim.x) {
+            const int c = i / Rpad, r = i - c * Rpad;
+            vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
+          }
+          if (MODE == 1)
+            for (int r = tid; r < R; r += blockDim.x) {
+              skmin[r] = fkey(INFINITY);
+              skmax[r] = fkey(-INFINITY);
+            }
+          __syncthreads();
+          cur_h = h;
+        }
+        if (TMA) {  // single r-group: vT rows are RG floats
+          constexpr int PV = Seg<TIn>::PV;
+          const uint8_t* sb = xbuf + (size_t)(u % L.stages) * kColStage + tid * kColBytes;
+          const int sw = (int)(smem_addr(sb) >> 7) & 7;  // the swizzle XORs address bits 4-6 with bits 7-9
 #pragma unroll
-            for (int k = 0; k < PV; ++k) {
-              const double v = (double)xv[k];
+          for (int jj = 0; jj < kColBytes / 16; ++jj) {
+            float xv[PV];
+            Seg<TIn>::unpack(*reinterpret_cast<const uint4*>(sb + ((jj ^ sw) << 4)), xv);
+            if (CALIB) {
+#pragma unroll
+              for (int k = 0; k < PV; ++k) {
+                const double v = ok ? (double)xv[k] : 0.0;
+                s1 += v;
+                s2 += v * v;
+              }
+            }
+            const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * RG;
+#pragma unroll
+            for (int k = 0; k < PV; ++k) fma_row<RG>(acc2, xv[k], vb + k * RG);
+          }
+        } else {
+          const TIn* xr = x + g * D;
+          for (int c = 0; c < D; ++c) {
+            const float xv = ok ? ldf(xr, c) : 0.0f;
+            if (CALIB && rg == 0) {
+              const double v = (double)xv;
               s1 += v;
               s2 += v * v;
             }
+            fma_row<RG>(acc2, xv, vT + (size_t)c * Rpad + rg);
           }
-#pragma unroll
-          for (int k = 0; k < PV; ++k) fma_row<RG>(acc2, xv[k], vT + (size_t)(j * PV + k) * Rpad + rg);
-        }
-      } else {
-        for (int c = 0; c < D; ++c) {
-          const float xv = ok ? ldf(xr, c) : 0.0f;
-          if (CALIB && rg == 0) {
-            const double v = (double)xv;
-            s1 += v;
-            s2 += v * v;
-          }
-          fma_row<RG>(acc2, xv, vT + (size_t)c * Rpad + rg);
         }
       }
+      if (stuck >= 0) break;
       float acc[RG];
 #pragma unroll
-      for (int r = 0; r < RG / 2; ++r) {
-        acc[2 * r] = acc2[r].x;
-        acc[2 * r + 1] = acc2[r].y;
-      }
+      for (int r = 0; r < RG / 2; ++r)
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * r]), "=f"(acc[2 * r + 1]) : "l"(acc2[r]));
 #pragma unroll
       for (int r = 0; r < RG; ++r)
         if (rg + r >= rank) acc[r] = 0.0f;  // projection.rs:96
@@ -290,21 +330,17 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
         }
       }
       if (MODE == 0 || MODE == 1) {
-        if (staged) {
-          if (PIPE && L.ostage < 0) __syncthreads();  // every row of this stage has been read
-          float* ps = reinterpret_cast<float*>(ostage);
+        if (ok) {
+          float* pr = o.P + g * R + rg;
+          if (rg + RG <= R && (R & 3) == 0) {
 #pragma unroll
-          for (int r = 0; r < RG; ++r)
-            if (r < R) ps[tid * R + r] = acc[r];
-          __syncthreads();
-          float* dst = o.P + g0 * R;
-          for (int i = tid; i < nrows * R; i += blockDim.x) dst[i] = ps[i];
-          __syncthreads();
-        } else if (ok) {
-          float* pr = o.P + g * R;
+            for (int q = 0; q < RG / 4; ++q)
+              reinterpret_cast<float4*>(pr)[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+          } else {
 #pragma unroll
-          for (int r = 0; r < RG; ++r)
-            if (rg + r < R) pr[rg + r] = acc[r];
+            for (int r = 0; r < RG; ++r)
+              if (rg + r < R) pr[r] = acc[r];
+          }
         }
       } else {  // MODE 2 (R <= RG)
         float mn = INFINITY, mx = -INFINITY;
@@ -313,35 +349,49 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
           if (r < R) mm_update(acc[r], mn, mx);
         const float scale = make_scale(mn, mx, o.levels);
         const float inv = __frcp_rn(scale);
+        uint32_t cd[RG];
+#pragma unroll
+        for (int r = 0; r < RG; ++r) cd[r] = (r < R) ? qcode_fast(acc[r], mn, scale, inv, o.levels) : 0u;
         if (ok) {
           o.scales[g] = scale;
           o.mins[g] = mn;
         }
-        if (PIPE && L.ostage < 0) __syncthreads();
-        uint8_t* cs = ostage;
+        if (o.packed && (R & 1) == 0) {  // this row's codes start on a byte boundary
+          if (ok) {
+            uint8_t* dp = o.packed + (g * R) / 2;
 #pragma unroll
-        for (int r = 0; r < RG; ++r)
-          if (r < R) cs[tid * R + r] = (uint8_t)qcode_fast(acc[r], mn, scale, inv, o.levels);
-        __syncthreads();
-        const int cnt = nrows * R;
-        if (o.packed) {
+            for (int b = 0; b < RG / 2; ++b)
+              if (2 * b < R) {
+                const uint32_t byte = (cd[2 * b] & 0xFu) | ((cd[2 * b + 1] & 0xFu) << 4);
+                dp[b] = (uint8_t)byte;
+                if (hist_on) atomicAdd(&shist[byte], 1u);
+              }
+          }
+        } else if (o.packed) {  // odd R: pairs run across rows; pack the tile through shared memory
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+            if (r < R) cstage[tid * R + r] = (uint8_t)cd[r];
+          __syncthreads();
+          const int cnt = nrows * R;
           uint8_t* dp = o.packed + (g0 * R) / 2;
           for (int b = tid; b < cnt / 2; b += blockDim.x) {
-            const uint32_t byte = (cs[2 * b] & 0xFu) | ((uint32_t)(cs[2 * b + 1] & 0xFu) << 4);
+            const uint32_t byte = (cstage[2 * b] & 0xFu) | ((uint32_t)(cstage[2 * b + 1] & 0xFu) << 4);
             dp[b] = (uint8_t)byte;
             if (hist_on) atomicAdd(&shist[byte], 1u);
           }
-        } else {
-          uint8_t* dc = o.codes + g0 * R;
-          for (int i = tid; i < cnt; i += blockDim.x) {
-            const uint8_t c = cs[i];
-            dc[i] = c;
-            if (hist_on) atomicAdd(&shist[c], 1u);
-          }
+          __syncthreads();
+        } else if (ok) {
+          uint8_t* dc = o.codes + g * R;
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+            if (r < R) {
+              dc[r] = (uint8_t)cd[r];
+              if (hist_on) atomicAdd(&shist[cd[r]], 1u);
+            }
         }
-        __syncthreads();
       }
     }
+    if (stuck >= 0) break;
     if (CALIB) {
       block_sum2(s1, s2);
       if (tid == 0) {
@@ -349,8 +399,13 @@ __global__ void __launch_bounds__(kProjThreads) k_project(const TIn* __restrict_
         o.cpart[2 * slot] = s1;
         o.cpart[2 * slot + 1] = s2;
       }
-      __syncthreads();  // block_sum2's shared slots are reused by the next item
     }
+  }
+  if (stuck >= 0) {
+    // copies still in flight land (bounded waits) before the block's shared memory is released
+    if (tid == 0 && o.status) atomicOr(o.status, kDevErrTimeout);
+    for (long long u = stuck; u < issued; ++u) mbar_wait(&bars[u % L.stages], (uint32_t)((u / L.stages) & 1));
+    return;
   }
   __syncthreads();
   flush_keys(cur_h);
@@ -364,10 +419,59 @@ struct LaunchCache {
   int per_sm = 0;
 };
 
-template <typename TIn, int RG, bool CALIB, int MODE, bool PIPE>
-cudaError_t project_launch(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
-                           size_t R, const ProjectOut& o, cudaStream_t st) {
-  const int Rpad = (int)(((R + RG - 1) / RG) * RG);
+// cuTensorMapEncodeTiled from the driver, looked up once (nullptr when absent)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [H*T rows, D columns] of TIn, boxes of 128 rows x 128 bytes, 128-byte swizzle
+template <typename TIn>
+bool encode_rows_map(CUtensorMap* map, const TIn* x, size_t rows, size_t D) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t gdim[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)(D * sizeof(TIn))};
+  const cuuint32_t box[2] = {(cuuint32_t)(kColBytes / sizeof(TIn)), (cuuint32_t)kProjRows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      sizeof(TIn) == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return enc(map, dt, 2, const_cast<TIn*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename TIn, int RG, bool CALIB, int MODE, bool TMA>
+cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
+                           const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st) {
+  auto kern = k_project<TIn, RG, CALIB, MODE, TMA>;
+  // per-device launch facts, looked up once per kernel instantiation
+  constexpr int kDevs = 64;
+  static int max_dyn[kDevs] = {};  // dynamic shared memory this kernel may opt in to (0: not yet known)
+  static int opted[kDevs] = {};    // opted in so far
+  static int sms[kDevs] = {};
+  static LaunchCache cache[kDevs][4];
+  cudaError_t e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
+  if (!max_dyn[dev]) {
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    max_dyn[dev] = std::max(1, optin - (int)fa.sharedSizeBytes);
+  }
+  const int Rpad = TMA ? RG : (int)(((R + RG - 1) / RG) * RG);
   const int Rk = (int)((R + 3) & ~size_t(3));
   ProjSmem L{};
   int off = (int)(D * Rpad * sizeof(float));
@@ -376,47 +480,27 @@ cudaError_t project_launch(const TIn* x, size_t H, size_t T, size_t D, const flo
   off = (off + 15) & ~15;
   L.hist = off;
   off += 256 * 4;
-  const int row_bytes = (int)(D * sizeof(TIn));
-  const int nvec = row_bytes / 16;
-  L.pow2 = nvec > 0 && (nvec & (nvec - 1)) == 0;
-  L.swz = PIPE && nvec >= 8 && L.pow2;
-  L.stride = PIPE ? (L.swz ? row_bytes : row_bytes + 16) : 0;
+  L.cstage = off;
+  off += (MODE == 2) ? kProjRows * (int)R : 0;
+  off = (off + 15) & ~15;
+  L.bars = off;
+  off += 8 * 8;
+  off = (off + 1023) & ~1023;  // the 128-byte swizzle repeats every 1024 bytes
   L.xbuf = off;
-  if (PIPE) off += 2 * kProjThreads * L.stride;
-  const bool staged = R <= (size_t)RG;
-  const int need_stage = staged ? (int)(kProjThreads * R * 4) : 0;
-  if (PIPE && staged && kProjThreads * L.stride >= need_stage) {
-    L.ostage = -1;  // reuse the current row stage
-  } else {
-    L.ostage = off;
-    off += need_stage;
-  }
-  L.total = (off + 15) & ~15;
-  if (L.total > 200 * 1024) {
-    if (PIPE) return project_launch<TIn, RG, CALIB, MODE, false>(x, H, T, D, bvt, ranks, R, o, st);
-    return cudaErrorInvalidValue;
-  }
-  auto kern = k_project<TIn, RG, CALIB, MODE, PIPE>;
-  // per-device launch facts, looked up once per kernel instantiation
-  constexpr int kDevs = 64;
-  static bool attr_set[kDevs] = {};
-  static int sms[kDevs] = {};
-  static LaunchCache cache[kDevs][4];
-  cudaError_t e;
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) != cudaSuccess)
+  L.stages = TMA ? 3 : 0;
+  off += L.stages * kColStage;
+  L.total = off;
+  if (L.total > max_dyn[dev]) return cudaErrorInvalidValue;
+  if (L.total > opted[dev] && L.total > 48 * 1024 - 1024) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total)) != cudaSuccess)
       return e;
-    if ((e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    attr_set[dev] = true;
+    opted[dev] = L.total;
   }
   int per_sm = 0;
   for (auto& c : cache[dev])
     if (c.smem == L.total) per_sm = c.per_sm;
   if (per_sm == 0) {
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, L.total)) != cudaSuccess)
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjRows, L.total)) != cudaSuccess)
       return e;
     per_sm = std::max(per_sm, 1);
     for (auto& c : cache[dev])
@@ -426,47 +510,47 @@ cudaError_t project_launch(const TIn* x, size_t H, size_t T, size_t D, const flo
         break;
       }
   }
-  const int nsm = sms[dev];
-  const size_t items = H * ((T + kProjThreads - 1) / kProjThreads);
-  const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * nsm));
-  kern<<<(unsigned)grid, kProjThreads, L.total, st>>>(x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
+  const size_t items = H * ((T + kProjRows - 1) / kProjRows);
+  const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * sms[dev]));
+  kern<<<(unsigned)grid, kProjRows, L.total, st>>>(map, x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
   note_launches(1);
   return cudaGetLastError();
 }
 
-template <typename TIn, int RG, bool PIPE>
-cudaError_t project_mode(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
-                         size_t R, const ProjectOut& o, cudaStream_t st) {
+template <typename TIn, int RG, bool TMA>
+cudaError_t project_mode(const CUtensorMap& map, const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
+                         const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st) {
   if (o.mode == 1) {
-    if (o.cpart) return project_launch<TIn, RG, true, 1, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-    return project_launch<TIn, RG, false, 1, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+    if (o.cpart) return project_launch<TIn, RG, true, 1, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+    return project_launch<TIn, RG, false, 1, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
   }
   if (o.cpart) return cudaErrorInvalidValue;  // calibration is fused into the key path only
   if (o.mode == 2) {
     if (R > (size_t)RG) return cudaErrorInvalidValue;
-    return project_launch<TIn, RG, false, 2, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+    return project_launch<TIn, RG, false, 2, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
   }
-  return project_launch<TIn, RG, false, 0, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+  return project_launch<TIn, RG, false, 0, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
 }
 
-template <typename TIn, bool PIPE>
-cudaError_t project_rg(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
-                       size_t R, const ProjectOut& o, cudaStream_t st) {
-  if (R <= 4) return project_mode<TIn, 4, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 8) return project_mode<TIn, 8, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 12) return project_mode<TIn, 12, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 16) return project_mode<TIn, 16, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-  if (R <= 24) return project_mode<TIn, 24, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
-  return project_mode<TIn, 32, PIPE>(x, H, T, D, bvt, ranks, R, o, st);
+template <typename TIn, bool TMA>
+cudaError_t project_rg(const CUtensorMap& map, const TIn* x, size_t H, size_t T, size_t D, const float* bvt,
+                       const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st) {
+  if (R <= 4) return project_mode<TIn, 4, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 8) return project_mode<TIn, 8, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 12) return project_mode<TIn, 12, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 16) return project_mode<TIn, 16, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  if (R <= 24) return project_mode<TIn, 24, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  return project_mode<TIn, 32, false>(map, x, H, T, D, bvt, ranks, R, o, st);  // several r-groups: generic path
 }
 
 template <typename TIn>
 cudaError_t project_typed(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
                           size_t R, const ProjectOut& o, cudaStream_t st) {
-  const bool pipe = (D * sizeof(TIn)) % 16 == 0 && aligned(x, 16) &&
-                    (D * 32 * 4 + 2 * kProjThreads * (D * sizeof(TIn) + 16) + 16 * 1024) <= 200 * 1024;
-  if (pipe) return project_rg<TIn, true>(x, H, T, D, bvt, ranks, R, o, st);
-  return project_rg<TIn, false>(x, H, T, D, bvt, ranks, R, o, st);
+  CUtensorMap map{};
+  const bool tma = (D * sizeof(TIn)) % kColBytes == 0 && aligned(x, 16) && R <= 24 && H * T < (1ull << 31) &&
+                   encode_rows_map(&map, x, H * T, D);
+  if (tma) return project_rg<TIn, true>(map, x, H, T, D, bvt, ranks, R, o, st);
+  return project_rg<TIn, false>(map, x, H, T, D, bvt, ranks, R, o, st);
 }
 
 // ---- calibration partials without projection ----------------------------------
@@ -764,7 +848,7 @@ cudaError_t calib_static_scratch(int device, double** out) {
   return cudaSuccess;
 }
 
-size_t project_num_tiles(size_t T) { return (T + kProjThreads - 1) / kProjThreads; }
+size_t project_num_tiles(size_t T) { return (T + kProjRows - 1) / kProjRows; }
 
 cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                            const float* basis_vt, const uint64_t* ranks, size_t R, const ProjectOut& o,

@@ -1,26 +1,28 @@
-// Chunked, 32-lane interleaved rANS (sm_100a).
+// Chunked rANS with 32 independent lane streams per chunk (sm_100a).
 //
 // The reference codes one serial stream with constriction's stack ANS
 // (crates/kvforge-cpu/src/entropy.rs:42-123). That stream cannot be split, so
 // this library defines its own container, mirrored bit for bit by the CPU
 // oracle so that each side decodes the other's output:
 //
-//   state x in [2^16, 2^32), 16-bit renormalisation words, 15-bit model.
-//   header (32 B): u32 magic "KVR1", u32 prob_bits = 15, u32 lanes = 32,
+//   state x in [2^16, 2^32), 16-bit renormalisation words, 13-bit model.
+//   header (32 B): u32 magic "KVR2", u32 prob_bits = 13, u32 lanes = 32,
 //                  u32 chunk_symbols, u64 original_len, u32 num_chunks,
 //                  u32 header_bytes = 32 + 4 * (num_chunks + 1)
 //   u32 chunk_offset[num_chunks + 1]: byte offset of each chunk payload from
 //                  the container start; the last entry is the total length
-//   chunk payload: u32 nwords; u32 final_state[32]; u16 words[nwords];
-//                  one zero u16 when nwords is odd (4-byte alignment)
+//   chunk payload: u32 final_state[32]; u16 lane_words[32];
+//                  u16 words[sum(lane_words)]: lane 0's stream, lane 1's, ...,
+//                  each in decoding order; one zero u16 when the sum is odd
 //
-// One warp codes one chunk; symbol i of a chunk belongs to lane i % 32, step
-// i / 32. The encoder runs steps backwards; in each step the active lanes
-// renormalise (emitters ordered by descending lane, found with a ballot) and
-// then encode. The decoder runs steps forwards and serves consuming lanes in
-// ascending order, so it reads the word array front to back.
+// Symbol i of a chunk belongs to lane i % 32, step i / 32, so a warp reads and
+// writes 32 consecutive bytes per step. Each lane is an ordinary rANS coder
+// over its own symbols with its own word stream: no lane ever waits for
+// another, and a decoding lane knows the address of its next word before it
+// needs it, so the only load on a state's dependency chain is the model
+// lookup. The price is 64 bytes of word counts per chunk.
 //
-// Model: counts -> q[s] = max(1, floor(count * 2^15 / N)) for seen symbols,
+// Model: counts -> q[s] = max(1, floor(count * 2^13 / N)) for seen symbols,
 // 0 for unseen; the deficit goes to the most frequent symbol, an excess is
 // removed from the largest entries. Integer only, identical on both sides;
 // every encode and decode block builds it from the 256 counts it is given.
@@ -35,8 +37,10 @@
 namespace kvf {
 namespace {
 
-constexpr int kWarpsPerBlock = 4;  // encoder: chunks per block
-constexpr int kDecWarps = 2;       // decoder: chunks per block
+constexpr int kEncWarps = 2;  // encoder: chunks per block
+constexpr int kDecWarps = 2;       // decoder: chunks per block (one slot table per block)
+constexpr int kDecBlockWarps = 8;  // every warp builds the slot tables; the extra ones then exit
+constexpr uint32_t kShift = 32 - kRansProbBits;  // a state >= q << kShift renormalises first
 
 // cp.async helpers: asynchronous global -> shared copies, many in flight per thread
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
@@ -52,53 +56,57 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
 
-// exclusive prefix sum of one value per thread over a block of blockDim.x threads
-template <typename T>
-__device__ __forceinline__ T block_exclusive_scan(T v, T* warp_tot, T* total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  T incl = v;
+// warp-wide copy of [src, src + bytes) to shared memory at dst, where dst and
+// src agree modulo 16 and both are 4-byte aligned: 16-byte copies for the
+// aligned body, 4-byte copies for the ends
+__device__ __forceinline__ void warp_stage(uint8_t* dst, const uint8_t* src, uint32_t bytes, int lane) {
+  const uint32_t head = std::min<uint32_t>((16u - (uint32_t)(reinterpret_cast<uintptr_t>(src) & 15u)) & 15u, bytes);
+  const uint32_t body = (bytes - head) & ~15u;
+  if ((uint32_t)lane < head / 4) cp_async4(dst + 4 * lane, src + 4 * lane);
+  for (uint32_t j = 16 * lane; j < body; j += 16 * 32) cp_async16(dst + head + j, src + head + j);
+  const uint32_t tail = head + body;
+  for (uint32_t j = tail + 4 * lane; j < bytes; j += 4 * 32) cp_async4(dst + j, src + j);
+}
+
+// inclusive prefix sum over the 32 lanes of a warp
+__device__ __forceinline__ uint32_t warp_inclusive_scan(uint32_t v, int lane) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const T u = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += u;
+    const uint32_t u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
   }
-  if (lane == 31) warp_tot[w] = incl;
-  __syncthreads();
-  if (w == 0) {
-    T t = (lane < nw) ? warp_tot[lane] : T(0);
-    T ti = t;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const T u = __shfl_up_sync(0xffffffffu, ti, o);
-      if (lane >= o) ti += u;
-    }
-    if (lane < nw) warp_tot[lane] = ti - t;
-    if (lane == nw - 1) *total = ti;
-  }
-  __syncthreads();
-  return warp_tot[w] + incl - v;
+  return v;
 }
 
 // The model (q, cum) built by a whole block from the 256 counts, identical to
-// the CPU mirror's: q = max(1, floor(count * 2^15 / N)) for
-// seen symbols; the deficit goes to the most frequent symbol (lowest index on
-// ties); an excess is removed from the largest entries. Returns false (on
-// every thread) when the counts admit no model.
+// the CPU mirror's: q = max(1, floor(count * 2^13 / N)) for seen symbols; the
+// deficit goes to the most frequent symbol (lowest index on ties); an excess
+// is removed from the largest entries. Returns false (on every thread) when
+// the counts admit no model. Sums and the arg-max use warp shuffles; the
+// quotients come from one double reciprocal of N, corrected to the exact
+// floor with integer products.
 struct ModelSmem {
-  unsigned long long N, best;
-  uint32_t S;
+  unsigned long long wsum[32], wkey[32];
+  uint32_t wq[32];
   int bad;
 };
 
-__device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint32_t* cum, ModelSmem& ms) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  if (tid == 0) {
-    ms.N = 0ull;
-    ms.best = 0ull;
-    ms.S = 0u;
-    ms.bad = 0;
+__device__ __forceinline__ unsigned long long warp_sum64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_max64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
   }
-  __syncthreads();
+  return v;
+}
+
+__device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint32_t* cum, ModelSmem& ms) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, w = tid >> 5, nw = (nt + 31) >> 5;
   unsigned long long n = 0ull, key = 0ull;
   for (int s = tid; s < 256; s += nt) {
     const uint32_t f = freq[s];
@@ -107,27 +115,43 @@ __device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint
     const unsigned long long k = ((unsigned long long)f << 8) | (unsigned long long)(255 - s);
     key = k > key ? k : key;
   }
-  atomicAdd(&ms.N, n);
-  atomicMax(&ms.best, key);
+  n = warp_sum64(n);
+  key = warp_max64(key);
+  if (lane == 0) {
+    ms.wsum[w] = n;
+    ms.wkey[w] = key;
+  }
   __syncthreads();
-  const unsigned long long N = ms.N;
+  unsigned long long N = 0ull, best = 0ull;
+  for (int i = 0; i < nw; ++i) {
+    N += ms.wsum[i];
+    best = ms.wkey[i] > best ? ms.wkey[i] : best;
+  }
   if (N == 0ull) return false;
+  const double inv = 1.0 / (double)N;
   uint32_t ssum = 0;
   for (int s = tid; s < 256; s += nt) {
     const uint32_t f = q[s];
     uint32_t qs = 0;
     if (f) {
-      const unsigned long long v = ((unsigned long long)f * kRansM) / N;
+      // floor(t / N) for t = f * 2^13 < 2^45: the double estimate is off by at most one
+      const unsigned long long t = (unsigned long long)f * kRansM;
+      unsigned long long v = (unsigned long long)((double)t * inv);
+      if (v * N > t) --v;
+      else if ((v + 1) * N <= t) ++v;
       qs = (uint32_t)(v < 1ull ? 1ull : v);
     }
     q[s] = qs;
     ssum += qs;
   }
-  atomicAdd(&ms.S, ssum);
+  ssum = (uint32_t)warp_sum64(ssum);
+  if (lane == 0) ms.wq[w] = ssum;
   __syncthreads();
   if (tid == 0) {
-    unsigned long long S = ms.S;
-    const int argmax = 255 - (int)(ms.best & 0xFF);
+    unsigned long long S = 0;
+    for (int i = 0; i < nw; ++i) S += ms.wq[i];
+    const int argmax = 255 - (int)(best & 0xFF);
+    ms.bad = 0;
     if (S < kRansM) {
       q[argmax] += (uint32_t)(kRansM - S);
     } else {
@@ -152,13 +176,7 @@ __device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint
       loc[k] = sum;
       sum += q[8 * tid + k];
     }
-    uint32_t incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
-      if (tid >= o) incl += u;
-    }
-    const uint32_t base = incl - sum;
+    const uint32_t base = warp_inclusive_scan(sum, tid) - sum;
 #pragma unroll
     for (int k = 0; k < 8; ++k) cum[8 * tid + k] = base + loc[k];
   }
@@ -166,24 +184,91 @@ __device__ bool build_model(const uint32_t* __restrict__ freq, uint32_t* q, uint
   return true;
 }
 
-// One warp per chunk. The chunk's symbols are staged in shared memory with
-// asynchronous copies; the loop is software-pipelined so that the next step's
-// symbol and model entries are loaded while the current state is updated.
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8_t* __restrict__ data,
-                                                                   uint64_t n, uint32_t chunk,
-                                                                   const uint32_t* __restrict__ freq,
-                                                                   uint8_t* __restrict__ slots,
-                                                                   uint64_t nchunks,
-                                                                   unsigned* __restrict__ status) {
-  extern __shared__ __align__(16) uint8_t sbuf[];  // [warps][chunk]
-  __shared__ uint32_t q[256], cum[256], rcp[256];
+// Encoder shared memory per warp: the chunk's symbols, then one word region
+// per lane. A region holds at least one word per step; its length is an odd
+// number of 4-byte words so that lanes writing at equal positions fall in
+// different banks.
+__host__ __device__ inline uint32_t enc_region_words(uint32_t chunk) {
+  uint32_t m = (chunk / kRansLanes + 1) / 2;
+  if ((m & 1u) == 0) ++m;
+  return 2 * m;
+}
+__host__ __device__ inline size_t enc_warp_smem(uint32_t chunk) {
+  return (size_t)chunk + 2 * (size_t)kRansLanes * enc_region_words(chunk);
+}
+
+// Chunk offsets come from a decoupled look-back over one status word per
+// chunk (zeroed before the launch): flag in the top two bits (1: the chunk's
+// payload size, 2: the inclusive prefix of payload sizes), value below. A warp
+// publishes its size, then reads its predecessors' words 32 at a time, adding
+// sizes back to the nearest published prefix. Predecessors of a chunk belong
+// to earlier or the same block, and blocks start in index order, so the wait
+// ends; it is bounded all the same, and a warp that gives up reports a device
+// timeout instead of writing.
+constexpr unsigned long long kLbSize = 1ull << 62, kLbPrefix = 2ull << 62, kLbValue = (1ull << 62) - 1;
+constexpr uint32_t kLbSpinLimit = 1u << 16;
+
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// bytes of the payloads before chunk c (c > 0); false when the wait gave up
+__device__ bool look_back(unsigned long long* lb, uint64_t c, unsigned* status, int lane,
+                          unsigned long long& prefix) {
+  prefix = 0ull;
+  int64_t top = (int64_t)c - 1;
+  uint32_t spins = 0;
+  while (true) {
+    const int64_t idx = top - lane;
+    const unsigned long long v = idx >= 0 ? ld_acquire(lb + idx) : kLbPrefix;  // before chunk 0: prefix 0
+    const unsigned flag = (unsigned)(v >> 62);
+    const unsigned pre = __ballot_sync(0xffffffffu, flag == 2u);
+    const unsigned empty = __ballot_sync(0xffffffffu, flag == 0u);
+    const int pl = pre ? __ffs(pre) - 1 : 31;  // the window ends at the nearest prefix
+    const unsigned used = pl == 31 ? 0xffffffffu : ((2u << pl) - 1u);
+    if (empty & used) {  // a predecessor has not published yet
+      if (++spins > kLbSpinLimit || (*reinterpret_cast<volatile unsigned*>(status) & kDevErrTimeout)) return false;
+      __nanosleep(64);
+      continue;
+    }
+    prefix += warp_sum64((unsigned)lane <= (unsigned)pl ? (v & kLbValue) : 0ull);
+    if (pre) return true;
+    top -= 32;
+    spins = 0;
+  }
+}
+
+// One warp per chunk, one lane stream per thread. The chunk's symbols are
+// staged in shared memory; each lane encodes its steps from last to first,
+// writing renormalisation words backwards into its region. The warp then
+// finds its payload's offset by look-back and writes the payload (states,
+// counts, lane streams one after another) straight into the container; the
+// last chunk writes the container header and length.
+__global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(const uint8_t* __restrict__ data,
+                                                               uint64_t n, uint32_t chunk,
+                                                               const uint32_t* __restrict__ freq,
+                                                               unsigned long long* __restrict__ lb,
+                                                               uint8_t* __restrict__ out,
+                                                               uint64_t* __restrict__ out_len,
+                                                               uint64_t nchunks,
+                                                               unsigned* __restrict__ status) {
+  extern __shared__ __align__(16) uint8_t sbuf[];
+  __shared__ uint32_t q[256], cum[256], qc[256], rcp[256];
   __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t c = (uint64_t)blockIdx.x * kWarpsPerBlock + w;
+  const uint64_t c = (uint64_t)blockIdx.x * kEncWarps + w;
   const bool live = c < nchunks;
   const uint64_t start = live ? c * chunk : 0;
   const uint32_t nsym = live ? (uint32_t)((n - start < chunk) ? (n - start) : chunk) : 0;
-  uint8_t* buf = sbuf + (size_t)w * chunk;
+  uint8_t* buf = sbuf + (size_t)w * enc_warp_smem(chunk);
+  const uint32_t RS = enc_region_words(chunk);
+  uint16_t* words = reinterpret_cast<uint16_t*>(buf + chunk);  // this warp's regions
+  uint16_t* region = words + (size_t)lane * RS;
   if (live) {
     const bool vec = (reinterpret_cast<uintptr_t>(data + start) & 15u) == 0;
     const uint32_t n16 = vec ? nsym / 16 : 0;
@@ -192,7 +277,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
   }
   // the model is built while the symbols are in flight
   const bool model_ok = build_model(freq, q, cum, ms);
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) rcp[i] = q[i] ? 0xFFFFFFFFu / q[i] : 0u;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    qc[i] = q[i] | (cum[i] << 16);
+    rcp[i] = q[i] ? 0xFFFFFFFFu / q[i] : 0u;
+  }
   cp_async_wait_all();
   __syncthreads();
   if (!model_ok) {
@@ -201,148 +289,170 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_rans_encode(const uint8
   }
   if (!live) return;
 
-  uint8_t* slot = slots + c * rans_slot_bytes(chunk);
-  uint16_t* words = reinterpret_cast<uint16_t*>(slot + kRansChunkHeader);
-  const uint32_t capw = chunk + 2;
-  uint32_t pos = capw;  // words are written backwards, ending at capw
-  uint32_t x = kRansL;
-  const uint32_t steps = (nsym + 31) / 32;
-  const unsigned above_mask = ~((2u << lane) - 1u);  // emitting lanes above this one
-  // one encoding step for a lane holding symbol entry (f, cu, rc); `act`
-  // false leaves the state alone (only the last step can be partial)
-  auto step = [&](bool act, uint32_t f, uint32_t cu, uint32_t rc) {
-    const bool need = act && (x >> 17) >= f;  // x >= f * 2^17
-    const unsigned mask = __ballot_sync(0xffffffffu, need);
-    if (need) words[pos - 1 - __popc(mask & above_mask)] = (uint16_t)(x & 0xFFFFu);
-    pos -= __popc(mask);
+  uint32_t x = kRansL, pos = RS;
+  // renormalise (at most one word), then x -> (x / f) * M + x % f + cum; the
+  // quotient comes from the reciprocal floor((2^32 - 1) / f), low by at most one
+  auto step = [&](uint32_t e, uint32_t rc) {
+    const uint32_t f = e & 0xFFFFu;
+    const bool need = (x >> kShift) >= f;
+    if (need) region[pos - 1] = (uint16_t)(x & 0xFFFFu);
+    pos -= need ? 1u : 0u;
     const uint32_t xs = need ? (x >> 16) : x;
     uint32_t qq = __umulhi(xs, rc);
     uint32_t r = xs - qq * f;
     const bool fix = r >= f;
     qq += fix ? 1u : 0u;
     r -= fix ? f : 0u;
-    x = act ? (qq << kRansProbBits) + r + cu : x;
+    x = (qq << kRansProbBits) + r + (e >> 16);
   };
-  // last (possibly partial) step
-  {
+  const uint32_t steps = (nsym + 31) / 32;
+  {  // last (possibly partial) step
     const uint32_t i = (steps - 1) * 32 + lane;
-    const bool act = i < nsym;
-    const uint32_t s = act ? buf[i] : 0u;
-    step(act, q[s], cum[s], rcp[s]);
+    if (i < nsym) {
+      const uint32_t s = buf[i];
+      step(qc[s], rcp[s]);
+    }
   }
-  // full steps, software-pipelined: the next step's model entries load while
-  // the current state updates
-  if (steps >= 2) {
+  if (steps >= 2) {  // full steps; the next step's model entries load one step ahead
     uint32_t s = buf[(steps - 2) * 32 + lane];
-    uint32_t f = q[s], cu = cum[s], rc = rcp[s];
+    uint32_t e = qc[s], rc = rcp[s];
+#pragma unroll 4
     for (uint32_t st = steps - 1; st-- > 0;) {
-      const uint32_t f0 = f, c0 = cu, r0 = rc;
-      if (st > 0) {
-        s = buf[(st - 1) * 32 + lane];
-        f = q[s];
-        cu = cum[s];
-        rc = rcp[s];
-      }
-      step(true, f0, c0, r0);
+      const uint32_t e0 = e, r0 = rc;
+      s = buf[(st > 0 ? st - 1 : 0) * 32 + lane];
+      e = qc[s];
+      rc = rcp[s];
+      step(e0, r0);
     }
   }
-  uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
-  hdr[1 + lane] = x;
-  if (lane == 0) hdr[0] = capw - pos;
-}
 
-// header + offsets: one block scans the chunk payload sizes
-__global__ void __launch_bounds__(1024) k_rans_offsets(const uint8_t* __restrict__ slots, uint64_t n,
-                                                       uint32_t chunk, uint64_t nchunks,
-                                                       uint8_t* __restrict__ out,
-                                                       uint64_t* __restrict__ out_len) {
-  __shared__ unsigned long long wtot[32], total;
-  const uint64_t per = (nchunks + blockDim.x - 1) / blockDim.x;
-  const uint64_t c0 = threadIdx.x * per;
-  const uint64_t c1 = (c0 + per < nchunks) ? c0 + per : nchunks;
-  const size_t sb = rans_slot_bytes(chunk);
-  unsigned long long local = 0;
-  for (uint64_t c = c0; c < c1; ++c) {
-    const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
-    local += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
+  // payload layout: lane streams one after another, in decoding order; the
+  // warp copies one lane's stream at a time with coalesced 2-byte stores
+  const uint32_t cnt = RS - pos;
+  const uint32_t incl = warp_inclusive_scan(cnt, lane);
+  const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const unsigned long long pbytes = kRansPayloadHeader + 2ull * total + 2ull * (total & 1u);
+  unsigned long long prefix = 0ull;
+  if (c == 0) {
+    if (lane == 0) st_release(lb, kLbPrefix | pbytes);
+  } else {
+    if (lane == 0) st_release(lb + c, kLbSize | pbytes);
+    if (!look_back(lb, c, status, lane, prefix)) {
+      if (lane == 0) atomicOr(status, kDevErrTimeout);
+      return;
+    }
+    if (lane == 0) st_release(lb + c, kLbPrefix | (prefix + pbytes));
   }
-  const unsigned long long excl = block_exclusive_scan<unsigned long long>(local, wtot, &total);
   const uint64_t hdr = kRansHeader + 4ull * (nchunks + 1);
-  uint32_t* off = reinterpret_cast<uint32_t*>(out + kRansHeader);
-  uint64_t run = hdr + excl;
-  for (uint64_t c = c0; c < c1; ++c) {
-    off[c] = (uint32_t)run;
-    const uint32_t nw = *reinterpret_cast<const uint32_t*>(slots + c * sb);
-    run += kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u);
-  }
-  if (threadIdx.x == 0) {
-    const uint64_t len = hdr + total;
-    off[nchunks] = (uint32_t)len;
-    *out_len = len;
-    uint32_t* h = reinterpret_cast<uint32_t*>(out);
-    h[0] = kRansMagic;
-    h[1] = kRansProbBits;
-    h[2] = kRansLanes;
-    h[3] = chunk;
-    h[4] = (uint32_t)(n & 0xFFFFFFFFull);
-    h[5] = (uint32_t)(n >> 32);
-    h[6] = (uint32_t)nchunks;
-    h[7] = (uint32_t)hdr;
-  }
-}
-
-// one block per chunk: copy nwords, states and words into place
-__global__ void __launch_bounds__(256) k_rans_compact(const uint8_t* __restrict__ slots, uint32_t chunk,
-                                                      uint8_t* __restrict__ out) {
-  const uint64_t c = blockIdx.x;
-  const uint8_t* slot = slots + c * rans_slot_bytes(chunk);
-  const uint32_t* off = reinterpret_cast<const uint32_t*>(out + kRansHeader);
-  uint8_t* dst = out + off[c];
-  const uint32_t* shdr = reinterpret_cast<const uint32_t*>(slot);
-  const uint32_t nw = shdr[0];
-  uint32_t* dhdr = reinterpret_cast<uint32_t*>(dst);
-  for (int i = threadIdx.x; i < 1 + (int)kRansLanes; i += blockDim.x) dhdr[i] = shdr[i];
-  const uint16_t* sw = reinterpret_cast<const uint16_t*>(slot + kRansChunkHeader) + (chunk + 2 - nw);
-  uint16_t* dw = reinterpret_cast<uint16_t*>(dst + kRansChunkHeader);
-  // eight independent loads in flight per thread
-  for (uint32_t i0 = threadIdx.x; i0 < nw; i0 += blockDim.x * 8) {
-    uint16_t v[8];
+  const uint64_t off = hdr + prefix;
+  uint32_t* offs = reinterpret_cast<uint32_t*>(out + kRansHeader);
+  uint8_t* pay = out + off;
+  reinterpret_cast<uint32_t*>(pay)[lane] = x;
+  reinterpret_cast<uint16_t*>(pay + 4 * kRansLanes)[lane] = (uint16_t)cnt;
+  uint16_t* dstw = reinterpret_cast<uint16_t*>(pay + kRansPayloadHeader);
+  for (int l = 0; l < 32; ++l) {
+    const uint32_t cl = __shfl_sync(0xffffffffu, cnt, l);
+    const uint32_t el = __shfl_sync(0xffffffffu, incl, l) - cl;
+    const uint16_t* src = words + (size_t)l * RS + (RS - cl);
+    for (uint32_t j0 = lane; j0 < cl; j0 += 8 * 32) {  // eight loads in flight per lane
+      uint16_t v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t i = i0 + k * blockDim.x;
-      v[k] = (i < nw) ? sw[i] : (uint16_t)0;
-    }
+      for (int k = 0; k < 8; ++k) v[k] = (j0 + 32 * k < cl) ? src[j0 + 32 * k] : (uint16_t)0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t i = i0 + k * blockDim.x;
-      if (i < nw) dw[i] = v[k];
+      for (int k = 0; k < 8; ++k)
+        if (j0 + 32 * k < cl) dstw[el + j0 + 32 * k] = v[k];
     }
   }
-  if ((nw & 1u) && threadIdx.x == 0) dw[nw] = 0;
+  if (lane == 0) {
+    if (total & 1u) dstw[total] = 0;
+    offs[c] = (uint32_t)off;
+    if (c == nchunks - 1) {
+      const uint64_t len = off + pbytes;
+      offs[nchunks] = (uint32_t)len;
+      *out_len = len;
+      uint32_t* h = reinterpret_cast<uint32_t*>(out);
+      h[0] = kRansMagic;
+      h[1] = kRansProbBits;
+      h[2] = kRansLanes;
+      h[3] = chunk;
+      h[4] = (uint32_t)(n & 0xFFFFFFFFull);
+      h[5] = (uint32_t)(n >> 32);
+      h[6] = (uint32_t)nchunks;
+      h[7] = (uint32_t)hdr;
+    }
+  }
 }
 
 __device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
   return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// One warp per chunk. Each block builds the model from the 256 counts and
-// two per-slot tables in shared memory: ent[slot] = q | (slot - cum) << 16
-// (the only lookup on the state's critical path) and sym[slot] (for the
-// output byte). The chunk's renormalisation words are staged in shared memory
-// with asynchronous 4-byte copies (chunks with more words than the staging
-// buffer read them from global memory instead).
-constexpr uint32_t kDecStage = 16384;  // words staged per decoding warp (a power of two)
+// Decodes one chunk whose payload (pay_bytes at pay, 4-byte aligned, already
+// checked to be at least the payload header) sits in shared or global memory.
+// Lane l reads its own stream; its next word is loaded one step before it can
+// be needed, at an index clamped to the lane's stream, so a corrupt count
+// reads nothing outside the payload. Returns true when the chunk is malformed.
+template <bool FULL_ONLY>
+__device__ __forceinline__ bool decode_chunk(const uint8_t* pay, uint32_t pay_bytes, const uint32_t* ent,
+                                             const uint8_t* sym, uint32_t nsym, uint8_t* __restrict__ o,
+                                             int lane) {
+  uint32_t x = reinterpret_cast<const uint32_t*>(pay)[lane];
+  const uint32_t cnt = reinterpret_cast<const uint16_t*>(pay + 4 * kRansLanes)[lane];
+  const uint32_t incl = warp_inclusive_scan(cnt, lane);
+  const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+  if ((uint32_t)kRansPayloadHeader + 2u * total + 2u * (total & 1u) != pay_bytes) return true;
+  bool bad = x < kRansL;
+  // this lane's stream; a lane without words points at the payload start,
+  // whose words it reads but never uses unless the chunk is corrupt
+  const uint16_t* wl = cnt ? reinterpret_cast<const uint16_t*>(pay + kRansPayloadHeader) + (incl - cnt)
+                           : reinterpret_cast<const uint16_t*>(pay);
+  const uint32_t last = cnt ? cnt - 1 : 0;
+  uint32_t k = 0;
+  uint32_t wn = wl[0];
+  const uint32_t full = nsym / 32;
+#pragma unroll 4
+  for (uint32_t st = 0; st < full; ++st) {
+    const uint32_t slot = x & (kRansM - 1);
+    const uint32_t e = ent[slot];
+    o[32 * st] = sym[slot];
+    x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+    const bool need = x < kRansL;
+    x = need ? ((x << 16) | wn) : x;
+    k += need ? 1u : 0u;
+    wn = wl[min(k, last)];
+  }
+  if (!FULL_ONLY && full * 32 < nsym) {  // last, partial step
+    if (full * 32 + lane < nsym) {
+      const uint32_t slot = x & (kRansM - 1);
+      const uint32_t e = ent[slot];
+      o[32 * full] = sym[slot];
+      x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+      if (x < kRansL) {
+        x = (x << 16) | wn;
+        ++k;
+      }
+    }
+  }
+  bad = bad || x != kRansL || k != cnt;
+  return __any_sync(0xffffffffu, bad);
+}
 
-__global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
+// Decoder shared memory: the slot tables ent[slot] = q | (slot - cum) << 16 and
+// sym[slot], then one staging buffer per warp holding a chunk payload of the
+// default chunk size (with 16 bytes of alignment slack); payloads of larger
+// chunks are read from global memory in place.
+constexpr uint32_t kDecStageBytes = (uint32_t)kRansPayloadHeader + 2u * kRansChunk + 32u;
+constexpr size_t kDecSmem = 5 * (size_t)kRansM + (size_t)kDecWarps * kDecStageBytes;
+
+__global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
                                                               uint64_t comp_len_host,
                                                               const uint64_t* __restrict__ comp_len_dev,
                                                               const uint32_t* __restrict__ freq,
                                                               uint64_t n, uint8_t* __restrict__ out,
                                                               unsigned* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t dsm[];
-  uint32_t* ent = reinterpret_cast<uint32_t*>(dsm);                     // [2^15]
-  uint8_t* sym = dsm + 4 * kRansM;                                      // [2^15]
-  uint16_t* wstage = reinterpret_cast<uint16_t*>(dsm + 5 * kRansM);    // [kDecWarps][kDecStage]
+  uint32_t* ent = reinterpret_cast<uint32_t*>(dsm);  // [2^13]
+  uint8_t* sym = dsm + 4 * kRansM;                   // [2^13]
   __shared__ uint32_t q[256], cum[256];
   __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -350,31 +460,50 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
     if (threadIdx.x == 0) atomicOr(status, kDevErrEntropy);
     return;
   }
-  {  // per-slot tables: each thread fills a contiguous slot range, walking symbols
-    const uint32_t per = kRansM / blockDim.x;
-    const uint32_t k0 = threadIdx.x * per;
-    int lo = 0, hi = 255;
+  {  // slot tables: mark the first slot of every coded symbol in sym[], then
+     // each warp turns a contiguous span of marks into both tables, a lane
+     // taking four consecutive slots per round (16-byte rows, no bank
+     // conflicts); the symbol of a slot is the last mark at or before it
+    for (uint32_t i = threadIdx.x; i < kRansM / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(sym)[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    for (int s = threadIdx.x; s < 256; s += blockDim.x)
+      if (q[s]) sym[cum[s]] = (uint8_t)s;
+    __syncthreads();
+    const uint32_t span = kRansM / (blockDim.x >> 5), lo_k = (uint32_t)w * span;
+    int lo = 0, hi = 255;  // symbol of the span's first slot: the last s with cum[s] <= lo_k
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (cum[mid] <= k0) lo = mid; else hi = mid - 1;
+      if (cum[mid] <= lo_k) lo = mid; else hi = mid - 1;
     }
-    int s = lo;
-    for (uint32_t k = k0; k < k0 + per; k += 4) {
-      uint32_t sw = 0;
-      uint4 e4;
-      uint32_t* e = &e4.x;
+    uint32_t carry = (uint32_t)lo;
+    const unsigned below = (1u << lane) - 1u;
+    for (uint32_t k0 = lo_k; k0 < lo_k + span; k0 += 128) {
+      const uint32_t k = k0 + 4 * lane;
+      const uint32_t m4 = *reinterpret_cast<const uint32_t*>(sym + k);
+      // the last mark among this lane's four slots (marks increase with the slot)
+      const uint32_t mlast = (m4 >> 24) ? (m4 >> 24) : (m4 >> 16) & 0xFFu ? (m4 >> 16) & 0xFFu
+                           : (m4 >> 8) & 0xFFu ? (m4 >> 8) & 0xFFu : m4 & 0xFFu;
+      const unsigned has = __ballot_sync(0xffffffffu, m4 != 0u);
+      const unsigned prev = has & below;
+      const uint32_t from = __shfl_sync(0xffffffffu, mlast, prev ? 31 - __clz(prev) : 0);
+      uint32_t v = prev ? from : carry;
+      uint32_t e[4], sw = 0;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const uint32_t kk = k + b;
-        while (cum[s] + q[s] <= kk) ++s;
-        e[b] = q[s] | ((kk - cum[s]) << 16);
-        sw |= (uint32_t)s << (8 * b);
+        const uint32_t mb = (m4 >> (8 * b)) & 0xFFu;
+        v = mb ? mb : v;
+        e[b] = q[v] | ((k + b - cum[v]) << 16);
+        sw |= v << (8 * b);
       }
-      *reinterpret_cast<uint4*>(ent + k) = e4;
+      carry = __shfl_sync(0xffffffffu, v, 31);
+      *reinterpret_cast<uint4*>(ent + k) = make_uint4(e[0], e[1], e[2], e[3]);
       *reinterpret_cast<uint32_t*>(sym + k) = sw;
     }
   }
   __syncthreads();
+  if (w >= kDecWarps) return;
+  uint8_t* stage = dsm + 5 * kRansM + (size_t)w * kDecStageBytes;
   const uint64_t comp_len = comp_len_dev ? *comp_len_dev : comp_len_host;
   // header checks (every warp reads the same 32 bytes)
   if (comp_len < kRansHeader) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
@@ -383,118 +512,58 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const uint64_t nchunks = rd32(comp + 24);
   const uint64_t hdr = kRansHeader + 4ull * (nchunks + 1);
   const bool hdr_ok = rd32(comp) == kRansMagic && rd32(comp + 4) == kRansProbBits &&
-                      rd32(comp + 8) == kRansLanes && chunk != 0 && (chunk % 32) == 0 && nn == n &&
-                      nchunks == (n + chunk - 1) / chunk && rd32(comp + 28) == hdr && hdr <= comp_len &&
+                      rd32(comp + 8) == kRansLanes && chunk != 0 && (chunk % 32) == 0 &&
+                      chunk <= kRansMaxChunk && nn == n && nchunks == (n + chunk - 1) / chunk &&
+                      rd32(comp + 28) == hdr && hdr <= comp_len &&
                       rd32(comp + kRansHeader + 4 * nchunks) == comp_len;
   if (!hdr_ok) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }
-  uint16_t* stage = wstage + (size_t)w * kDecStage;
   const uint64_t nwarps = (uint64_t)gridDim.x * kDecWarps;
   for (uint64_t c = (uint64_t)blockIdx.x * kDecWarps + w; c < nchunks; c += nwarps) {
     const uint64_t off = rd32(comp + kRansHeader + 4 * c);
     const uint64_t end = rd32(comp + kRansHeader + 4 * (c + 1));
-    if (off < hdr || end > comp_len || end < off + kRansChunkHeader || (off & 3u)) {
+    if (off < hdr || end > comp_len || end < off + kRansPayloadHeader || ((off | end) & 3u)) {
       if (lane == 0) atomicOr(status, kDevErrCorrupt);
       continue;
     }
-    const uint32_t nw = rd32(comp + off);
-    if (off + kRansChunkHeader + 2ull * nw + 2ull * (nw & 1u) != end) {
-      if (lane == 0) atomicOr(status, kDevErrCorrupt);
-      continue;
-    }
-    uint32_t x = rd32(comp + off + 4 + 4 * lane);
-    bool bad = x < kRansL;
+    const uint32_t pay_bytes = (uint32_t)(end - off);
     const uint64_t start = c * chunk;
     const uint32_t nsym = (uint32_t)((n - start < chunk) ? (n - start) : chunk);
-    const uint32_t full = nsym / 32;  // steps with every lane active
     uint8_t* o = out + start + lane;
-    const uint32_t lt = (1u << lane) - 1u;
-    uint32_t p = 0;
-    if (nw <= kDecStage) {
-      // stage pairs of words (the payload is padded to 4 bytes); indices are
-      // masked into the staging buffer, so even a corrupt stream reads inside
-      // it, and the end-of-chunk checks reject it
-      const uint32_t npair = (nw + 1) / 2;
-      const uint8_t* src = comp + off + kRansChunkHeader;
-      for (uint32_t j = lane; j < npair; j += 32) cp_async4(stage + 2 * j, src + 4 * j);
+    const uint32_t mis = (uint32_t)(reinterpret_cast<uintptr_t>(comp + off) & 15u);
+    bool bad;
+    if (mis + pay_bytes <= kDecStageBytes) {
+      __syncwarp();  // the previous chunk's reads of the staging buffer are done
+      warp_stage(stage + mis, comp + off, pay_bytes, lane);
       cp_async_wait_all();
       __syncwarp();
-      for (uint32_t st = 0; st < full; ++st) {
-        const uint32_t slot = x & (kRansM - 1);
-        const uint32_t e = ent[slot];
-        x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
-        o[32 * st] = sym[slot];
-        const bool need = x < kRansL;
-        const unsigned mask = __ballot_sync(0xffffffffu, need);
-        const uint32_t w16 = stage[(p + __popc(mask & lt)) & (kDecStage - 1)];
-        x = need ? ((x << 16) | w16) : x;
-        p += __popc(mask);
-      }
-      if (full * 32 < nsym) {  // last, partial step
-        const bool active = full * 32 + lane < nsym;
-        const uint32_t slot = x & (kRansM - 1);
-        const uint32_t e = ent[slot];
-        if (active) {
-          x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
-          o[32 * full] = sym[slot];
-        }
-        const bool need = active && x < kRansL;
-        const unsigned mask = __ballot_sync(0xffffffffu, need);
-        const uint32_t w16 = stage[(p + __popc(mask & lt)) & (kDecStage - 1)];
-        x = need ? ((x << 16) | w16) : x;
-        p += __popc(mask);
-      }
-      bad = bad || p > nw;
-    } else {  // words read from global memory, every index checked
-      const uint16_t* words = reinterpret_cast<const uint16_t*>(comp + off + kRansChunkHeader);
-      const uint32_t steps = (nsym + 31) / 32;
-      for (uint32_t st = 0; st < steps; ++st) {
-        const bool active = st * 32 + lane < nsym;
-        const uint32_t slot = x & (kRansM - 1);
-        const uint32_t e = ent[slot];
-        if (active) {
-          x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
-          o[32 * st] = sym[slot];
-        }
-        const bool need = active && x < kRansL;
-        const unsigned mask = __ballot_sync(0xffffffffu, need);
-        const uint32_t idx = p + __popc(mask & lt);
-        if (need) {
-          if (idx < nw) x = (x << 16) | words[idx];
-          else { bad = true; x = kRansL; }
-        }
-        p += __popc(mask);
-      }
+      bad = (nsym % 32 == 0) ? decode_chunk<true>(stage + mis, pay_bytes, ent, sym, nsym, o, lane)
+                             : decode_chunk<false>(stage + mis, pay_bytes, ent, sym, nsym, o, lane);
+    } else {
+      bad = decode_chunk<false>(comp + off, pay_bytes, ent, sym, nsym, o, lane);
     }
-    bad = bad || x != kRansL || p != nw;
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, kDevErrCorrupt);
-    __syncwarp();
+    if (bad && lane == 0) atomicOr(status, kDevErrCorrupt);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
-                               uint8_t* slots, unsigned* status, cudaStream_t st) {
+                               unsigned long long* lookback, uint8_t* out, uint64_t* out_len, unsigned* status,
+                               cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  if (chunk == 0 || chunk % kRansLanes || chunk > kRansMaxChunk) return cudaErrorInvalidValue;
+  if (!aligned(out, 4)) return cudaErrorInvalidValue;
   const size_t nc = rans_num_chunks(n, chunk);
-  const size_t smem = (size_t)kWarpsPerBlock * chunk;
+  const size_t smem = (size_t)kEncWarps * enc_warp_smem(chunk);
   if (smem > kSmemOptIn) {
     cudaError_t e = cudaFuncSetAttribute(k_rans_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  const unsigned grid = (unsigned)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  k_rans_encode<<<grid, kWarpsPerBlock * 32, smem, st>>>(data, n, chunk, freq, slots, nc, status);
+  cudaError_t e = cudaMemsetAsync(lookback, 0, nc * sizeof(unsigned long long), st);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)((nc + kEncWarps - 1) / kEncWarps);
+  k_rans_encode<<<grid, kEncWarps * 32, smem, st>>>(data, n, chunk, freq, lookback, out, out_len, nc, status);
   note_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rans_assemble(const uint8_t* slots, size_t n, uint32_t chunk, uint8_t* out,
-                                 uint64_t* out_len, cudaStream_t st) {
-  if (n == 0) return cudaSuccess;
-  const size_t nc = rans_num_chunks(n, chunk);
-  k_rans_offsets<<<1, 1024, 0, st>>>(slots, n, chunk, nc, out, out_len);
-  k_rans_compact<<<(unsigned)nc, 256, 0, st>>>(slots, chunk, out);
-  note_launches(2);
   return cudaGetLastError();
 }
 
@@ -502,14 +571,15 @@ cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint6
                                const uint32_t* freq, size_t n, uint8_t* out, unsigned* status,
                                cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  if (!aligned(comp, 4)) return cudaErrorInvalidValue;  // payloads are read as 4-byte words
   // the grid is sized for the encoder's default chunk size; warps loop over
   // chunks, so a container with any chunk size named in its header decodes
   const size_t nc = rans_num_chunks(n, kRansChunk);
   const unsigned grid = (unsigned)((nc + kDecWarps - 1) / kDecWarps);
-  const size_t smem = 5 * (size_t)kRansM + (size_t)kDecWarps * kDecStage * 2;
-  const cudaError_t e = cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const cudaError_t e =
+      cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecSmem);
   if (e != cudaSuccess) return e;
-  k_rans_decode<<<grid, kDecWarps * 32, smem, st>>>(comp, comp_len, comp_len_dev, freq, n, out, status);
+  k_rans_decode<<<grid, kDecBlockWarps * 32, kDecSmem, st>>>(comp, comp_len, comp_len_dev, freq, n, out, status);
   note_launches(1);
   return cudaGetLastError();
 }

@@ -393,34 +393,37 @@ int orc_reconstruct(const float* projected, size_t H, size_t T, size_t R, size_t
 
 /* -------------------------------------------------------------------------
  * Entropy coding. The histogram follows entropy.rs:24-31. The coder is this
- * project's chunked, 32-lane interleaved rANS container (the reference's
- * single-stream constriction coder, entropy.rs:55-73, is not reproducible):
+ * project's chunked rANS container with 32 independent lane streams per chunk
+ * (the reference's single-stream constriction coder, entropy.rs:55-73, cannot
+ * be split across threads):
  *
- *   state x in [2^16, 2^32), 16-bit renormalisation words, 15-bit model.
- *   header  (32 B): u32 magic "KVR1", u32 prob_bits=15, u32 lanes=32,
+ *   state x in [2^16, 2^32), 16-bit renormalisation words, 13-bit model.
+ *   header  (32 B): u32 magic "KVR2", u32 prob_bits=13, u32 lanes=32,
  *                   u32 chunk_symbols, u64 original_len, u32 num_chunks,
  *                   u32 header_bytes (= 32 + 4*(num_chunks+1))
  *   u32 chunk_offset[num_chunks+1]   byte offset of each chunk payload;
  *                                    the last entry is the container length
- *   chunk payload: u32 nwords; u32 final_state[32]; u16 words[nwords];
- *                  u16 zero pad when nwords is odd
+ *   chunk payload: u32 final_state[32]; u16 lane_words[32];
+ *                  u16 words[sum(lane_words)]: lane 0's stream, then lane 1's,
+ *                  ..., each in the order the decoder reads it;
+ *                  one zero u16 when the word total is odd
  *
  * Chunk c holds symbols [c*chunk, min((c+1)*chunk, n)); symbol i of a chunk
- * belongs to lane i % 32 and step i / 32. The encoder walks steps from last to
- * first; in each step every active lane first renormalises (emitting at most one
- * word; emitters ordered by descending lane) then encodes. Emitted words are
- * laid out so that the decoder, walking steps forward and serving consuming
- * lanes in ascending order, reads the word array front to back.
+ * belongs to lane i % 32 and step i / 32. Each lane is an ordinary rANS coder
+ * over its own symbols: the encoder walks its steps from last to first, emits
+ * at most one word per step before encoding, and the decoder walks them first
+ * to last, reading that lane's words front to back.
  * ------------------------------------------------------------------------- */
 #define RANS_M (1u << ORC_RANS_PROB_BITS)
 #define RANS_L (1u << 16)
+#define RANS_PAYLOAD_HDR (4u * ORC_RANS_LANES + 2u * ORC_RANS_LANES)
 
 void orc_histogram(const uint8_t* data, size_t n, uint32_t* freq) {
   memset(freq, 0, 256 * sizeof(uint32_t));
   for (size_t i = 0; i < n; ++i) freq[data[i]] += 1;
 }
 
-/* Integer-only model: symbols seen q = max(1, floor(count * 2^15 / N)); unseen
+/* Integer-only model: symbols seen q = max(1, floor(count * 2^13 / N)); unseen
  * symbols get no slot. A deficit goes to the most frequent symbol (lowest index
  * on ties); an excess is taken from the largest entries, one symbol at a time. */
 int orc_rans_normalize(const uint32_t* freq, uint32_t* q, uint32_t* cum) {
@@ -463,16 +466,18 @@ int orc_rans_normalize(const uint32_t* freq, uint32_t* q, uint32_t* cum) {
 
 size_t orc_rans_max_encoded_len(size_t n, uint32_t chunk) {
   size_t nc = (n + chunk - 1) / chunk;
-  return 32 + 4 * (nc + 1) + nc * (4 + 4 * ORC_RANS_LANES + 2) + 2 * n;
+  return 32 + 4 * (nc + 1) + nc * (RANS_PAYLOAD_HDR + 2) + 2 * n;
 }
 
+static inline void put16(uint8_t* p, uint16_t v) { memcpy(p, &v, 2); }
+static inline uint16_t get16(const uint8_t* p) { uint16_t v; memcpy(&v, p, 2); return v; }
 static inline void put32(uint8_t* p, uint32_t v) { memcpy(p, &v, 4); }
 static inline uint32_t get32(const uint8_t* p) { uint32_t v; memcpy(&v, p, 4); return v; }
 static inline uint64_t get64(const uint8_t* p) { uint64_t v; memcpy(&v, p, 8); return v; }
 
 int orc_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, uint8_t* out, size_t out_cap,
                     size_t* out_len, uint32_t* freq) {
-  if (chunk == 0 || chunk % ORC_RANS_LANES) return ORC_ERR_INVALID_CONFIG;
+  if (chunk == 0 || chunk % ORC_RANS_LANES || chunk > ORC_RANS_MAX_CHUNK) return ORC_ERR_INVALID_CONFIG;
   orc_histogram(data, n, freq);
   if (n == 0) { *out_len = 0; return ORC_OK; }
   uint32_t q[256], cum[256];
@@ -481,7 +486,8 @@ int orc_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, uint8_t* out,
   size_t nc = (n + chunk - 1) / chunk;
   size_t hdr = 32 + 4 * (nc + 1);
   if (out_cap < hdr) return ORC_ERR_ENTROPY;
-  uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * (chunk + 1));
+  const size_t smax = chunk / ORC_RANS_LANES; /* steps, and so words, per lane at most */
+  uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * ORC_RANS_LANES * smax);
   if (!tmp) return ORC_ERR_PIPELINE;
   size_t pos = hdr;
   for (size_t c = 0; c < nc; ++c) {
@@ -489,36 +495,39 @@ int orc_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, uint8_t* out,
     size_t nsym = (n - start < chunk) ? n - start : chunk;
     size_t steps = (nsym + ORC_RANS_LANES - 1) / ORC_RANS_LANES;
     uint32_t x[ORC_RANS_LANES];
-    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) x[l] = RANS_L;
-    size_t cap = chunk + 1, emitted = 0; /* tmp written from the back */
-    for (size_t st_i = steps; st_i-- > 0;) {
-      for (int l = (int)ORC_RANS_LANES - 1; l >= 0; --l) { /* renormalise, descending lanes */
-        size_t i = st_i * ORC_RANS_LANES + (size_t)l;
-        if (i >= nsym) continue;
-        uint32_t f = q[data[start + i]];
-        uint64_t xmax = ((uint64_t)(RANS_L >> ORC_RANS_PROB_BITS) << 16) * f;
-        if ((uint64_t)x[l] >= xmax) {
-          tmp[cap - 1 - emitted] = (uint16_t)(x[l] & 0xFFFFu);
-          ++emitted;
-          x[l] >>= 16;
-        }
-      }
-      for (unsigned l = 0; l < ORC_RANS_LANES; ++l) { /* encode */
+    size_t cnt[ORC_RANS_LANES], total = 0;
+    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
+      uint16_t* region = tmp + (size_t)l * smax; /* filled from its end */
+      uint32_t xl = RANS_L;
+      size_t k = 0;
+      for (size_t st_i = steps; st_i-- > 0;) {
         size_t i = st_i * ORC_RANS_LANES + l;
         if (i >= nsym) continue;
         uint8_t s = data[start + i];
         uint32_t f = q[s];
-        x[l] = ((x[l] / f) << ORC_RANS_PROB_BITS) + (x[l] % f) + cum[s];
+        uint64_t xmax = ((uint64_t)(RANS_L >> ORC_RANS_PROB_BITS) << 16) * f;
+        if ((uint64_t)xl >= xmax) {
+          region[smax - 1 - k] = (uint16_t)(xl & 0xFFFFu);
+          ++k;
+          xl >>= 16;
+        }
+        xl = ((xl / f) << ORC_RANS_PROB_BITS) + (xl % f) + cum[s];
       }
+      x[l] = xl;
+      cnt[l] = k;
+      total += k;
     }
-    size_t bytes = 4 + 4 * ORC_RANS_LANES + 2 * emitted + (emitted & 1) * 2;
+    size_t bytes = RANS_PAYLOAD_HDR + 2 * total + (total & 1) * 2;
     if (pos + bytes > out_cap) { free(tmp); return ORC_ERR_ENTROPY; }
     put32(out + 32 + 4 * c, (uint32_t)pos);
-    put32(out + pos, (uint32_t)emitted);
-    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) put32(out + pos + 4 + 4 * l, x[l]);
-    uint8_t* w = out + pos + 4 + 4 * ORC_RANS_LANES;
-    memcpy(w, tmp + (cap - emitted), 2 * emitted);
-    if (emitted & 1) { w[2 * emitted] = 0; w[2 * emitted + 1] = 0; }
+    uint8_t* w = out + pos + RANS_PAYLOAD_HDR;
+    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
+      put32(out + pos + 4 * l, x[l]);
+      put16(out + pos + 4 * ORC_RANS_LANES + 2 * l, (uint16_t)cnt[l]);
+      memcpy(w, tmp + (size_t)l * smax + (smax - cnt[l]), 2 * cnt[l]);
+      w += 2 * cnt[l];
+    }
+    if (total & 1) { w[0] = 0; w[1] = 0; }
     pos += bytes;
   }
   free(tmp);
@@ -546,57 +555,52 @@ int orc_rans_decode(const uint8_t* comp, size_t comp_len, const uint32_t* freq,
   uint32_t chunk = get32(comp + 12);
   uint64_t n = get64(comp + 16);
   uint32_t nc = get32(comp + 24);
-  if (chunk == 0 || chunk % ORC_RANS_LANES || n != original_len) return ORC_ERR_CORRUPT_STREAM;
+  if (chunk == 0 || chunk % ORC_RANS_LANES || chunk > ORC_RANS_MAX_CHUNK || n != original_len)
+    return ORC_ERR_CORRUPT_STREAM;
   if ((uint64_t)nc != (n + chunk - 1) / chunk) return ORC_ERR_CORRUPT_STREAM;
   size_t hdr = 32 + 4 * ((size_t)nc + 1);
   if (get32(comp + 28) != hdr || comp_len < hdr) return ORC_ERR_CORRUPT_STREAM;
   if (get32(comp + 32 + 4 * (size_t)nc) != comp_len) return ORC_ERR_CORRUPT_STREAM;
   uint32_t q[256], cum[256];
   if (orc_rans_normalize(freq, q, cum)) return ORC_ERR_ENTROPY;
-  uint8_t* slot2sym = (uint8_t*)malloc(RANS_M);
-  if (!slot2sym) return ORC_ERR_PIPELINE;
+  uint8_t slot2sym[RANS_M];
   for (int s = 0; s < 256; ++s)
     for (uint32_t k = 0; k < q[s]; ++k) slot2sym[cum[s] + k] = (uint8_t)s;
-  int status = ORC_OK;
-  for (size_t c = 0; c < nc && status == ORC_OK; ++c) {
+  for (size_t c = 0; c < nc; ++c) {
     size_t off = get32(comp + 32 + 4 * c), end = get32(comp + 32 + 4 * (c + 1));
-    if (off < hdr || end > comp_len || end < off + 4 + 4 * ORC_RANS_LANES) { status = ORC_ERR_CORRUPT_STREAM; break; }
-    size_t nw = get32(comp + off);
-    if (off + 4 + 4 * ORC_RANS_LANES + 2 * nw + (nw & 1) * 2 != end) { status = ORC_ERR_CORRUPT_STREAM; break; }
-    uint32_t x[ORC_RANS_LANES];
-    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
-      x[l] = get32(comp + off + 4 + 4 * l);
-      if (x[l] < RANS_L) status = ORC_ERR_CORRUPT_STREAM;
-    }
-    const uint8_t* w = comp + off + 4 + 4 * ORC_RANS_LANES;
-    size_t p = 0, start = c * (size_t)chunk;
+    if (off < hdr || end > comp_len || end < off + RANS_PAYLOAD_HDR) return ORC_ERR_CORRUPT_STREAM;
+    size_t start = c * (size_t)chunk;
     size_t nsym = (n - start < chunk) ? (size_t)(n - start) : chunk;
     size_t steps = (nsym + ORC_RANS_LANES - 1) / ORC_RANS_LANES;
-    for (size_t s_i = 0; s_i < steps && status == ORC_OK; ++s_i) {
-      for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
+    size_t base[ORC_RANS_LANES], cnt[ORC_RANS_LANES], total = 0;
+    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
+      cnt[l] = get16(comp + off + 4 * ORC_RANS_LANES + 2 * l);
+      base[l] = total;
+      total += cnt[l];
+    }
+    if (off + RANS_PAYLOAD_HDR + 2 * total + (total & 1) * 2 != end) return ORC_ERR_CORRUPT_STREAM;
+    const uint8_t* w = comp + off + RANS_PAYLOAD_HDR;
+    for (unsigned l = 0; l < ORC_RANS_LANES; ++l) {
+      uint32_t xl = get32(comp + off + 4 * l);
+      if (xl < RANS_L) return ORC_ERR_CORRUPT_STREAM;
+      size_t k = 0;
+      for (size_t s_i = 0; s_i < steps; ++s_i) {
         size_t i = s_i * ORC_RANS_LANES + l;
         if (i >= nsym) continue;
-        uint32_t slot = x[l] & (RANS_M - 1);
+        uint32_t slot = xl & (RANS_M - 1);
         uint8_t s = slot2sym[slot];
-        x[l] = q[s] * (x[l] >> ORC_RANS_PROB_BITS) + slot - cum[s];
+        xl = q[s] * (xl >> ORC_RANS_PROB_BITS) + slot - cum[s];
         out[start + i] = s;
-        if (x[l] < RANS_L) {
-          if (p >= nw) { status = ORC_ERR_CORRUPT_STREAM; break; }
-          uint16_t word;
-          memcpy(&word, w + 2 * p, 2);
-          ++p;
-          x[l] = (x[l] << 16) | word;
+        if (xl < RANS_L) {
+          if (k >= cnt[l]) return ORC_ERR_CORRUPT_STREAM;
+          xl = (xl << 16) | get16(w + 2 * (base[l] + k));
+          ++k;
         }
       }
-    }
-    if (status == ORC_OK) {
-      if (p != nw) status = ORC_ERR_CORRUPT_STREAM;
-      for (unsigned l = 0; l < ORC_RANS_LANES; ++l)
-        if (x[l] != RANS_L) status = ORC_ERR_CORRUPT_STREAM;
+      if (xl != RANS_L || k != cnt[l]) return ORC_ERR_CORRUPT_STREAM;
     }
   }
-  free(slot2sym);
-  return status;
+  return ORC_OK;
 }
 
 /* Shannon bound of the empirical distribution, in bits (for reporting). */

@@ -49,10 +49,11 @@ enum { ORC_INT4 = 0, ORC_INT8 = 1, ORC_F32 = 2 };            /* DataType, types.
 enum { ORC_PER_CHANNEL = 0, ORC_PER_TOKEN = 1 };            /* QuantAxis, types.rs:97-103 */
 
 /* rANS container constants (this project's format, mirrored on the GPU) */
-#define ORC_RANS_PROB_BITS 15u
+#define ORC_RANS_PROB_BITS 13u
 #define ORC_RANS_LANES 32u
 #define ORC_RANS_DEFAULT_CHUNK 16384u
-#define ORC_RANS_MAGIC 0x3152564Bu /* "KVR1" */
+#define ORC_RANS_MAX_CHUNK (ORC_RANS_LANES * 65535u) /* lane word counts are u16 */
+#define ORC_RANS_MAGIC 0x3252564Bu /* "KVR2" */
 
 uint8_t orc_pack_int4(uint8_t a, uint8_t b);
 void orc_unpack_int4(uint8_t byte, uint8_t* lo, uint8_t* hi);

@@ -23,7 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "..", ".."))
 from oracle import quant_numpy as QN  # noqa: E402
 
-PROB_BITS = 15
+PROB_BITS = 13
 M = 1 << PROB_BITS
 L = 1 << 16
 
@@ -64,26 +64,25 @@ def py_rans_encode(data: bytes, chunk: int) -> bytes:
     for c in range(nc):
         sym = data[c * chunk:(c + 1) * chunk]
         steps = (len(sym) + 31) // 32
-        x = [L] * 32
-        emitted = []  # in emission order
-        for st in range(steps - 1, -1, -1):
-            for lane in range(31, -1, -1):
-                i = st * 32 + lane
-                if i >= len(sym):
-                    continue
-                f = q[sym[i]]
-                if x[lane] >= (f << 17):
-                    emitted.append(x[lane] & 0xFFFF)
-                    x[lane] >>= 16
-            for lane in range(32):
+        states, streams = [], []
+        for lane in range(32):
+            x = L
+            emitted = []  # in emission order
+            for st in range(steps - 1, -1, -1):
                 i = st * 32 + lane
                 if i >= len(sym):
                     continue
                 s = sym[i]
                 f = q[s]
-                x[lane] = ((x[lane] // f) << PROB_BITS) + (x[lane] % f) + cum[s]
-        words = list(reversed(emitted))  # decoder reads the last emitted word first
-        body = struct.pack("<I", len(words)) + struct.pack("<32I", *x) + struct.pack(f"<{len(words)}H", *words)
+                if x >= (f << (32 - PROB_BITS)):
+                    emitted.append(x & 0xFFFF)
+                    x >>= 16
+                x = ((x // f) << PROB_BITS) + (x % f) + cum[s]
+            states.append(x)
+            streams.append(list(reversed(emitted)))  # the decoder reads the last emitted word first
+        words = [w for stream in streams for w in stream]
+        body = (struct.pack("<32I", *states) + struct.pack("<32H", *[len(t) for t in streams])
+                + struct.pack(f"<{len(words)}H", *words))
         if len(words) % 2:
             body += b"\x00\x00"
         payloads.append(body)
@@ -93,7 +92,7 @@ def py_rans_encode(data: bytes, chunk: int) -> bytes:
         offs.append(pos)
         pos += len(p)
     offs.append(pos)
-    header = struct.pack("<IIIIQII", 0x3152564B, PROB_BITS, 32, chunk, n, nc, hdr_len)
+    header = struct.pack("<IIIIQII", 0x3252564B, PROB_BITS, 32, chunk, n, nc, hdr_len)
     return header + struct.pack(f"<{nc + 1}I", *offs) + b"".join(payloads), np.array(freq, np.uint32)
 
 
