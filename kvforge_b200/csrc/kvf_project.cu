@@ -58,32 +58,35 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 }
 
 // ---- projection -------------------------------------------------------------
-// One persistent kernel. The grid walks (head, 128-token tile) items in
-// contiguous ranges per block; thread t owns row t of every tile and computes
-// its R coefficients. Each coefficient is a fused multiply-add chain over
-// c = 0..D-1 from +0.0; two chains advance per fma.rn.f32x2 (each element
-// rounded once), so values are identical to the CPU oracle's fmaf chain. The
-// basis of head h sits transposed in shared memory, vT[c][RG], read with
-// broadcast 16-byte loads at compile-time offsets.
+// One persistent kernel. The grid walks (head, 256-token tile) items in
+// contiguous ranges per block; thread t owns rows t and t + 128 of every tile
+// and computes their R coefficients. Each coefficient is a fused multiply-add
+// chain over c = 0..D-1 from +0.0; two chains advance per fma.rn.f32x2 (each
+// element rounded once), so values are identical to the CPU oracle's fmaf
+// chain. The basis of head h sits transposed in shared memory, vT[c][RG],
+// read with broadcast 16-byte loads at compile-time offsets; each load feeds
+// both of a thread's rows.
 //
-// TMA variant (rows a multiple of 128 bytes, 16-byte aligned input): a tile
-// is streamed as column blocks of 128 rows x 128 bytes (16 KB), each one 2-D
-// tensor copy (cp.async.bulk.tensor, no multicast) with the 128-byte swizzle,
+// TMA variant (rows a multiple of 64 bytes, 16-byte aligned input): a tile is
+// streamed as column blocks of 256 rows x 64 bytes (16 KB), each one 2-D
+// tensor copy (cp.async.bulk.tensor, no multicast) with the 64-byte swizzle,
 // several blocks in flight per CTA; the accumulators stay in registers across
-// a tile's column blocks. The swizzle stores 16-byte chunk j of a 128-byte
-// row at j ^ (bits 7-9 of the row's address), so the reads of eight
-// consecutive rows fall on distinct banks. Small stages keep several CTAs resident per SM. Waits are
-// bounded: a wait that expires raises the device timeout status.
+// a tile's column blocks. The swizzle stores 16-byte chunk j of a 64-byte row
+// at j ^ (bits 7-8 of the row's address), so the reads of eight consecutive
+// rows fall on distinct banks. Small stages keep several CTAs resident per
+// SM. Waits are bounded: a wait that expires raises the device timeout status.
 // Generic variant: scalar loads from global memory.
 //
-// Epilogues (each thread stores its own row; consecutive rows are contiguous):
+// Epilogues (each thread stores its own rows; consecutive rows are contiguous):
 //   MODE 0: P [H,T,R];
 //   MODE 1: P and per-(head, r) min/max folded into block-local keys,
 //           flushed with one global atomic per (block, head, r);
 //   MODE 2: per-token quantization: scale/min per token, codes as bytes or
 //           INT4-packed bytes, plus an optional byte histogram.
-constexpr int kProjRows = 128;             // token rows per tile = threads per block
-constexpr int kColBytes = 128;             // bytes of each row per streamed column block
+constexpr int kProjThreads = 128;
+constexpr int kProjNR = 2;                           // token rows per thread
+constexpr int kProjRows = kProjThreads * kProjNR;    // token rows per tile
+constexpr int kColBytes = 64;                        // bytes of each row per streamed column block
 constexpr int kColStage = kProjRows * kColBytes;
 constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before a wait gives up
 
@@ -156,27 +159,31 @@ struct ProjSmem {
   int total;
 };
 
-// acc[q] holds coefficients (2q, 2q + 1) as one packed f32x2 register pair;
-// x is broadcast to both halves once, the basis row is read as packed pairs
+// acc[q] holds coefficients (2q, 2q + 1) of one row as a packed f32x2 register
+// pair; each basis pair loaded from shared memory feeds both of a thread's rows
 template <int RG>
-__device__ __forceinline__ void fma_row(unsigned long long (&acc)[RG / 2], float xv, const float* vrow) {
-  unsigned long long xx;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(xx) : "f"(xv));
+__device__ __forceinline__ void fma_rows(unsigned long long (&acc)[kProjNR][RG / 2], const float (&xv)[kProjNR],
+                                         const float* vrow) {
+  unsigned long long xx[kProjNR];
+#pragma unroll
+  for (int rr = 0; rr < kProjNR; ++rr) asm("mov.b64 %0, {%1, %1};" : "=l"(xx[rr]) : "f"(xv[rr]));
   const ulonglong2* vr = reinterpret_cast<const ulonglong2*>(vrow);
 #pragma unroll
   for (int q = 0; q < RG / 4; ++q) {
     const ulonglong2 v = vr[q];
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[2 * q]) : "l"(xx), "l"(v.x));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[2 * q + 1]) : "l"(xx), "l"(v.y));
+#pragma unroll
+    for (int rr = 0; rr < kProjNR; ++rr) {
+      asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[rr][2 * q]) : "l"(xx[rr]), "l"(v.x));
+      asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[rr][2 * q + 1]) : "l"(xx[rr]), "l"(v.y));
+    }
   }
 }
 
 template <typename TIn, int RG, bool CALIB, int MODE, bool TMA>
-__global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant__ CUtensorMap xmap,
-                                                     const TIn* __restrict__ x, int H, int T, int D,
-                                                     const float* __restrict__ bvt,
-                                                     const uint64_t* __restrict__ ranks, int R, int Rpad,
-                                                     ProjSmem L, ProjectOut o) {
+__global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
+    k_project(const __grid_constant__ CUtensorMap xmap, const TIn* __restrict__ x, int H, int T, int D,
+              const float* __restrict__ bvt, const uint64_t* __restrict__ ranks, int R, int Rpad, ProjSmem L,
+              ProjectOut o) {
   extern __shared__ __align__(1024) uint8_t smraw[];
   float* vT = reinterpret_cast<float*>(smraw);  // [D][Rpad]
   const int Rk = (R + 3) & ~3;
@@ -232,16 +239,23 @@ __global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant_
   for (long long li = 0; li < nit; ++li) {
     const long long it = i0 + li;
     const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
-    const int t = tile * kProjRows + tid;
-    const bool ok = t < T;
-    const size_t g = (size_t)h * T + (ok ? t : 0);
     const size_t g0 = (size_t)h * T + (size_t)tile * kProjRows;
     const int nrows = min(kProjRows, T - tile * kProjRows);
+    bool ok[kProjNR];
+    size_t g[kProjNR];
+#pragma unroll
+    for (int rr = 0; rr < kProjNR; ++rr) {
+      const int row = tid + rr * kProjThreads;  // this thread's rows of the tile
+      ok[rr] = row < nrows;
+      g[rr] = g0 + (ok[rr] ? row : 0);
+    }
     double s1 = 0.0, s2 = 0.0;
     for (int rg = 0; rg < R; rg += RG) {
-      unsigned long long acc2[RG / 2];
+      unsigned long long acc2[kProjNR][RG / 2];
 #pragma unroll
-      for (int r = 0; r < RG / 2; ++r) acc2[r] = 0ull;  // +0.0f in both halves
+      for (int rr = 0; rr < kProjNR; ++rr)
+#pragma unroll
+        for (int r = 0; r < RG / 2; ++r) acc2[rr][r] = 0ull;  // +0.0f in both halves
       for (int cb = 0; cb < ncb; ++cb) {
         const long long u = li * ncb + cb;
         if (TMA) {
@@ -275,52 +289,75 @@ __global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant_
         }
         if (TMA) {  // single r-group: vT rows are RG floats
           constexpr int PV = Seg<TIn>::PV;
-          const uint8_t* sb = xbuf + (size_t)(u % L.stages) * kColStage + tid * kColBytes;
-          const int sw = (int)(smem_addr(sb) >> 7) & 7;  // the swizzle XORs address bits 4-6 with bits 7-9
+          const uint8_t* sb[kProjNR];
+          int sw[kProjNR];
+#pragma unroll
+          for (int rr = 0; rr < kProjNR; ++rr) {
+            sb[rr] = xbuf + (size_t)(u % L.stages) * kColStage + (tid + rr * kProjThreads) * kColBytes;
+            sw[rr] = (int)(smem_addr(sb[rr]) >> 7) & 3;  // the swizzle XORs address bits 4-5 with bits 7-8
+          }
 #pragma unroll
           for (int jj = 0; jj < kColBytes / 16; ++jj) {
-            float xv[PV];
-            Seg<TIn>::unpack(*reinterpret_cast<const uint4*>(sb + ((jj ^ sw) << 4)), xv);
+            float xv[kProjNR][PV];
+#pragma unroll
+            for (int rr = 0; rr < kProjNR; ++rr)
+              Seg<TIn>::unpack(*reinterpret_cast<const uint4*>(sb[rr] + ((jj ^ sw[rr]) << 4)), xv[rr]);
             if (CALIB) {
 #pragma unroll
-              for (int k = 0; k < PV; ++k) {
-                const double v = ok ? (double)xv[k] : 0.0;
+              for (int rr = 0; rr < kProjNR; ++rr)
+#pragma unroll
+                for (int k = 0; k < PV; ++k) {
+                  const double v = ok[rr] ? (double)xv[rr][k] : 0.0;
+                  s1 += v;
+                  s2 += v * v;
+                }
+            }
+            const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * RG;
+#pragma unroll
+            for (int k = 0; k < PV; ++k) {
+              float xk[kProjNR];
+#pragma unroll
+              for (int rr = 0; rr < kProjNR; ++rr) xk[rr] = xv[rr][k];
+              fma_rows<RG>(acc2, xk, vb + k * RG);
+            }
+          }
+        } else {
+          for (int c = 0; c < D; ++c) {
+            float xk[kProjNR];
+#pragma unroll
+            for (int rr = 0; rr < kProjNR; ++rr) {
+              xk[rr] = ok[rr] ? ldf(x + g[rr] * D, c) : 0.0f;
+              if (CALIB && rg == 0) {
+                const double v = (double)xk[rr];
                 s1 += v;
                 s2 += v * v;
               }
             }
-            const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * RG;
-#pragma unroll
-            for (int k = 0; k < PV; ++k) fma_row<RG>(acc2, xv[k], vb + k * RG);
-          }
-        } else {
-          const TIn* xr = x + g * D;
-          for (int c = 0; c < D; ++c) {
-            const float xv = ok ? ldf(xr, c) : 0.0f;
-            if (CALIB && rg == 0) {
-              const double v = (double)xv;
-              s1 += v;
-              s2 += v * v;
-            }
-            fma_row<RG>(acc2, xv, vT + (size_t)c * Rpad + rg);
+            fma_rows<RG>(acc2, xk, vT + (size_t)c * Rpad + rg);
           }
         }
       }
       if (stuck >= 0) break;
-      float acc[RG];
+      float acc[kProjNR][RG];
 #pragma unroll
-      for (int r = 0; r < RG / 2; ++r)
-        asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * r]), "=f"(acc[2 * r + 1]) : "l"(acc2[r]));
+      for (int rr = 0; rr < kProjNR; ++rr)
 #pragma unroll
-      for (int r = 0; r < RG; ++r)
-        if (rg + r >= rank) acc[r] = 0.0f;  // projection.rs:96
+        for (int r = 0; r < RG / 2; ++r)
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[rr][2 * r]), "=f"(acc[rr][2 * r + 1]) : "l"(acc2[rr][r]));
+#pragma unroll
+      for (int rr = 0; rr < kProjNR; ++rr)
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+          if (rg + r >= rank) acc[rr][r] = 0.0f;  // projection.rs:96
 
       if (MODE == 1) {  // column min/max of this tile into the block's keys
 #pragma unroll
         for (int r = 0; r < RG; ++r) {
           if (rg + r < R) {  // warp-uniform
             float mn = INFINITY, mx = -INFINITY;
-            if (ok) mm_update(acc[r], mn, mx);
+#pragma unroll
+            for (int rr = 0; rr < kProjNR; ++rr)
+              if (ok[rr]) mm_update(acc[rr][r], mn, mx);
             warp_minmax(mn, mx);
             if ((tid & 31) == 0) {
               atomicMin(&skmin[rg + r], fkey(mn));
@@ -330,35 +367,44 @@ __global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant_
         }
       }
       if (MODE == 0 || MODE == 1) {
-        if (ok) {
-          float* pr = o.P + g * R + rg;
-          if (rg + RG <= R && (R & 3) == 0) {
 #pragma unroll
-            for (int q = 0; q < RG / 4; ++q)
-              reinterpret_cast<float4*>(pr)[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-          } else {
+        for (int rr = 0; rr < kProjNR; ++rr)
+          if (ok[rr]) {
+            float* pr = o.P + g[rr] * R + rg;
+            if (rg + RG <= R && (R & 3) == 0) {
+#pragma unroll
+              for (int q = 0; q < RG / 4; ++q)
+                reinterpret_cast<float4*>(pr)[q] =
+                    make_float4(acc[rr][4 * q], acc[rr][4 * q + 1], acc[rr][4 * q + 2], acc[rr][4 * q + 3]);
+            } else {
+#pragma unroll
+              for (int r = 0; r < RG; ++r)
+                if (rg + r < R) pr[r] = acc[rr][r];
+            }
+          }
+      } else {  // MODE 2 (R <= RG)
+        const bool direct = o.packed == nullptr || (R & 1) == 0;
+#pragma unroll
+        for (int rr = 0; rr < kProjNR; ++rr) {
+          float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+            if (r < R) mm_update(acc[rr][r], mn, mx);
+          const float scale = make_scale(mn, mx, o.levels);
+          const float inv = __frcp_rn(scale);
+          uint32_t cd[RG];
+#pragma unroll
+          for (int r = 0; r < RG; ++r) cd[r] = (r < R) ? qcode_fast(acc[rr][r], mn, scale, inv, o.levels) : 0u;
+          if (ok[rr]) {
+            o.scales[g[rr]] = scale;
+            o.mins[g[rr]] = mn;
+          }
+          if (!direct) {  // odd R: pairs run across rows; pack the tile through shared memory
 #pragma unroll
             for (int r = 0; r < RG; ++r)
-              if (rg + r < R) pr[r] = acc[r];
-          }
-        }
-      } else {  // MODE 2 (R <= RG)
-        float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < RG; ++r)
-          if (r < R) mm_update(acc[r], mn, mx);
-        const float scale = make_scale(mn, mx, o.levels);
-        const float inv = __frcp_rn(scale);
-        uint32_t cd[RG];
-#pragma unroll
-        for (int r = 0; r < RG; ++r) cd[r] = (r < R) ? qcode_fast(acc[r], mn, scale, inv, o.levels) : 0u;
-        if (ok) {
-          o.scales[g] = scale;
-          o.mins[g] = mn;
-        }
-        if (o.packed && (R & 1) == 0) {  // this row's codes start on a byte boundary
-          if (ok) {
-            uint8_t* dp = o.packed + (g * R) / 2;
+              if (r < R) cstage[(tid + rr * kProjThreads) * R + r] = (uint8_t)cd[r];
+          } else if (ok[rr] && o.packed) {  // this row's codes start on a byte boundary
+            uint8_t* dp = o.packed + (g[rr] * R) / 2;
 #pragma unroll
             for (int b = 0; b < RG / 2; ++b)
               if (2 * b < R) {
@@ -366,11 +412,17 @@ __global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant_
                 dp[b] = (uint8_t)byte;
                 if (hist_on) atomicAdd(&shist[byte], 1u);
               }
-          }
-        } else if (o.packed) {  // odd R: pairs run across rows; pack the tile through shared memory
+          } else if (ok[rr]) {
+            uint8_t* dc = o.codes + g[rr] * R;
 #pragma unroll
-          for (int r = 0; r < RG; ++r)
-            if (r < R) cstage[tid * R + r] = (uint8_t)cd[r];
+            for (int r = 0; r < RG; ++r)
+              if (r < R) {
+                dc[r] = (uint8_t)cd[r];
+                if (hist_on) atomicAdd(&shist[cd[r]], 1u);
+              }
+          }
+        }
+        if (!direct) {
           __syncthreads();
           const int cnt = nrows * R;
           uint8_t* dp = o.packed + (g0 * R) / 2;
@@ -380,14 +432,6 @@ __global__ void __launch_bounds__(kProjRows, 4) k_project(const __grid_constant_
             if (hist_on) atomicAdd(&shist[byte], 1u);
           }
           __syncthreads();
-        } else if (ok) {
-          uint8_t* dc = o.codes + g * R;
-#pragma unroll
-          for (int r = 0; r < RG; ++r)
-            if (r < R) {
-              dc[r] = (uint8_t)cd[r];
-              if (hist_on) atomicAdd(&shist[cd[r]], 1u);
-            }
         }
       }
     }
@@ -433,7 +477,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// [H*T rows, D columns] of TIn, boxes of 128 rows x 128 bytes, 128-byte swizzle
+// [H*T rows, D columns] of TIn, boxes of kProjRows rows x 64 bytes, 64-byte swizzle
 template <typename TIn>
 bool encode_rows_map(CUtensorMap* map, const TIn* x, size_t rows, size_t D) {
   auto enc = tensor_map_encoder();
@@ -445,7 +489,7 @@ bool encode_rows_map(CUtensorMap* map, const TIn* x, size_t rows, size_t D) {
   const CUtensorMapDataType dt =
       sizeof(TIn) == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   return enc(map, dt, 2, const_cast<TIn*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -485,7 +529,7 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   off = (off + 15) & ~15;
   L.bars = off;
   off += 8 * 8;
-  off = (off + 1023) & ~1023;  // the 128-byte swizzle repeats every 1024 bytes
+  off = (off + 1023) & ~1023;  // swizzled stages start on a 1024-byte boundary
   L.xbuf = off;
   L.stages = TMA ? 3 : 0;
   off += L.stages * kColStage;
@@ -500,7 +544,7 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   for (auto& c : cache[dev])
     if (c.smem == L.total) per_sm = c.per_sm;
   if (per_sm == 0) {
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjRows, L.total)) != cudaSuccess)
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kProjThreads, L.total)) != cudaSuccess)
       return e;
     per_sm = std::max(per_sm, 1);
     for (auto& c : cache[dev])
@@ -512,7 +556,7 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   }
   const size_t items = H * ((T + kProjRows - 1) / kProjRows);
   const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * sms[dev]));
-  kern<<<(unsigned)grid, kProjRows, L.total, st>>>(map, x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
+  kern<<<(unsigned)grid, kProjThreads, L.total, st>>>(map, x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
   note_launches(1);
   return cudaGetLastError();
 }
@@ -681,6 +725,165 @@ __global__ void __launch_bounds__(128) k_dequant_reconstruct(
   }
 }
 
+// Register-basis variant (D <= 128, D % 4 == 0, R <= 16): a persistent grid
+// walks (head, 128-token tile) items; lane l of every warp keeps columns
+// 4l..4l+3 of the head's basis rows in registers for as long as the head
+// lasts. Each thread dequantizes one token row of the tile into shared memory
+// as duplicated pairs (d, d), so one broadcast 16-byte load supplies the f32x2
+// multiplicand of two rows; warp w then computes rows 8g..8g+7 for
+// g = w, w + 4, ... with packed fma.rn.f32x2 (EXACT: __fmul_rn then
+// __fadd_rn per element). The next
+// tile's codes and scales are read into registers before the current tile is
+// computed. Terms r >= rank get d = 0 and a zero basis row, which leave every
+// sum unchanged (it starts at +0.0), so results equal the per-rank loop.
+template <int MODE, bool EXACT, int RG>
+__global__ void __launch_bounds__(128, (RG >= 12 ? 3 : 4)) k_reconstruct_reg(const uint8_t* __restrict__ codes,
+                                                         const float* __restrict__ raw,
+                                                         const float* __restrict__ scales,
+                                                         const float* __restrict__ mins, int axis, int H, int T,
+                                                         int R, int D, const float* __restrict__ bvt,
+                                                         const uint64_t* __restrict__ ranks, float* __restrict__ out) {
+  __shared__ __align__(16) unsigned long long dT2[2][RG][kRecRows];  // (d, d) per (r, row)
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int tiles = (T + kRecRows - 1) / kRecRows;
+  const long long items = (long long)H * tiles;
+  const long long i0 = items * blockIdx.x / gridDim.x;
+  const long long i1 = items * (blockIdx.x + 1) / gridDim.x;
+  const bool col_ok = 4 * lane < D;
+
+  // this thread's row of item `it`: raw inputs fetched now, dequantized later
+  struct RowIn {
+    uint32_t q[(RG + 3) / 4];  // codes, one byte each
+    float raw[MODE == 0 ? RG : 1];
+    float sc, mn;
+  };
+  auto fetch = [&](long long it, RowIn& in) {
+    const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+    const size_t t = (size_t)tile * kRecRows + tid;
+    const bool ok = t < (size_t)T;
+    const size_t g = (size_t)h * T + (ok ? t : 0);
+    if (MODE != 0 && axis != KVF_PER_CHANNEL) {
+      in.sc = ok ? __ldg(scales + g) : 0.0f;
+      in.mn = ok ? __ldg(mins + g) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < (RG + 3) / 4; ++k) in.q[k] = 0u;
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+      const size_t fi = g * R + r;
+      if (MODE == 0) {
+        in.raw[r] = (ok && r < R) ? __ldg(raw + fi) : 0.0f;
+      } else if (ok && r < R) {
+        uint32_t q = codes[MODE == 2 ? (fi >> 1) : fi];
+        if (MODE == 2) q = (fi & 1) ? (q >> 4) & 0xFu : q & 0xFu;
+        in.q[r >> 2] |= q << (8 * (r & 3));
+      }
+    }
+  };
+  auto stage = [&](long long it, const RowIn& in, int buf, int rank) {
+    const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+    const bool ok = (size_t)tile * kRecRows + tid < (size_t)T;
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+      float d = 0.0f;
+      if (ok && r < rank) {
+        if (MODE == 0) {
+          d = in.raw[r];
+        } else {
+          float sc = in.sc, mn = in.mn;
+          if (axis == KVF_PER_CHANNEL) {
+            sc = __ldg(scales + (size_t)h * R + r);
+            mn = __ldg(mins + (size_t)h * R + r);
+          }
+          d = __fadd_rn(__fmul_rn((float)((in.q[r >> 2] >> (8 * (r & 3))) & 0xFFu), sc), mn);
+        }
+      }
+      unsigned long long dd;
+      asm("mov.b64 %0, {%1, %1};" : "=l"(dd) : "f"(d));
+      dT2[buf][r][tid] = dd;
+    }
+  };
+  auto rank_of = [&](long long it) {
+    const int h = (int)(it / tiles);
+    const uint64_t rk = ranks[h];
+    return (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
+  };
+
+  ulonglong2 vreg[RG];  // basis columns 4l..4l+3 as two packed pairs per row
+  int cur_h = -1;
+  RowIn nxt;
+  if (i0 < i1) {
+    fetch(i0, nxt);
+    stage(i0, nxt, 0, rank_of(i0));
+  }
+  __syncthreads();
+  for (long long it = i0; it < i1; ++it) {
+    const int buf = (int)((it - i0) & 1);
+    const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+    if (it + 1 < i1) fetch(it + 1, nxt);  // loads in flight during this tile's arithmetic
+    if (h != cur_h) {
+      const int rank = rank_of(it);
+      const float* B = bvt + (size_t)h * R * D;
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rank && col_ok) v = __ldg(reinterpret_cast<const float4*>(B + (size_t)r * D + 4 * lane));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(vreg[r].x) : "f"(v.x), "f"(v.y));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(vreg[r].y) : "f"(v.z), "f"(v.w));
+      }
+      cur_h = h;
+    }
+    const size_t t0 = (size_t)tile * kRecRows;
+    for (int g8 = w; g8 < kRecRows / 8; g8 += 4) {
+      unsigned long long acc[8][2];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = 0ull;  // +0.0f
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        const ulonglong2* dp = reinterpret_cast<const ulonglong2*>(&dT2[buf][r][8 * g8]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const ulonglong2 d2 = dp[p];
+          const unsigned long long dd[2] = {d2.x, d2.y};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * p + e;
+            if (EXACT) {  // separately rounded product and sum, element by element
+              float a[4], v[4], d, d2;
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(a[0]), "=f"(a[1]) : "l"(acc[i][0]));
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(a[2]), "=f"(a[3]) : "l"(acc[i][1]));
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[0]), "=f"(v[1]) : "l"(vreg[r].x));
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[2]), "=f"(v[3]) : "l"(vreg[r].y));
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(d), "=f"(d2) : "l"(dd[e]));
+#pragma unroll
+              for (int k = 0; k < 4; ++k) a[k] = __fadd_rn(a[k], __fmul_rn(d, v[k]));
+              asm("mov.b64 %0, {%1, %2};" : "=l"(acc[i][0]) : "f"(a[0]), "f"(a[1]));
+              asm("mov.b64 %0, {%1, %2};" : "=l"(acc[i][1]) : "f"(a[2]), "f"(a[3]));
+            } else {
+              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[i][0]) : "l"(dd[e]), "l"(vreg[r].x));
+              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[i][1]) : "l"(dd[e]), "l"(vreg[r].y));
+            }
+          }
+        }
+      }
+      if (col_ok) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const size_t t = t0 + 8 * g8 + i;
+          if (t < (size_t)T) {
+            float4 o4;
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(o4.x), "=f"(o4.y) : "l"(acc[i][0]));
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(o4.z), "=f"(o4.w) : "l"(acc[i][1]));
+            __stcs(reinterpret_cast<float4*>(out + ((size_t)h * T + t) * D + 4 * lane), o4);
+          }
+        }
+      }
+    }
+    if (it + 1 < i1) stage(it + 1, nxt, buf ^ 1, rank_of(it + 1));
+    __syncthreads();  // the next tile's coefficients are in place; this buffer is free again
+  }
+}
+
 // any D: one thread per output element
 template <int MODE, bool EXACT>
 __global__ void __launch_bounds__(256) k_dequant_reconstruct_scalar(
@@ -720,7 +923,34 @@ cudaError_t dequant_reconstruct_mode(const uint8_t* codes, const float* raw, con
                                      size_t D, const float* bvt, const uint64_t* ranks, float* out,
                                      cudaStream_t st) {
   const size_t smem = ((size_t)R * D + (size_t)R * kRecRows) * sizeof(float);
-  if (D % 4 == 0 && smem <= 200 * 1024 && aligned(out, 16)) {
+  if (D % 4 == 0 && D <= 128 && R <= 16 && aligned(out, 16) && aligned(bvt, 16) && H * T < (1ull << 31)) {
+    static int sms[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!sms[dev] && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    const size_t items = H * ((T + kRecRows - 1) / kRecRows);
+    // persistent grid: as many blocks as fit at once, cached per instantiation and device
+#define KVF_RR(RGV)                                                                                           \
+  {                                                                                                           \
+    auto kern = k_reconstruct_reg<MODE, EXACT, RGV>;                                                          \
+    static int per_sm[64] = {};                                                                               \
+    if (!per_sm[dev]) {                                                                                       \
+      int n = 0;                                                                                              \
+      if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 128, 0)) != cudaSuccess) return e;     \
+      per_sm[dev] = std::max(n, 1);                                                                           \
+    }                                                                                                         \
+    const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)sms[dev] * per_sm[dev])); \
+    kern<<<grid, 128, 0, st>>>(codes, raw, scales, mins, axis, (int)H, (int)T, (int)R, (int)D, bvt, ranks, out); \
+  }
+    if (R <= 4) KVF_RR(4)
+    else if (R <= 8) KVF_RR(8)
+    else if (R <= 12) KVF_RR(12)
+    else KVF_RR(16)
+#undef KVF_RR
+  } else if (D % 4 == 0 && smem <= 200 * 1024 && aligned(out, 16)) {
     auto kern = k_dequant_reconstruct<MODE, EXACT>;
     if (smem > kSmemOptIn) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
