@@ -620,35 +620,33 @@ __global__ void __launch_bounds__(256) k_calib_partials(const TIn* __restrict__ 
 }
 
 // calibration.rs:56-71: variance per head, clamped at 0, normalised by the max
-// (uniform 0.5 when the max is below 1e-12). One block; for each head the
-// threads sum a fixed, strided share of the partials and the block combines
-// them in a fixed order, so the result does not depend on scheduling.
+// (uniform 0.5 when the max is below 1e-12). One block; warp w sums the
+// partials of heads w, w + 8, ...: lane l adds every 32nd partial in order,
+// then a fixed shuffle tree combines the lanes, so the result does not depend
+// on scheduling.
 __global__ void __launch_bounds__(256) k_calib_finalize(const double* __restrict__ cpart, int H, int tiles,
                                                         double n, float* __restrict__ scores) {
   extern __shared__ double var[];
-  for (int h = 0; h < H; ++h) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int h = w; h < H; h += nw) {
     double s1 = 0.0, s2 = 0.0;
-    for (int k = threadIdx.x; k < tiles; k += blockDim.x) {
+    for (int k = lane; k < tiles; k += 32) {
       s1 += cpart[2 * ((size_t)h * tiles + k)];
       s2 += cpart[2 * ((size_t)h * tiles + k) + 1];
     }
-    block_sum2(s1, s2);
-    if (threadIdx.x == 0) {
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
       const double mean = s1 / n;
       const double v = (s2 / n) - (mean * mean);
       var[h] = (isnan(v) || v < 0.0) ? 0.0 : v;  // variance.max(0.0)
     }
-    __syncthreads();
-  }
-  __shared__ double maxv;
-  if (threadIdx.x == 0) {
-    double m = 0.0;
-    for (int h = 0; h < H; ++h) m = var[h] > m ? var[h] : m;
-    maxv = m;
   }
   __syncthreads();
+  double m = 0.0;
+  for (int h = 0; h < H; ++h) m = var[h] > m ? var[h] : m;
   for (int h = threadIdx.x; h < H; h += blockDim.x)
-    scores[h] = (maxv < 1e-12) ? 0.5f : (float)(var[h] / maxv);
+    scores[h] = (m < 1e-12) ? 0.5f : (float)(var[h] / m);
 }
 
 // ---- dequantize + reconstruct ------------------------------------------------

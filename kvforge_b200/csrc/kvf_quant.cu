@@ -335,22 +335,25 @@ __global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ pac
 
 // ---- per-channel codes from projected coefficients ---------------------------
 // P [H,T,R] f32 with its per-(head, r) min/max already folded into kmin/kmax
-// by the projection kernel: one thread per output byte forms the code(s),
-// packs INT4 nibbles over the flat index and counts the packed byte. The
-// first np threads also write the (scale, min) parameters.
+// by the projection kernel. A grid of a few blocks per SM; each thread takes
+// groups of eight consecutive codes (two 16-byte loads of P), walks their
+// (head, r) parameter index with counters instead of divisions, packs INT4
+// nibbles over the flat index and stores the group's bytes with one 4- or
+// 8-byte store; packed bytes are counted in per-warp shared histograms that
+// are merged once per block. The first np threads also write the (scale,
+// min) parameters.
 template <bool INT4, bool HIST>
 __global__ void __launch_bounds__(256) k_quantpack_channel(const float* __restrict__ P, uint64_t n, uint64_t T,
                                                            uint64_t R, const int* __restrict__ kmin,
                                                            const int* __restrict__ kmax, float levels,
                                                            float* __restrict__ scales, float* __restrict__ mins,
                                                            uint64_t np, uint8_t* __restrict__ out,
-                                                           uint32_t* __restrict__ hist) {
+                                                           uint32_t* __restrict__ hist, bool vec) {
   __shared__ uint32_t sh[8][256];
+  __shared__ float ps[kQpTable], pm[kQpTable], pi[kQpTable];
   const int w = threadIdx.x >> 5;
-  if (HIST) {
+  if (HIST)
     for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) (&sh[0][0])[i] = 0;
-    __syncthreads();
-  }
   const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = tid; i < np; i += stride) {
@@ -359,9 +362,8 @@ __global__ void __launch_bounds__(256) k_quantpack_channel(const float* __restri
     mins[i] = mn;
   }
   // (scale, min, 1/scale) per (head, r) in shared memory when they fit
-  __shared__ float ps[kQpTable], pm[kQpTable], pi[kQpTable];
   const bool table = np <= (uint64_t)kQpTable;
-  if (table) {
+  if (table)
     for (uint64_t i = threadIdx.x; i < np; i += blockDim.x) {
       const float mn = kfloat(kmin[i]), mx = kfloat(kmax[i]);
       const float sc = make_scale(mn, mx, levels);
@@ -369,33 +371,74 @@ __global__ void __launch_bounds__(256) k_quantpack_channel(const float* __restri
       pm[i] = mn;
       pi[i] = __frcp_rn(sc);
     }
-    __syncthreads();
-  }
-  const bool small = n < (1ull << 32);
-  auto code = [&](uint64_t i) -> uint32_t {
-    uint64_t g, c, p;
-    if (small) {
-      const uint32_t i32 = (uint32_t)i, g32 = i32 / (uint32_t)R;
-      g = g32;
-      c = i32 - g32 * (uint32_t)R;
-      p = (uint64_t)(g32 / (uint32_t)T) * R + c;
-    } else {
-      g = i / R;
-      c = i - g * R;
-      p = (g / T) * R + c;
-    }
-    if (table) return qcode_fast(__ldg(P + i), pm[p], ps[p], pi[p], levels);
+  __syncthreads();
+  const uint64_t per_head = T * R;
+  auto qc = [&](float v, uint64_t p) -> uint32_t {
+    if (table) return qcode_fast(v, pm[p], ps[p], pi[p], levels);
     const float mn = kfloat(__ldg(kmin + p)), mx = kfloat(__ldg(kmax + p));
     const float sc = make_scale(mn, mx, levels);
-    return qcode_fast(__ldg(P + i), mn, sc, __frcp_rn(sc), levels);
+    return qcode_fast(v, mn, sc, __frcp_rn(sc), levels);
   };
-  const uint64_t nb = INT4 ? (n + 1) / 2 : n;
-  for (uint64_t b = tid; b < nb; b += stride) {
-    uint32_t byte;
-    if (INT4) byte = code(2 * b) | ((2 * b + 1 < n) ? (code(2 * b + 1) << 4) : 0u);
-    else byte = code(b);
-    out[b] = (uint8_t)byte;
-    if (HIST) atomicAdd(&sh[w][byte], 1u);
+  const uint64_t groups = (n + 7) / 8;
+  for (uint64_t gi = tid; gi < groups; gi += stride) {
+    const uint64_t i0 = 8 * gi;
+    float v[8];
+    if (vec && i0 + 8 <= n) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(P + i0));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(P + i0) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = (i0 + k < n) ? __ldg(P + i0 + k) : 0.0f;
+    }
+    uint64_t h = i0 / per_head;
+    uint64_t c = i0 - h * per_head;
+    uint64_t rr = c % R;
+    uint64_t left = per_head - c;  // codes before the next head starts
+    uint32_t cd[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      cd[k] = (i0 + k < n) ? qc(v[k], h * R + rr) : 0u;  // no parameter lookups past the end
+      if (++rr == R) rr = 0;
+      if (--left == 0) {
+        ++h;
+        left = per_head;
+        rr = 0;
+      }
+    }
+    if (INT4) {  // bytes 4 gi .. 4 gi + 3
+      const uint64_t nb = (n + 1) / 2, b0 = 4 * gi;
+      uint32_t word = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t byte = (cd[2 * k] & 0xFu) | ((i0 + 2 * k + 1 < n) ? (cd[2 * k + 1] & 0xFu) << 4 : 0u);
+        word |= byte << (8 * k);
+        if (HIST && b0 + k < nb) atomicAdd(&sh[w][byte], 1u);
+      }
+      if (vec && b0 + 4 <= nb) {
+        *reinterpret_cast<uint32_t*>(out + b0) = word;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (b0 + k < nb) out[b0 + k] = (uint8_t)(word >> (8 * k));
+      }
+    } else {  // bytes 8 gi .. 8 gi + 7
+      if (vec && i0 + 8 <= n) {
+        uint2 u;
+        u.x = cd[0] | (cd[1] << 8) | (cd[2] << 16) | (cd[3] << 24);
+        u.y = cd[4] | (cd[5] << 8) | (cd[6] << 16) | (cd[7] << 24);
+        *reinterpret_cast<uint2*>(out + i0) = u;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (i0 + k < n) out[i0 + k] = (uint8_t)cd[k];
+      }
+      if (HIST)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (i0 + k < n) atomicAdd(&sh[w][cd[k]], 1u);
+    }
   }
   if (HIST) {
     __syncthreads();
@@ -487,14 +530,16 @@ cudaError_t launch_quantpack_channel(const float* P, size_t H, size_t T, size_t 
   const size_t np = H * R;
   const size_t nb = std::max(packed_len(n, data_type), np);
   if (nb == 0) return cudaSuccess;
-  const unsigned grid = (unsigned)std::min<size_t>((nb + 255) / 256, (size_t)kSMs * 16);
+  const size_t groups = (n + 7) / 8;
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>((std::max(groups, np) + 255) / 256, (size_t)kSMs * 2));
   const float levels = quant_levels(data_type);
+  const bool vec = aligned(P, 16) && aligned(out, 8);
   if (data_type == KVF_INT4) {
-    if (hist) k_quantpack_channel<true, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist);
-    else k_quantpack_channel<true, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr);
+    if (hist) k_quantpack_channel<true, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist, vec);
+    else k_quantpack_channel<true, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr, vec);
   } else {
-    if (hist) k_quantpack_channel<false, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist);
-    else k_quantpack_channel<false, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr);
+    if (hist) k_quantpack_channel<false, true><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, hist, vec);
+    else k_quantpack_channel<false, false><<<grid, 256, 0, st>>>(P, n, T, R, kmin, kmax, levels, scales, mins, np, out, nullptr, vec);
   }
   note_launches(1);
   return cudaGetLastError();
