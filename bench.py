@@ -45,15 +45,72 @@ def _peaks():
         return 6650.0, "fallback"
 
 
-def _traffic():
-    """Per-launch DRAM traffic of the dominant kernel from the committed ncu
-    summary (profiles/), scaled to the workload; None when absent."""
-    path = os.path.join(ROOT, "profiles", "reconstruct_traffic.json")
+def _traffic(kernel: str):
+    """Per-launch DRAM traffic (read + write bytes) of `kernel` from the committed
+    ncu summary (profiles/kernel_traffic.json); None when absent."""
+    path = os.path.join(ROOT, "profiles", "kernel_traffic.json")
     try:
         with open(path) as f:
-            return json.load(f)
+            return json.load(f).get(kernel)
     except Exception:
         return None
+
+
+def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
+    """Isolated launches of the step's bandwidth-bound kernels on layer 0, timed
+    with CUDA events on their own stream: value/key projection (+ per-token INT4
+    quantization for values) and value/key reconstruction. Algorithmic bytes per
+    launch: inputs read once plus outputs written once."""
+    _, k, v, kb, vb = lay
+    if kb is None:
+        return []
+    H, T, D = k.shape
+    st = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    ctx = L.context(dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    res = []
+
+    def timed(fn):
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                fn()
+            e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    for name, x, b, per_token in (("project_values_int4_per_token", v, vb, True), ("project_keys", k, kb, False)):
+        R = b.R
+        if per_token:
+            n = H * T * R
+            packed = torch.empty((n + 1) // 2, dtype=torch.uint8, device=x.device)
+            sc = torch.empty(H * T, device=x.device)
+            mn = torch.empty(H * T, device=x.device)
+            ms = timed(lambda: L.check(lib.kvf_fused_project_quantize(
+                ctx, P(x), 1, H, T, D, C.c_void_p(b.device_vt()), C.c_void_p(b.device_ranks()), R, 0, 1, P(packed),
+                P(sc), P(mn), sp)))
+            nbytes = x.numel() * 2 + (n + 1) // 2 + 8 * H * T
+            kern = "k_project (MODE 2: per-token INT4 epilogue)"
+        else:
+            Pk = torch.empty((H, T, R), dtype=torch.float32, device=x.device)
+            ms = timed(lambda: L.check(lib.kvf_project(ctx, P(x), 1, H, T, D, C.c_void_p(b.device_vt()),
+                                                       C.c_void_p(b.device_ranks()), R, P(Pk), sp)))
+            nbytes = x.numel() * 2 + 4 * H * T * R
+            kern = "k_project (MODE 0: coefficients)"
+        res.append({"name": name, "kernel": kern, "bytes": nbytes, "ms": ms, "R": R})
+    for name, b in (("reconstruct_values", vb), ("reconstruct_keys", kb)):
+        R = b.R
+        Pc = torch.zeros((H, T, R), dtype=torch.float32, device=k.device)
+        out = torch.empty((H, T, D), dtype=torch.float32, device=k.device)
+        ms = timed(lambda: L.check(lib.kvf_reconstruct(ctx, P(Pc), H, T, R, D, C.c_void_p(b.device_vt()),
+                                                       C.c_void_p(b.device_ranks()), P(out), sp)))
+        res.append({"name": name, "kernel": "k_reconstruct_reg (f32 coefficients)", "bytes": 4 * H * T * R + 4 * H * T * D,
+                    "ms": ms, "R": R})
+    return res
 
 
 class ClockSampler:
@@ -327,7 +384,11 @@ def gpu_arm(args):
         import torch.distributed as dist
         dist.barrier()
 
-    # end-to-end through the host-buffer C-ABI entry points
+    # end-to-end through the host-buffer C-ABI entry points: pinned host inputs
+    # in, f32 host outputs back, every step. The entry points return only when
+    # their host buffers are complete, so layers are spread over a few host
+    # threads, each with its own stream and output buffers: one layer's
+    # host->device copy overlaps another's device->host copy and compute.
     e2e = None
     if args.e2e_steps > 0:
         kh = [torch.empty((H, T, D), dtype=lay[1].dtype, pin_memory=True) for lay in layers]
@@ -335,30 +396,57 @@ def gpu_arm(args):
         for i, lay in enumerate(layers):
             kh[i].copy_(lay[1])
             vh[i].copy_(lay[2])
-        koh = torch.empty((H, T, D), dtype=torch.float32, pin_memory=True)
-        voh = torch.empty((H, T, D), dtype=torch.float32, pin_memory=True)
+        nthr = max(1, min(args.e2e_threads, len(layers)))
+        estreams = [torch.cuda.Stream(device=dev) for _ in range(nthr)]
+        eouts = [(torch.empty((H, T, D), dtype=torch.float32, pin_memory=True),
+                  torch.empty((H, T, D), dtype=torch.float32, pin_memory=True)) for _ in range(nthr)]
+        errs = []
+
+        def e2e_worker(j):
+            try:
+                sp = C.c_void_p(estreams[j].cuda_stream)
+                koh, voh = eouts[j]
+                for i in range(j, len(layers), nthr):
+                    l, _, _, kb, vb = layers[i]
+                    h = C.c_void_p()
+                    L.check(lib.kvf_compress_layer_host(ctx, C.c_void_p(kh[i].data_ptr()), C.c_void_p(vh[i].data_ptr()),
+                                                        in_code, H, T, D, l, C.byref(cfg), kb.handle if kb else None,
+                                                        vb.handle if vb else None, C.byref(h), sp))
+                    L.check(lib.kvf_decompress_layer_host(ctx, h, C.c_void_p(koh.data_ptr()),
+                                                          C.c_void_p(voh.data_ptr()), sp))
+                    lib.kvf_compressed_free(h)
+            except Exception as ex:  # reported after the join
+                errs.append(ex)
 
         def e2e_step():
-            for i, (l, _, _, kb, vb) in enumerate(layers):
-                h = C.c_void_p()
-                L.check(lib.kvf_compress_layer_host(ctx, C.c_void_p(kh[i].data_ptr()), C.c_void_p(vh[i].data_ptr()),
-                                                    in_code, H, T, D, l, C.byref(cfg), kb.handle if kb else None,
-                                                    vb.handle if vb else None, C.byref(h), sptr))
-                L.check(lib.kvf_decompress_layer_host(ctx, h, C.c_void_p(koh.data_ptr()), C.c_void_p(voh.data_ptr()),
-                                                      sptr))
-                lib.kvf_compressed_free(h)
+            ts = [threading.Thread(target=e2e_worker, args=(j,)) for j in range(nthr)]
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            if errs:
+                raise errs[0]
 
         e2e_step()
         torch.cuda.synchronize()
+        t0 = time.perf_counter()
         e0.record(stream)
+        for es in estreams:
+            es.wait_event(e0)
         for _ in range(args.e2e_steps):
             e2e_step()
+        for es in estreams:
+            ev = torch.cuda.Event()
+            ev.record(es)
+            stream.wait_event(ev)
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        e2e_wall_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
         e2e = {"ms": e2e_ms, "h2d": in_bytes, "d2h": orig_bytes}
     else:
         e2e_ms = float("nan")
+        e2e_wall_ms = float("nan")
 
     stats = {"layers": len(layers), "input_bytes": in_bytes, "compressed_bytes": comp_bytes,
              "original_bytes": orig_bytes, "ms": ms, **err}
@@ -367,6 +455,8 @@ def gpu_arm(args):
     e2e_per = gather_stats({"ms": e2e_ms, "input_bytes": in_bytes, "original_bytes": orig_bytes},
                            device=f"cuda:{dev}" if world > 1 else None)
     e2e_tot = reduce_stats(e2e_per)
+
+    kr = kernel_rooflines(lib, L, K, torch, layers[0], dev) if rank == 0 else []
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -390,10 +480,18 @@ def gpu_arm(args):
     value = tot["input_bytes"] / (step_ms / 1e3) / GB
     # algorithmic bytes per step: inputs + compressed (written) + compressed (read) + f32 outputs
     alg = tot["input_bytes"] + 2 * tot["compressed_bytes"] + tot["original_bytes"]
-    dom = max(prof.items(), key=lambda kv: kv[1][0])
-    dname, (dms, dcount, dbytes) = dom
-    achieved = (dbytes / dcount) / ((dms / dcount) / 1e3) / GB if dcount and dms > 0 else None
-    traffic = _traffic()
+    for r in kr:
+        r["achieved_gbs"] = r["bytes"] / (r["ms"] / 1e3) / GB
+        r["frac"] = r["achieved_gbs"] / peak
+    dom = max(kr, key=lambda r: r["ms"]) if kr else None
+    roof = None
+    if dom is not None:
+        traffic = _traffic(dom["name"])
+        roof = {"kernel": f'{dom["name"]}: {dom["kernel"]}', "bound": "hbm", "achieved": dom["achieved_gbs"],
+                "peak": peak, "unit": "GB/s", "frac": dom["frac"],
+                "traffic": traffic["bytes_per_launch"] if traffic else None,
+                "algorithmic_bytes_per_launch": dom["bytes"], "avg_launch_ms": dom["ms"], "peak_kind": peak_kind,
+                "timing": "isolated launches on layer 0 inside bench.py, CUDA events on the launching stream"}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
@@ -403,13 +501,10 @@ def gpu_arm(args):
         "rel_err": {"keys": (tot["err2_k"] / tot["ref2_k"]) ** 0.5, "values": (tot["err2_v"] / tot["ref2_v"]) ** 0.5},
         "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak,
                           "frac": alg / (step_ms / 1e3) / GB / peak, "peak_kind": peak_kind},
-        "roofline": {"kernel": dname, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": (achieved / peak) if achieved else None,
-                     "traffic": (traffic or {}).get("bytes_per_launch"),
-                     "algorithmic_bytes_per_launch": dbytes / dcount if dcount else None,
-                     "launches": dcount, "avg_launch_ms": dms / dcount if dcount else None,
-                     "peak_kind": peak_kind},
-        "stages_ms_per_step": {k: v[0] / args.steps for k, v in prof.items() if v[1]},
+        "roofline": roof,
+        "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac")}
+                             for r in kr],
+        "stages_ms_per_step_overlapped": {k: v[0] / args.steps for k, v in prof.items() if v[1]},
         "basis_ms_per_layer_untimed": 1e3 * t_basis / max(len(layers), 1),
         "gpu_launches": int(n1 - n0),
         "clocks": clk,
@@ -418,7 +513,9 @@ def gpu_arm(args):
         e2e_val = e2e_tot["input_bytes"] / (e2e_tot["ms"] / 1e3) / GB
         line["e2e"] = {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(e2e_tot["input_bytes"]),
                        "d2h_bytes_per_step": int(e2e_tot["original_bytes"]), "ms_per_step": e2e_tot["ms"],
-                       "api": "kvf_compress_layer_host + kvf_decompress_layer_host (pinned host buffers)"}
+                       "wall_ms_per_step_rank0": e2e_wall_ms,
+                       "api": "kvf_compress_layer_host + kvf_decompress_layer_host (pinned host buffers), "
+                              f"{args.e2e_threads} host threads with one stream each"}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -434,6 +531,7 @@ def main():
     ap.add_argument("--workload", default="llama3_8b_32k")
     ap.add_argument("--layers", type=int, default=0, help="number of layers (default: the workload's)")
     ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-threads", type=int, default=4, help="host threads (one stream each) for the e2e leg")
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -18,9 +18,13 @@
  *  - Calls are stream-ordered. The only host synchronisations are the ones a
  *    function documents (sizes that must reach the host, and the one-off basis
  *    step, which runs its eigen-solve on the host).
- *  - One kvf_ctx per device. Calls on one context may be issued from one host
- *    thread at a time; all scratch memory is taken per call from the device's
- *    stream-ordered pool, so calls on different streams do not share scratch.
+ *  - One kvf_ctx per device. Calls on one context may come from several host
+ *    threads at once, each issuing on its own stream; all scratch memory is
+ *    taken per call from the context's stream-ordered pool, so calls on
+ *    different streams share no scratch and never wait for one another. The
+ *    context has one device status word: a device-side error (corrupt stream,
+ *    expired wait) is reported by the next call that reads it, which may be
+ *    another thread's.
  *  - Layout: tensors are [num_heads, seq_len, head_dim] row-major, as in the
  *    reference KVCache (crates/kvforge-core/src/types.rs:5-12).
  */

@@ -5,15 +5,18 @@
 // Pipeline (crates/kvforge-cpu/src/pipeline.rs:38-186): keys are quantized
 // per channel and values per token; with projection each tensor is first
 // projected on its calibrated basis; with entropy coding the packed codes go
-// through the chunked rANS coder. Scratch memory comes from the device's
-// stream-ordered pool (cudaMallocAsync) and is released in stream order at the
-// end of each call; result buffers belong to the kvf_compressed object.
+// through the chunked rANS coder. Scratch memory comes from the context's
+// stream-ordered pool (cudaMallocFromPoolAsync) and is released in stream
+// order at the end of each call; result buffers belong to the kvf_compressed
+// object.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -69,15 +72,16 @@ struct DeviceGuard {
 // per-call scratch, released in stream order when the call returns
 struct Scratch {
   cudaStream_t st;
+  cudaMemPool_t pool;
   std::vector<void*> ptrs;
-  explicit Scratch(cudaStream_t s) : st(s) {}
+  Scratch(cudaStream_t s, cudaMemPool_t p) : st(s), pool(p) {}
   ~Scratch() {
     for (void* p : ptrs) cudaFreeAsync(p, st);
   }
   template <class T>
   T* get(size_t count) {
     void* p = nullptr;
-    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), st) != cudaSuccess) return nullptr;
+    if (cudaMallocFromPoolAsync(&p, std::max<size_t>(count, 1) * sizeof(T), pool, st) != cudaSuccess) return nullptr;
     ptrs.push_back(p);
     return static_cast<T*>(p);
   }
@@ -127,6 +131,10 @@ struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
   unsigned* d_status = nullptr;
+  // the context's own stream-ordered pool: freed blocks stay cached, and a
+  // block freed on one stream is reused on another only once its free has
+  // completed, so the pool never makes one caller stream wait for another
+  cudaMemPool_t pool = nullptr;
   // a layer's value tensor runs on a side stream paired with the caller's
   // stream while its key tensor runs on the caller's stream; fork/join events
   // order the two. One side stream per caller stream, made on first use, so
@@ -135,8 +143,13 @@ struct kvf_ctx {
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
   };
-  std::vector<std::pair<cudaStream_t, Side>> sides;
+  // a context may be used from several host threads at once (one caller
+  // stream each): the side streams and the profile records are guarded by mu;
+  // a deque keeps each Side at a fixed address as more are added
+  std::mutex mu;
+  std::deque<std::pair<cudaStream_t, Side>> sides;
   cudaError_t side_for(cudaStream_t st, Side** out) {
+    std::lock_guard<std::mutex> lock(mu);
     for (auto& kv : sides)
       if (kv.first == st) {
         *out = &kv.second;
@@ -161,6 +174,7 @@ struct kvf_ctx {
   std::vector<Rec> recs;
   std::vector<cudaEvent_t> spare;
   cudaEvent_t event() {
+    std::lock_guard<std::mutex> lock(mu);
     if (!spare.empty()) {
       cudaEvent_t e = spare.back();
       spare.pop_back();
@@ -190,6 +204,7 @@ struct StageTimer {
     if (a) {
       cudaEvent_t b = ctx->event();
       cudaEventRecord(b, st);
+      std::lock_guard<std::mutex> lock(ctx->mu);
       ctx->recs.push_back({stage, a, b, bytes});
     }
   }
@@ -214,7 +229,8 @@ struct kvf_compressed {
   template <class T>
   T* alloc(size_t count, cudaStream_t on) {
     void* p = nullptr;
-    if (cudaMallocAsync(&p, std::max<size_t>(count, 1) * sizeof(T), on) != cudaSuccess) return nullptr;
+    if (cudaMallocFromPoolAsync(&p, std::max<size_t>(count, 1) * sizeof(T), ctx->pool, on) != cudaSuccess)
+      return nullptr;
     owned.push_back(p);
     return static_cast<T*>(p);
   }
@@ -293,7 +309,7 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
                            size_t T, size_t D, int dt, int axis, const std::shared_ptr<BasisData>& basis,
                            bool entropy, bool calib, float* d_scores, TensorC* out, cudaStream_t st) {
   KVF_TRY(check_qcfg(dt, axis));
-  Scratch sc(st);
+  Scratch sc(st, ctx->pool);
   out->data_type = dt;
   out->axis = axis;
   out->H = H;
@@ -420,7 +436,7 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
 
 // decompress_tensor (crates/kvforge-cpu/src/pipeline.rs:75-97)
 kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStream_t st) {
-  Scratch sc(st);
+  Scratch sc(st, ctx->pool);
   const uint8_t* codes = t.d_data;
   if (t.has_freq) {
     uint8_t* dec = sc.get<uint8_t>(t.packed_len);
@@ -537,7 +553,7 @@ kvf_status compute_basis(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, si
   b->D = D;
   std::vector<double> G(H * D * D);
   {
-    Scratch sc(st);
+    Scratch sc(st, ctx->pool);
     const size_t tiles = gram_num_tiles(T);
     float* partial = sc.get<float>(H * tiles * D * D);
     double* gram = sc.get<double>(H * D * D);
@@ -740,14 +756,22 @@ kvf_status kvf_init(int device, kvf_ctx** out) {
   if (!g.ok) return fail(KVF_ERR_CUDA, "cudaSetDevice failed");
   auto* ctx = new kvf_ctx();
   ctx->device = device;
-  cudaMemPool_t pool;
-  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
-    uint64_t thr = UINT64_MAX;  // keep freed blocks cached in this process's pool
-    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  cudaMemPoolProps props{};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = device;
+  cudaError_t e = cudaMemPoolCreate(&ctx->pool, &props);
+  if (e == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    int no = 0;
+    e = cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &thr);
+    if (e == cudaSuccess) e = cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolReuseAllowInternalDependencies, &no);
   }
-  cudaError_t e = cudaMalloc(&ctx->d_status, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(unsigned));
   if (e != cudaSuccess) {
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
     delete ctx;
     return fail(KVF_ERR_CUDA, std::string("context allocation: ") + cudaGetErrorString(e));
   }
@@ -770,6 +794,9 @@ kvf_status kvf_destroy(kvf_ctx* ctx) {
     cudaEventDestroy(kv.second.join);
   }
   cudaFree(ctx->d_status);
+  // outstanding blocks (compressed objects still alive) keep the pool's
+  // memory until they are freed
+  if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
   delete ctx;
   return KVF_OK;
 }
@@ -811,6 +838,7 @@ kvf_status kvf_profile_read(kvf_ctx* ctx, double* ms, uint64_t* count, double* b
     if (bytes) bytes[i] = 0.0;
   }
   kvf_status st = KVF_OK;
+  std::lock_guard<std::mutex> lock(ctx->mu);
   for (auto& r : ctx->recs) {
     float t = 0.0f;
     cudaError_t e = cudaEventSynchronize(r.b);
@@ -861,7 +889,7 @@ kvf_status kvf_calibrate(kvf_ctx* ctx, const void* keys, int32_t in_dtype, size_
     return fail(KVF_ERR_INVALID_CONFIG, "Need at least " + std::to_string(min_tokens) +
                                             " tokens for calibration, got " + std::to_string(T));
   DeviceGuard g(ctx->device);
-  Scratch sc(S(stream));
+  Scratch sc(S(stream), ctx->pool);
   const size_t tiles = calib_partial_tiles(T, D);
   double* cpart = sc.get<double>(2 * H * tiles);
   if (!cpart) return fail(KVF_ERR_CUDA, "scratch allocation failed");
@@ -903,7 +931,7 @@ kvf_status kvf_quantize(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t
   KVF_TRY(check_qcfg(data_type, axis));
   KVF_TRY(check_shape(H, T, D));
   DeviceGuard g(ctx->device);
-  Scratch sc(S(stream));
+  Scratch sc(S(stream), ctx->pool);
   return quantize_into(sc, data, in_dtype, H, T, D, data_type, axis, packed, scales, mins, nullptr, S(stream));
 }
 
@@ -963,7 +991,7 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
   if (T == 0 || D == 0) return fail(KVF_ERR_PROJECTION, "Cannot project empty tensor");
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
-  Scratch sc(S(stream));
+  Scratch sc(S(stream), ctx->pool);
   cudaStream_t st = S(stream);
   const size_t n = H * T * R;
   ProjectOut po;
@@ -1017,7 +1045,7 @@ kvf_status kvf_rans_encode(kvf_ctx* ctx, const uint8_t* data, size_t n, uint8_t*
   }
   if (out_cap < rans_max_len(n, kRansChunk)) return fail(KVF_ERR_ENTROPY, "output capacity too small");
   if (!aligned(out, 4)) return fail(KVF_ERR_INVALID_CONFIG, "output buffer must be 4-byte aligned");
-  Scratch sc(st);
+  Scratch sc(st, ctx->pool);
   uint64_t* d_len = sc.get<uint64_t>(1);
   if (!d_len) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   KVF_CUDA(launch_histogram(data, n, freq, st));
@@ -1037,7 +1065,7 @@ kvf_status kvf_rans_decode(kvf_ctx* ctx, const uint8_t* comp, size_t comp_len, c
   if (!aligned(comp, 4)) return fail(KVF_ERR_INVALID_CONFIG, "container must be 4-byte aligned");
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
-  Scratch sc(st);
+  Scratch sc(st, ctx->pool);
   KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, freq, original_len, out, ctx->d_status, st));
   return read_status(ctx, st);
 }
@@ -1055,7 +1083,7 @@ kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t 
   if (plen == 0) return KVF_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
-  Scratch sc(st);
+  Scratch sc(st, ctx->pool);
   uint8_t* dec = sc.get<uint8_t>(plen);
   if (!dec) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   KVF_CUDA(launch_rans_decode(comp, comp_len, nullptr, freq, plen, dec, ctx->d_status, st));
@@ -1205,7 +1233,7 @@ kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const vo
   const size_t bytes = H * T * D * (in_dtype == KVF_IN_F16 ? 2 : 4);
   kvf_status s;
   {
-    Scratch sc(st);
+    Scratch sc(st, ctx->pool);
     uint8_t* dk = sc.get<uint8_t>(bytes);
     uint8_t* dv = sc.get<uint8_t>(bytes);
     if (!dk || !dv) return fail(KVF_ERR_CUDA, "scratch allocation failed");
@@ -1228,7 +1256,7 @@ kvf_status kvf_decompress_layer_host(kvf_ctx* ctx, const kvf_compressed* c, floa
   cudaStream_t st = S(stream);
   const size_t bytes = c->H * c->T * c->D * 4;
   {
-    Scratch sc(st);
+    Scratch sc(st, ctx->pool);
     float* dk = sc.get<float>(c->H * c->T * c->D);
     float* dv = sc.get<float>(c->H * c->T * c->D);
     if (!dk || !dv) return fail(KVF_ERR_CUDA, "scratch allocation failed");

@@ -523,9 +523,9 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   off += 2 * Rk * 4;
   off = (off + 15) & ~15;
   L.hist = off;
-  off += 256 * 4;
+  off += (MODE == 2) ? 256 * 4 : 0;
   L.cstage = off;
-  off += (MODE == 2) ? kProjRows * (int)R : 0;
+  off += (MODE == 2 && o.packed && (R & 1)) ? kProjRows * (int)R : 0;  // odd R packs through shared memory
   off = (off + 15) & ~15;
   L.bars = off;
   off += 8 * 8;
