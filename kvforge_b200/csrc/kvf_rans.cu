@@ -37,8 +37,8 @@
 namespace kvf {
 namespace {
 
-constexpr int kEncWarps = 2;  // encoder: chunks per block
-constexpr int kDecWarps = 2;       // decoder: chunks per block (one slot table per block)
+constexpr int kEncWarps = 4;  // encoder: chunks per block (one per scheduler)
+constexpr int kDecWarps = 4;       // decoder: chunks per block (one slot table per block, one per scheduler)
 constexpr int kDecBlockWarps = 8;  // every warp builds the slot tables; the extra ones then exit
 constexpr uint32_t kShift = 32 - kRansProbBits;  // a state >= q << kShift renormalises first
 
