@@ -384,6 +384,52 @@ def gpu_arm(args):
         import torch.distributed as dist
         dist.barrier()
 
+    # compress-only and decompress-only passes over the same layers and streams
+    # (untimed warm-up pass first); the handles of all layers stay alive between them
+    def split_pass():
+        handles = [None] * len(layers)
+
+        def comp():
+            start_ev.record(stream)
+            for w in workers:
+                w.wait_event(start_ev)
+            for i, (l, k, v, kb, vb) in enumerate(layers):
+                h = C.c_void_p()
+                L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), in_code, H,
+                                               T, D, l, C.byref(cfg), kb.handle if kb else None,
+                                               vb.handle if vb else None, C.byref(h), wptr[i % nstreams]))
+                handles[i] = h
+            for w, e in zip(workers, done_ev):
+                e.record(w)
+                stream.wait_event(e)
+
+        def decomp():
+            start_ev.record(stream)
+            for w in workers:
+                w.wait_event(start_ev)
+            for i in range(len(layers)):
+                wi = i % nstreams
+                L.check(lib.kvf_decompress_layer(ctx, handles[i], C.c_void_p(outs[wi][0].data_ptr()),
+                                                 C.c_void_p(outs[wi][1].data_ptr()), wptr[wi]))
+            for w, e in zip(workers, done_ev):
+                e.record(w)
+                stream.wait_event(e)
+
+        t = []
+        for f in (comp, decomp):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            f()
+            b.record(stream)
+            t.append((a, b))
+        torch.cuda.synchronize()
+        for h in handles:
+            lib.kvf_compressed_free(h)
+        return [a.elapsed_time(b) for a, b in t]
+
+    split_pass()
+    split_ms = np.mean([split_pass() for _ in range(max(1, min(args.steps, 10)))], axis=0)
+
     # end-to-end through the host-buffer C-ABI entry points: pinned host inputs
     # in, f32 host outputs back, every step. The entry points return only when
     # their host buffers are complete, so layers are spread over a few host
@@ -449,7 +495,8 @@ def gpu_arm(args):
         e2e_wall_ms = float("nan")
 
     stats = {"layers": len(layers), "input_bytes": in_bytes, "compressed_bytes": comp_bytes,
-             "original_bytes": orig_bytes, "ms": ms, **err}
+             "original_bytes": orig_bytes, "ms": ms, "compress_ms": float(split_ms[0]),
+             "decompress_ms": float(split_ms[1]), **err}
     per = gather_stats(stats, device=f"cuda:{dev}" if world > 1 else None)
     tot = reduce_stats(per)
     e2e_per = gather_stats({"ms": e2e_ms, "input_bytes": in_bytes, "original_bytes": orig_bytes},
@@ -504,6 +551,11 @@ def gpu_arm(args):
         "roofline": roof,
         "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac")}
                              for r in kr],
+        "compress_only": {"ms_per_step": tot["compress_ms"],
+                          "gbs": tot["input_bytes"] / (tot["compress_ms"] / 1e3) / GB},
+        "decompress_only": {"ms_per_step": tot["decompress_ms"],
+                            "gbs": tot["input_bytes"] / (tot["decompress_ms"] / 1e3) / GB,
+                            "output_gbs": tot["original_bytes"] / (tot["decompress_ms"] / 1e3) / GB},
         "stages_ms_per_step_overlapped": {k: v[0] / args.steps for k, v in prof.items() if v[1]},
         "basis_ms_per_layer_untimed": 1e3 * t_basis / max(len(layers), 1),
         "gpu_launches": int(n1 - n0),

@@ -8,7 +8,8 @@ squared error, reference energy, times), over NCCL on GPUs or gloo on CPUs.
 from __future__ import annotations
 
 STAT_KEYS = ("layers", "input_bytes", "compressed_bytes", "original_bytes", "err2_k", "ref2_k", "err2_v",
-             "ref2_v", "ms")
+             "ref2_v", "ms", "compress_ms", "decompress_ms")
+TIME_KEYS = ("ms", "compress_ms", "decompress_ms")
 
 
 def layer_shard(num_layers: int, world_size: int, rank: int) -> range:
@@ -37,9 +38,9 @@ def gather_stats(stats: dict, device=None, group=None) -> list:
 
 
 def reduce_stats(per_rank: list) -> dict:
-    """Sums over ranks; ms is the max (the slowest rank bounds the job)."""
+    """Sums over ranks; times are the max (the slowest rank bounds the job)."""
     tot = {k: 0.0 for k in STAT_KEYS}
     for s in per_rank:
         for k in STAT_KEYS:
-            tot[k] = max(tot[k], s[k]) if k == "ms" else tot[k] + s[k]
+            tot[k] = max(tot[k], s[k]) if k in TIME_KEYS else tot[k] + s[k]
     return tot
