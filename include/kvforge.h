@@ -92,7 +92,10 @@ const char* kvf_last_error(void);
 int kvf_abi_version(void);
 /* 1: reconstruction uses separate multiply and add in the reference's order
  * (projection.rs:160-166), bit-identical to the CPU oracle.
- * 0 (default): one fused multiply-add per term (same order), within 1e-6. */
+ * 0 (default): head_dim 128 with at most 16 coefficients runs as a tcgen05
+ * tensor-core GEMM (operands split into two tf32 parts, three products),
+ * other shapes as one fused multiply-add per term in the same order; within
+ * relative Frobenius error 1e-5 of the reference loop. */
 kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
 /* waits for `stream` and reports any error a device kernel recorded
  * (corrupt rANS container, bounded wait expiry) since the last check */

@@ -451,7 +451,7 @@ kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStr
     StageTimer tm(ctx, KVF_STAGE_RECONSTRUCT, out_bytes + (double)t.H * t.basis->R * t.D * 4, st);
     KVF_CUDA(launch_dequant_reconstruct(codes, nullptr, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T,
                                         t.qcols, t.D, t.basis->d_vt, t.basis->d_ranks, ctx->exact_reconstruct,
-                                        out, st));
+                                        out, ctx->d_status, st));
   } else {
     StageTimer tm(ctx, KVF_STAGE_DEQUANTIZE, out_bytes, st);
     KVF_CUDA(launch_dequantize(codes, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T, t.D, out, st));
@@ -976,7 +976,7 @@ kvf_status kvf_reconstruct(kvf_ctx* ctx, const float* projected, size_t H, size_
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
   KVF_CUDA(launch_dequant_reconstruct(nullptr, projected, nullptr, nullptr, KVF_F32, KVF_PER_TOKEN, H, T, R, D,
-                                      basis_vt, ranks, ctx->exact_reconstruct, out, S(stream)));
+                                      basis_vt, ranks, ctx->exact_reconstruct, out, ctx->d_status, S(stream)));
   return KVF_OK;
 }
 

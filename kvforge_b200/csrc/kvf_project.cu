@@ -67,14 +67,17 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 // read with broadcast 16-byte loads at compile-time offsets; each load feeds
 // both of a thread's rows.
 //
-// TMA variant (rows a multiple of 64 bytes, 16-byte aligned input): a tile is
-// streamed as column blocks of 256 rows x 64 bytes (16 KB), each one 2-D
-// tensor copy (cp.async.bulk.tensor, no multicast) with the 64-byte swizzle,
-// several blocks in flight per CTA; the accumulators stay in registers across
-// a tile's column blocks. The swizzle stores 16-byte chunk j of a 64-byte row
-// at j ^ (bits 7-8 of the row's address), so the reads of eight consecutive
-// rows fall on distinct banks. Small stages keep several CTAs resident per
-// SM. Waits are bounded: a wait that expires raises the device timeout status.
+// TMA variant (rows a multiple of 64 bytes, 16-byte aligned input): each warp
+// streams its own 64 rows of a tile as column blocks of 64 rows x 64 bytes
+// (4 KB), each one 2-D tensor copy (cp.async.bulk.tensor, no multicast) with
+// the 64-byte swizzle, issued by lane 0 into the warp's own stages and
+// mbarriers, several in flight; the accumulators stay in registers across a
+// tile's column blocks. Warps synchronise with each other only when the head
+// (and so the shared basis) changes. The swizzle stores 16-byte chunk j of a
+// 64-byte row at j ^ (bits 7-8 of the row's address), so the reads of eight
+// consecutive rows fall on distinct banks. Small stages keep several CTAs
+// resident per SM. Waits are bounded: a wait that expires raises the device
+// timeout status.
 // Generic variant: scalar loads from global memory.
 //
 // Epilogues (each thread stores its own rows; consecutive rows are contiguous):
@@ -87,7 +90,9 @@ constexpr int kProjThreads = 128;
 constexpr int kProjNR = 2;                           // token rows per thread
 constexpr int kProjRows = kProjThreads * kProjNR;    // token rows per tile
 constexpr int kColBytes = 64;                        // bytes of each row per streamed column block
-constexpr int kColStage = kProjRows * kColBytes;
+constexpr int kProjWarps = kProjThreads / 32;
+constexpr int kWarpRows = kProjRows / kProjWarps;    // token rows of a tile streamed by one warp
+constexpr int kWarpStage = kWarpRows * kColBytes;    // bytes of one warp's stage
 constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before a wait gives up
 
 template <typename TIn>
@@ -153,8 +158,8 @@ struct ProjSmem {
   int keys;    // [2 * Rk] int (MODE 1)
   int hist;    // [256] u32 (MODE 2)
   int cstage;  // [kProjRows][R] code bytes (MODE 2, odd R packing)
-  int bars;    // [stages] u64 (TMA)
-  int xbuf;    // [stages][kColStage] (TMA), 1024-byte aligned
+  int bars;    // [warps][stages] u64 stage barriers (TMA)
+  int xbuf;    // [warps][stages][kWarpStage] (TMA), 1024-byte aligned
   int stages;
   int total;
 };
@@ -191,9 +196,10 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
   int* skmax = skmin + Rk;
   uint32_t* shist = reinterpret_cast<uint32_t*>(smraw + L.hist);
   uint8_t* cstage = smraw + L.cstage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smraw + L.bars);
-  uint8_t* xbuf = smraw + L.xbuf;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  // this warp's pipeline: its stage barriers and stage buffers
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(smraw + L.bars) + w * L.stages;
+  uint8_t* wbuf = smraw + L.xbuf + (size_t)w * L.stages * kWarpStage;
   const int tiles = (T + kProjRows - 1) / kProjRows;
   const long long items = (long long)H * tiles;
   const long long i0 = items * blockIdx.x / gridDim.x;
@@ -205,22 +211,25 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
   const bool hist_on = (MODE == 2) && o.hist != nullptr;
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
-  if (TMA && tid == 0) {
-    for (int s = 0; s < L.stages; ++s) mbar_init(&bars[s], 1);
+  if (TMA && lane == 0) {
+    for (int s = 0; s < L.stages; ++s) mbar_init(&wbar[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  // unit u = column block (u mod ncb) of item (u / ncb), into stage u mod stages
+  // unit u = column block (u mod ncb) of item (u / ncb); this warp's 64 rows of
+  // it go to stage u mod stages, copied by lane 0
   long long issued = 0;
   auto issue = [&](long long u) {
-    if (TMA && tid == 0) {
+    if (!TMA || u >= units) return;
+    if (lane == 0) {
       const long long it = i0 + u / ncb;
       const int cb = (int)(u % ncb);
       const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
       const int s = (int)(u % L.stages);
-      mbar_expect_tx(&bars[s], (uint32_t)kColStage);
-      tma_load_2d(xbuf + (size_t)s * kColStage, &xmap, cb * kColElems, h * T + tile * kProjRows, &bars[s]);
+      mbar_expect_tx(&wbar[s], (uint32_t)kWarpStage);
+      tma_load_2d(wbuf + (size_t)s * kWarpStage, &xmap, cb * kColElems, h * T + tile * kProjRows + w * kWarpRows,
+                  &wbar[s]);
     }
     issued = u + 1;
   };
@@ -232,10 +241,13 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
       }
   };
 
-  if (TMA)
-    for (long long u = 0; u < L.stages - 1 && u < units; ++u) issue(u);
+  for (long long u = 0; u < L.stages - 1; ++u) issue(u);
   int cur_h = -1, rank = 0;
-  long long stuck = -1;  // the unit whose wait expired
+  // A wait that runs out makes the warp dead: it computes and stores nothing
+  // more but still reaches every block barrier, so no other warp is left
+  // waiting; at the end it waits (bounded) for copies it has in flight.
+  bool dead = false;
+  long long stuck = -1;
   for (long long li = 0; li < nit; ++li) {
     const long long it = i0 + li;
     const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
@@ -243,11 +255,31 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
     const int nrows = min(kProjRows, T - tile * kProjRows);
     bool ok[kProjNR];
     size_t g[kProjNR];
+    int wrow[kProjNR];  // the row within this warp's 64
 #pragma unroll
     for (int rr = 0; rr < kProjNR; ++rr) {
-      const int row = tid + rr * kProjThreads;  // this thread's rows of the tile
+      wrow[rr] = lane + 32 * rr;
+      const int row = w * kWarpRows + wrow[rr];
       ok[rr] = row < nrows;
       g[rr] = g0 + (ok[rr] ? row : 0);
+    }
+    if (h != cur_h) {  // block-uniform: this head's basis
+      __syncthreads();  // every warp is done with the previous head's basis and keys
+      flush_keys(cur_h);
+      const uint64_t rk = ranks[h];
+      rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
+      const float* B = bvt + (size_t)h * R * D;
+      for (int i = tid; i < D * Rpad; i += blockDim.x) {
+        const int c = i / Rpad, r = i - c * Rpad;
+        vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
+      }
+      if (MODE == 1)
+        for (int r = tid; r < R; r += blockDim.x) {
+          skmin[r] = fkey(INFINITY);
+          skmax[r] = fkey(-INFINITY);
+        }
+      __syncthreads();
+      cur_h = h;
     }
     double s1 = 0.0, s2 = 0.0;
     for (int rg = 0; rg < R; rg += RG) {
@@ -259,41 +291,24 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
       for (int cb = 0; cb < ncb; ++cb) {
         const long long u = li * ncb + cb;
         if (TMA) {
-          const int s = (int)(u % L.stages);
-          const bool ok_wait = mbar_wait(&bars[s], (uint32_t)((u / L.stages) & 1));
-          // also: every thread is done with unit u - 1, whose stage is refilled next
-          if (__syncthreads_or(!ok_wait)) {
-            stuck = u;
-            break;
-          }
-          if (u + L.stages - 1 < units) issue(u + L.stages - 1);
-        } else if (cb == 0) {
-          __syncthreads();
-        }
-        if (cb == 0 && rg == 0 && h != cur_h) {  // block-uniform: this head's basis
-          flush_keys(cur_h);
-          const uint64_t rk = ranks[h];
-          rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
-          const float* B = bvt + (size_t)h * R * D;
-          for (int i = tid; i < D * Rpad; i += blockDim.x) {
-            const int c = i / Rpad, r = i - c * Rpad;
-            vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
-          }
-          if (MODE == 1)
-            for (int r = tid; r < R; r += blockDim.x) {
-              skmin[r] = fkey(INFINITY);
-              skmax[r] = fkey(-INFINITY);
+          if (!dead) {
+            const bool okw = mbar_wait(&wbar[u % L.stages], (uint32_t)((u / L.stages) & 1));
+            if (!__all_sync(0xffffffffu, okw)) {
+              dead = true;
+              stuck = u;
             }
-          __syncthreads();
-          cur_h = h;
+          }
+          __syncwarp();  // every lane is done with unit u - 1, whose stage is refilled next
+          if (!dead) issue(u + L.stages - 1);
         }
+        if (dead) continue;
         if (TMA) {  // single r-group: vT rows are RG floats
           constexpr int PV = Seg<TIn>::PV;
           const uint8_t* sb[kProjNR];
           int sw[kProjNR];
 #pragma unroll
           for (int rr = 0; rr < kProjNR; ++rr) {
-            sb[rr] = xbuf + (size_t)(u % L.stages) * kColStage + (tid + rr * kProjThreads) * kColBytes;
+            sb[rr] = wbuf + (size_t)(u % L.stages) * kWarpStage + wrow[rr] * kColBytes;
             sw[rr] = (int)(smem_addr(sb[rr]) >> 7) & 3;  // the swizzle XORs address bits 4-5 with bits 7-8
           }
 #pragma unroll
@@ -337,7 +352,6 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
           }
         }
       }
-      if (stuck >= 0) break;
       float acc[kProjNR][RG];
 #pragma unroll
       for (int rr = 0; rr < kProjNR; ++rr)
@@ -350,7 +364,7 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
         for (int r = 0; r < RG; ++r)
           if (rg + r >= rank) acc[rr][r] = 0.0f;  // projection.rs:96
 
-      if (MODE == 1) {  // column min/max of this tile into the block's keys
+      if (MODE == 1 && !dead) {  // column min/max of this tile into the block's keys
 #pragma unroll
         for (int r = 0; r < RG; ++r) {
           if (rg + r < R) {  // warp-uniform
@@ -359,14 +373,14 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
             for (int rr = 0; rr < kProjNR; ++rr)
               if (ok[rr]) mm_update(acc[rr][r], mn, mx);
             warp_minmax(mn, mx);
-            if ((tid & 31) == 0) {
+            if (lane == 0) {
               atomicMin(&skmin[rg + r], fkey(mn));
               atomicMax(&skmax[rg + r], fkey(mx));
             }
           }
         }
       }
-      if (MODE == 0 || MODE == 1) {
+      if ((MODE == 0 || MODE == 1) && !dead) {
 #pragma unroll
         for (int rr = 0; rr < kProjNR; ++rr)
           if (ok[rr]) {
@@ -382,47 +396,49 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
                 if (rg + r < R) pr[r] = acc[rr][r];
             }
           }
-      } else {  // MODE 2 (R <= RG)
+      } else if (MODE == 2) {  // R <= RG
         const bool direct = o.packed == nullptr || (R & 1) == 0;
+        if (!dead) {
 #pragma unroll
-        for (int rr = 0; rr < kProjNR; ++rr) {
-          float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-          for (int r = 0; r < RG; ++r)
-            if (r < R) mm_update(acc[rr][r], mn, mx);
-          const float scale = make_scale(mn, mx, o.levels);
-          const float inv = __frcp_rn(scale);
-          uint32_t cd[RG];
-#pragma unroll
-          for (int r = 0; r < RG; ++r) cd[r] = (r < R) ? qcode_fast(acc[rr][r], mn, scale, inv, o.levels) : 0u;
-          if (ok[rr]) {
-            o.scales[g[rr]] = scale;
-            o.mins[g[rr]] = mn;
-          }
-          if (!direct) {  // odd R: pairs run across rows; pack the tile through shared memory
+          for (int rr = 0; rr < kProjNR; ++rr) {
+            float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
             for (int r = 0; r < RG; ++r)
-              if (r < R) cstage[(tid + rr * kProjThreads) * R + r] = (uint8_t)cd[r];
-          } else if (ok[rr] && o.packed) {  // this row's codes start on a byte boundary
-            uint8_t* dp = o.packed + (g[rr] * R) / 2;
+              if (r < R) mm_update(acc[rr][r], mn, mx);
+            const float scale = make_scale(mn, mx, o.levels);
+            const float inv = __frcp_rn(scale);
+            uint32_t cd[RG];
 #pragma unroll
-            for (int b = 0; b < RG / 2; ++b)
-              if (2 * b < R) {
-                const uint32_t byte = (cd[2 * b] & 0xFu) | ((cd[2 * b + 1] & 0xFu) << 4);
-                dp[b] = (uint8_t)byte;
-                if (hist_on) atomicAdd(&shist[byte], 1u);
-              }
-          } else if (ok[rr]) {
-            uint8_t* dc = o.codes + g[rr] * R;
+            for (int r = 0; r < RG; ++r) cd[r] = (r < R) ? qcode_fast(acc[rr][r], mn, scale, inv, o.levels) : 0u;
+            if (ok[rr]) {
+              o.scales[g[rr]] = scale;
+              o.mins[g[rr]] = mn;
+            }
+            if (!direct) {  // odd R: pairs run across rows; pack the tile through shared memory
 #pragma unroll
-            for (int r = 0; r < RG; ++r)
-              if (r < R) {
-                dc[r] = (uint8_t)cd[r];
-                if (hist_on) atomicAdd(&shist[cd[r]], 1u);
-              }
+              for (int r = 0; r < RG; ++r)
+                if (r < R) cstage[(w * kWarpRows + wrow[rr]) * R + r] = (uint8_t)cd[r];
+            } else if (ok[rr] && o.packed) {  // this row's codes start on a byte boundary
+              uint8_t* dp = o.packed + (g[rr] * R) / 2;
+#pragma unroll
+              for (int b = 0; b < RG / 2; ++b)
+                if (2 * b < R) {
+                  const uint32_t byte = (cd[2 * b] & 0xFu) | ((cd[2 * b + 1] & 0xFu) << 4);
+                  dp[b] = (uint8_t)byte;
+                  if (hist_on) atomicAdd(&shist[byte], 1u);
+                }
+            } else if (ok[rr]) {
+              uint8_t* dc = o.codes + g[rr] * R;
+#pragma unroll
+              for (int r = 0; r < RG; ++r)
+                if (r < R) {
+                  dc[r] = (uint8_t)cd[r];
+                  if (hist_on) atomicAdd(&shist[cd[r]], 1u);
+                }
+            }
           }
         }
-        if (!direct) {
+        if (!direct) {  // block-uniform
           __syncthreads();
           const int cnt = nrows * R;
           uint8_t* dp = o.packed + (g0 * R) / 2;
@@ -435,27 +451,26 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
         }
       }
     }
-    if (stuck >= 0) break;
-    if (CALIB) {
-      block_sum2(s1, s2);
-      if (tid == 0) {
-        const size_t slot = (size_t)h * tiles + tile;
+    if (CALIB && !dead) {  // this warp's share of the item, one partial slot per warp
+      s1 = warp_sum(s1);
+      s2 = warp_sum(s2);
+      if (lane == 0) {
+        const size_t slot = ((size_t)h * tiles + tile) * kProjWarps + w;
         o.cpart[2 * slot] = s1;
         o.cpart[2 * slot + 1] = s2;
       }
     }
-  }
-  if (stuck >= 0) {
-    // copies still in flight land (bounded waits) before the block's shared memory is released
-    if (tid == 0 && o.status) atomicOr(o.status, kDevErrTimeout);
-    for (long long u = stuck; u < issued; ++u) mbar_wait(&bars[u % L.stages], (uint32_t)((u / L.stages) & 1));
-    return;
   }
   __syncthreads();
   flush_keys(cur_h);
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x)
       if (shist[i]) atomicAdd(&o.hist[i], shist[i]);
+  if (dead) {
+    // copies still in flight land (bounded waits) before the block's shared memory is released
+    if (lane == 0 && o.status) atomicOr(o.status, kDevErrTimeout);
+    for (long long u = stuck; u < issued; ++u) mbar_wait(&wbar[u % L.stages], (uint32_t)((u / L.stages) & 1));
+  }
 }
 
 struct LaunchCache {
@@ -463,18 +478,8 @@ struct LaunchCache {
   int per_sm = 0;
 };
 
-// cuTensorMapEncodeTiled from the driver, looked up once (nullptr when absent)
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encode_fn());
 }
 
 // [H*T rows, D columns] of TIn, boxes of kProjRows rows x 64 bytes, 64-byte swizzle
@@ -484,7 +489,7 @@ bool encode_rows_map(CUtensorMap* map, const TIn* x, size_t rows, size_t D) {
   if (!enc) return false;
   const cuuint64_t gdim[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t gstride[1] = {(cuuint64_t)(D * sizeof(TIn))};
-  const cuuint32_t box[2] = {(cuuint32_t)(kColBytes / sizeof(TIn)), (cuuint32_t)kProjRows};
+  const cuuint32_t box[2] = {(cuuint32_t)(kColBytes / sizeof(TIn)), (cuuint32_t)kWarpRows};
   const cuuint32_t estride[2] = {1, 1};
   const CUtensorMapDataType dt =
       sizeof(TIn) == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -528,11 +533,11 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   off += (MODE == 2 && o.packed && (R & 1)) ? kProjRows * (int)R : 0;  // odd R packs through shared memory
   off = (off + 15) & ~15;
   L.bars = off;
-  off += 8 * 8;
+  off += 8 * kProjWarps * 4;  // up to 4 stage barriers per warp
   off = (off + 1023) & ~1023;  // swizzled stages start on a 1024-byte boundary
   L.xbuf = off;
   L.stages = TMA ? 3 : 0;
-  off += L.stages * kColStage;
+  off += kProjWarps * L.stages * kWarpStage;
   L.total = off;
   if (L.total > max_dyn[dev]) return cudaErrorInvalidValue;
   if (L.total > opted[dev] && L.total > 48 * 1024 - 1024) {
@@ -1076,7 +1081,21 @@ cudaError_t calib_static_scratch(int device, double** out) {
   return cudaSuccess;
 }
 
-size_t project_num_tiles(size_t T) { return (T + kProjRows - 1) / kProjRows; }
+void* tensor_map_encode_fn() {
+  static std::once_flag once;
+  static void* fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = p;
+  });
+  return fn;
+}
+
+// calibration partial slots per head of the projection kernel: one per (tile, warp)
+size_t project_num_tiles(size_t T) { return ((T + kProjRows - 1) / kProjRows) * kProjWarps; }
 
 cudaError_t launch_project(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                            const float* basis_vt, const uint64_t* ranks, size_t R, const ProjectOut& o,
@@ -1118,9 +1137,14 @@ cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t til
 cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
                                        const float* mins, int data_type, int axis, size_t H,
                                        size_t T, size_t R, size_t D, const float* basis_vt,
-                                       const uint64_t* ranks, int exact, float* out,
+                                       const uint64_t* ranks, int exact, float* out, unsigned* status,
                                        cudaStream_t st) {
   if (H == 0 || T == 0 || D == 0) return cudaSuccess;
+  if (!exact) {  // tensor cores where the shape allows them
+    const cudaError_t e = launch_reconstruct_tc(codes, raw, scales, mins, data_type, axis, H, T, R, D, basis_vt,
+                                                ranks, out, status, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   const int mode = raw ? 0 : (data_type == KVF_INT8 ? 1 : 2);
 #define KVF_DR(M)                                                                                      \
   return exact ? dequant_reconstruct_mode<M, true>(codes, raw, scales, mins, axis, H, T, R, D, basis_vt, ranks, out, st) \

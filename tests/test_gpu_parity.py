@@ -3,9 +3,11 @@ checked against the CPU oracle on the same seeded inputs.
 
 Bars: quantized codes, scales, mins, dequantized values, projected
 coefficients, rANS containers and compression ratios are bit-exact; the
-fused-multiply-add reconstruction is within relative Frobenius error 1e-6
-(bit-exact in the exact-reconstruction mode); calibration scores within 1e-6
-relative."""
+default reconstruction (tcgen05 split-tf32 GEMM for head_dim 128 and rank
+<= 16, fused multiply-add otherwise) is within relative Frobenius error
+REC_TOL = 1e-5 of the reference's loop, ten times inside the 1e-4 that the
+f32 projection/reconstruction contract allows, and bit-exact in the
+exact-reconstruction mode; calibration scores within 1e-6 relative."""
 import ctypes as C
 
 import numpy as np
@@ -16,6 +18,8 @@ pytestmark = pytest.mark.gpu
 
 INT4, INT8 = 0, 1
 PC, PT = 0, 1
+# relative Frobenius error of the default (tensor-core / fused) reconstruction
+REC_TOL = 1e-5
 
 
 def dev(x):
@@ -168,7 +172,7 @@ def test_reconstruct_parity(kvf, oracle, shape, thr):
     ref = oracle.reconstruct(Po, bvt, ranks)
     pr = kvf.GpuProjector()
     out = host(pr.reconstruct(dev(Po), basis))
-    assert rel(out, ref) < 1e-6
+    assert rel(out, ref) < REC_TOL
     ctx = L.context(0)
     L.check(L.lib().kvf_set_exact_reconstruct(ctx, 1))
     try:
@@ -176,6 +180,62 @@ def test_reconstruct_parity(kvf, oracle, shape, thr):
     finally:
         L.check(L.lib().kvf_set_exact_reconstruct(ctx, 0))
     assert np.array_equal(bits(out_exact), bits(ref))
+
+
+def _exact(L, on):
+    L.check(L.lib().kvf_set_exact_reconstruct(L.context(0), 1 if on else 0))
+
+
+@pytest.mark.parametrize("H,T,R,ranks", [(1, 1, 1, [1]), (2, 127, 3, [3, 2]), (3, 128, 8, [8, 8, 5]),
+                                         (2, 129, 9, [9, 1]), (2, 1000, 16, [16, 12]), (5, 300, 13, [13, 0, 7, 13, 4])])
+def test_tensor_core_reconstruct_raw(kvf, oracle, H, T, R, ranks):
+    """head_dim 128, R <= 16: the tcgen05 path (partial tiles, ranks below R,
+    rank 0) against the reference loop; the exact mode stays bit-exact."""
+    from kvforge_b200 import _lib as L
+    rng = np.random.default_rng(H * 1000 + T + R)
+    D = 128
+    bvt = rng.standard_normal((H, R, D)).astype(np.float32) / np.sqrt(D)
+    rk = np.asarray(ranks, np.uint64)
+    Po = (rng.standard_normal((H, T, R)) * 4).astype(np.float32)
+    ref = oracle.reconstruct(Po, bvt, rk)
+    basis = kvf.Basis.from_host(bvt, rk)
+    pr = kvf.GpuProjector()
+    out = host(pr.reconstruct(dev(Po), basis))
+    assert rel(out, ref) < REC_TOL
+    _exact(L, True)
+    try:
+        out_exact = host(pr.reconstruct(dev(Po), basis))
+    finally:
+        _exact(L, False)
+    assert np.array_equal(bits(out_exact), bits(ref))
+
+
+@pytest.mark.parametrize("dt", [INT8, INT4])
+@pytest.mark.parametrize("shape,thr", [((2, 300, 128), 0.9), ((3, 77, 128), 0.75)])
+def test_tensor_core_reconstruct_codes(kvf, oracle, dt, shape, thr):
+    """Projected INT8 and INT4 codes, keys per channel and values per token,
+    decompressed on the tcgen05 path against the reference pipeline."""
+    from kvforge_b200 import _lib as L
+    from kvforge_b200 import synth
+    H, T, D = shape
+    k, v = synth.numpy_layer(H, T, D, seed=T + dt, rank=10, dtype="float16")
+    cfg = kvf.config_from_preset("balanced")
+    cfg.key_data_type = cfg.value_data_type = dt
+    cfg.projection_variance_threshold = thr
+    kb = kvf.Basis.compute(dev(k), thr, max_rank=12)
+    vb = kvf.Basis.compute(dev(v), thr, max_rank=12)
+    assert kb.R <= 12 and vb.R <= 12
+    c = kvf.CompressionPipeline().compress_with_config(kvf.KVCache(dev(k), dev(v), 0), cfg, kb, vb)
+    kr = oracle.decompress_tensor(oracle.compress_tensor(k.astype(np.float32), dt, PC, kb.host()[:2]))
+    vr = oracle.decompress_tensor(oracle.compress_tensor(v.astype(np.float32), dt, PT, vb.host()[:2]))
+    out = kvf.decompress(c)
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
+    _exact(L, True)
+    try:
+        out = kvf.decompress(c)
+    finally:
+        _exact(L, False)
+    assert np.array_equal(bits(out.keys()), bits(kr)) and np.array_equal(bits(out.values()), bits(vr))
 
 
 @pytest.mark.parametrize("shape,thr,f16", [((2, 400, 16), 0.9, False), ((4, 4096, 128), 0.75, True),
@@ -303,7 +363,7 @@ def test_pipeline_parity(kvf, oracle, preset, shape, f16):
     c, co = _pipeline_case(kvf, oracle, k, v, preset)
     kr, vr = oracle.decompress(co, threads=4)
     out = kvf.decompress(c)
-    assert rel(out.keys(), kr) < 1e-6 and rel(out.values(), vr) < 1e-6
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
     ctx = L.context(0)
     L.check(L.lib().kvf_set_exact_reconstruct(ctx, 1))
     try:
@@ -368,12 +428,12 @@ def test_host_buffer_entry_points(kvf):
 def test_full_size_llama_layer(kvf, oracle):
     """One Llama-3-8B-shaped layer at full size ([8, 32768, 128] fp16,
     Aggressive): codes, bitstreams and ratio bit-exact against the oracle;
-    reconstruction within 1e-6 of the oracle's."""
+    reconstruction within REC_TOL of the oracle's."""
     from kvforge_b200 import synth
     k, v = synth.workload_layer("llama3_8b_32k", 0, backend="torch")
     kh, vh = host(k), host(v)
     c, co = _pipeline_case(kvf, oracle, kh, vh, "aggressive")
     out = kvf.decompress(c)
     kr, vr = oracle.decompress(co, threads=8)
-    assert rel(out.keys(), kr) < 1e-6 and rel(out.values(), vr) < 1e-6
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
     assert c.ratio() > 10
