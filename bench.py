@@ -59,8 +59,8 @@ def _traffic(kernel: str):
 def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
     """Isolated launches of the step's bandwidth-bound kernels on layer 0, timed
     with CUDA events on their own stream: value/key projection (+ per-token INT4
-    quantization for values) and value/key reconstruction. Algorithmic bytes per
-    launch: inputs read once plus outputs written once."""
+    quantization for values) and value/key reconstruction on both engines.
+    Algorithmic bytes per launch: inputs read once plus outputs written once."""
     _, k, v, kb, vb = lay
     if kb is None:
         return []
@@ -101,15 +101,22 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
                                                        C.c_void_p(b.device_ranks()), R, P(Pk), sp)))
             nbytes = x.numel() * 2 + 4 * H * T * R
             kern = "k_project (MODE 0: coefficients)"
-        res.append({"name": name, "kernel": kern, "bytes": nbytes, "ms": ms, "R": R})
-    for name, b in (("reconstruct_values", vb), ("reconstruct_keys", kb)):
-        R = b.R
-        Pc = torch.zeros((H, T, R), dtype=torch.float32, device=k.device)
-        out = torch.empty((H, T, D), dtype=torch.float32, device=k.device)
-        ms = timed(lambda: L.check(lib.kvf_reconstruct(ctx, P(Pc), H, T, R, D, C.c_void_p(b.device_vt()),
-                                                       C.c_void_p(b.device_ranks()), P(out), sp)))
-        res.append({"name": name, "kernel": "k_reconstruct_reg (f32 coefficients)", "bytes": 4 * H * T * R + 4 * H * T * D,
-                    "ms": ms, "R": R})
+        res.append({"name": name, "kernel": kern, "bytes": nbytes, "ms": ms, "R": R, "in_step": True})
+    # the CUDA-core engine runs in the step; the opt-in tcgen05 engine is timed beside it
+    for engine, suffix, kern in ((L.RECON_CUDA_CORE, "", "k_reconstruct_reg (f32 coefficients)"),
+                                 (L.RECON_TENSOR_CORE, "_tcgen05", "k_reconstruct_tc (tcgen05 split-tf32, opt-in)")):
+        L.check(lib.kvf_set_reconstruct_engine(ctx, engine))
+        try:
+            for name, b in (("reconstruct_values", vb), ("reconstruct_keys", kb)):
+                R = b.R
+                Pc = torch.zeros((H, T, R), dtype=torch.float32, device=k.device)
+                out = torch.empty((H, T, D), dtype=torch.float32, device=k.device)
+                ms = timed(lambda: L.check(lib.kvf_reconstruct(ctx, P(Pc), H, T, R, D, C.c_void_p(b.device_vt()),
+                                                               C.c_void_p(b.device_ranks()), P(out), sp)))
+                res.append({"name": name + suffix, "kernel": kern, "bytes": 4 * H * T * R + 4 * H * T * D,
+                            "ms": ms, "R": R, "in_step": engine == L.RECON_CUDA_CORE})
+        finally:
+            L.check(lib.kvf_set_reconstruct_engine(ctx, L.RECON_CUDA_CORE))
     return res
 
 
@@ -530,7 +537,8 @@ def gpu_arm(args):
     for r in kr:
         r["achieved_gbs"] = r["bytes"] / (r["ms"] / 1e3) / GB
         r["frac"] = r["achieved_gbs"] / peak
-    dom = max(kr, key=lambda r: r["ms"]) if kr else None
+    in_step = [r for r in kr if r["in_step"]]
+    dom = max(in_step, key=lambda r: r["ms"]) if in_step else None
     roof = None
     if dom is not None:
         traffic = _traffic(dom["name"])
@@ -549,8 +557,8 @@ def gpu_arm(args):
         "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak,
                           "frac": alg / (step_ms / 1e3) / GB / peak, "peak_kind": peak_kind},
         "roofline": roof,
-        "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac")}
-                             for r in kr],
+        "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac",
+                                                   "in_step")} for r in kr],
         "compress_only": {"ms_per_step": tot["compress_ms"],
                           "gbs": tot["input_bytes"] / (tot["compress_ms"] / 1e3) / GB},
         "decompress_only": {"ms_per_step": tot["decompress_ms"],

@@ -92,11 +92,17 @@ const char* kvf_last_error(void);
 int kvf_abi_version(void);
 /* 1: reconstruction uses separate multiply and add in the reference's order
  * (projection.rs:160-166), bit-identical to the CPU oracle.
- * 0 (default): head_dim 128 with at most 16 coefficients runs as a tcgen05
- * tensor-core GEMM (operands split into two tf32 parts, three products),
- * other shapes as one fused multiply-add per term in the same order; within
+ * 0 (default): the engine chosen by kvf_set_reconstruct_engine, within
  * relative Frobenius error 1e-5 of the reference loop. */
 kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
+/* engine of the non-exact reconstruction (kvf_reconstruct, decompression):
+ * CUDA_CORE (default): one fused multiply-add per term in the reference's
+ *   order, many small blocks per SM that share the GPU with concurrent work;
+ * TENSOR_CORE: for head_dim 128 and at most 16 coefficients, a tcgen05 GEMM
+ *   (operands split into two tf32 parts, three products, accumulators in
+ *   TMEM) with one block per SM; other shapes fall back to CUDA cores. */
+typedef enum { KVF_RECON_CUDA_CORE = 0, KVF_RECON_TENSOR_CORE = 1 } kvf_recon_engine;
+kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine);
 /* waits for `stream` and reports any error a device kernel recorded
  * (corrupt rANS container, bounded wait expiry) since the last check */
 kvf_status kvf_sync(kvf_ctx* ctx, void* stream);

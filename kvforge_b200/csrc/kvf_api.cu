@@ -130,6 +130,7 @@ struct TensorC {
 struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
+  int recon_engine = KVF_RECON_CUDA_CORE;
   unsigned* d_status = nullptr;
   // the context's own stream-ordered pool: freed blocks stay cached, and a
   // block freed on one stream is reused on another only once its free has
@@ -451,7 +452,7 @@ kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStr
     StageTimer tm(ctx, KVF_STAGE_RECONSTRUCT, out_bytes + (double)t.H * t.basis->R * t.D * 4, st);
     KVF_CUDA(launch_dequant_reconstruct(codes, nullptr, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T,
                                         t.qcols, t.D, t.basis->d_vt, t.basis->d_ranks, ctx->exact_reconstruct,
-                                        out, ctx->d_status, st));
+                                        ctx->recon_engine == KVF_RECON_TENSOR_CORE, out, ctx->d_status, st));
   } else {
     StageTimer tm(ctx, KVF_STAGE_DEQUANTIZE, out_bytes, st);
     KVF_CUDA(launch_dequantize(codes, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T, t.D, out, st));
@@ -807,6 +808,14 @@ kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact) {
   return KVF_OK;
 }
 
+kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine) {
+  KVF_TRY(check_ctx(ctx));
+  if (engine != KVF_RECON_CUDA_CORE && engine != KVF_RECON_TENSOR_CORE)
+    return fail(KVF_ERR_INVALID_CONFIG, "unknown reconstruction engine");
+  ctx->recon_engine = engine;
+  return KVF_OK;
+}
+
 kvf_status kvf_sync(kvf_ctx* ctx, void* stream) {
   KVF_TRY(check_ctx(ctx));
   DeviceGuard g(ctx->device);
@@ -976,7 +985,8 @@ kvf_status kvf_reconstruct(kvf_ctx* ctx, const float* projected, size_t H, size_
   if (R == 0 || R > D) return fail(KVF_ERR_PROJECTION, "projected width must be in 1..head_dim");
   DeviceGuard g(ctx->device);
   KVF_CUDA(launch_dequant_reconstruct(nullptr, projected, nullptr, nullptr, KVF_F32, KVF_PER_TOKEN, H, T, R, D,
-                                      basis_vt, ranks, ctx->exact_reconstruct, out, ctx->d_status, S(stream)));
+                                      basis_vt, ranks, ctx->exact_reconstruct,
+                                      ctx->recon_engine == KVF_RECON_TENSOR_CORE, out, ctx->d_status, S(stream)));
   return KVF_OK;
 }
 

@@ -196,12 +196,14 @@ cudaError_t launch_reconstruct_tc(const uint8_t* codes, const float* raw, const 
                                   int data_type, int axis, size_t H, size_t T, size_t R, size_t D,
                                   const float* basis_vt, const uint64_t* ranks, float* out, unsigned* status,
                                   cudaStream_t st);
-// packed codes (or raw f32 when data_type == KVF_F32) + params + basis -> f32 [H,T,D]
+// packed codes (or raw f32 when data_type == KVF_F32) + params + basis -> f32 [H,T,D];
+// exact: the reference's separately rounded order on CUDA cores; otherwise
+// tensor_cores selects the tcgen05 kernel where the shape allows it
 cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
                                        const float* mins, int data_type, int axis, size_t H,
                                        size_t T, size_t R, size_t D, const float* basis_vt,
-                                       const uint64_t* ranks, int exact, float* out, unsigned* status,
-                                       cudaStream_t st);
+                                       const uint64_t* ranks, int exact, int tensor_cores, float* out,
+                                       unsigned* status, cudaStream_t st);
 size_t gram_num_tiles(size_t T);
 cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                         float* partial, double* gram, cudaStream_t st);

@@ -1137,10 +1137,10 @@ cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t til
 cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
                                        const float* mins, int data_type, int axis, size_t H,
                                        size_t T, size_t R, size_t D, const float* basis_vt,
-                                       const uint64_t* ranks, int exact, float* out, unsigned* status,
-                                       cudaStream_t st) {
+                                       const uint64_t* ranks, int exact, int tensor_cores, float* out,
+                                       unsigned* status, cudaStream_t st) {
   if (H == 0 || T == 0 || D == 0) return cudaSuccess;
-  if (!exact) {  // tensor cores where the shape allows them
+  if (!exact && tensor_cores) {  // tensor cores where the shape allows them
     const cudaError_t e = launch_reconstruct_tc(codes, raw, scales, mins, data_type, axis, H, T, R, D, basis_vt,
                                                 ranks, out, status, st);
     if (e != cudaErrorNotSupported) return e;

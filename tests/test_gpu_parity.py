@@ -3,11 +3,11 @@ checked against the CPU oracle on the same seeded inputs.
 
 Bars: quantized codes, scales, mins, dequantized values, projected
 coefficients, rANS containers and compression ratios are bit-exact; the
-default reconstruction (tcgen05 split-tf32 GEMM for head_dim 128 and rank
-<= 16, fused multiply-add otherwise) is within relative Frobenius error
-REC_TOL = 1e-5 of the reference's loop, ten times inside the 1e-4 that the
-f32 projection/reconstruction contract allows, and bit-exact in the
-exact-reconstruction mode; calibration scores within 1e-6 relative."""
+default reconstruction (fused multiply-add on CUDA cores, or the tcgen05
+split-tf32 GEMM engine for head_dim 128 and rank <= 16) is within relative
+Frobenius error REC_TOL = 1e-5 of the reference's loop, ten times inside the
+1e-4 that the f32 projection/reconstruction contract allows, and bit-exact in
+the exact-reconstruction mode; calibration scores within 1e-6 relative."""
 import ctypes as C
 
 import numpy as np
@@ -186,9 +186,18 @@ def _exact(L, on):
     L.check(L.lib().kvf_set_exact_reconstruct(L.context(0), 1 if on else 0))
 
 
+@pytest.fixture
+def tensor_cores():
+    """Selects the tcgen05 reconstruction engine for one test."""
+    from kvforge_b200 import _lib as L
+    L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_TENSOR_CORE))
+    yield
+    L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_CUDA_CORE))
+
+
 @pytest.mark.parametrize("H,T,R,ranks", [(1, 1, 1, [1]), (2, 127, 3, [3, 2]), (3, 128, 8, [8, 8, 5]),
                                          (2, 129, 9, [9, 1]), (2, 1000, 16, [16, 12]), (5, 300, 13, [13, 0, 7, 13, 4])])
-def test_tensor_core_reconstruct_raw(kvf, oracle, H, T, R, ranks):
+def test_tensor_core_reconstruct_raw(kvf, oracle, tensor_cores, H, T, R, ranks):
     """head_dim 128, R <= 16: the tcgen05 path (partial tiles, ranks below R,
     rank 0) against the reference loop; the exact mode stays bit-exact."""
     from kvforge_b200 import _lib as L
@@ -202,6 +211,11 @@ def test_tensor_core_reconstruct_raw(kvf, oracle, H, T, R, ranks):
     pr = kvf.GpuProjector()
     out = host(pr.reconstruct(dev(Po), basis))
     assert rel(out, ref) < REC_TOL
+    if H * T >= 128 and max(ranks) > 1:  # a different engine ran: its roundings differ somewhere
+        L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_CUDA_CORE))
+        out_fma = host(pr.reconstruct(dev(Po), basis))
+        L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_TENSOR_CORE))
+        assert not np.array_equal(bits(out), bits(out_fma))
     _exact(L, True)
     try:
         out_exact = host(pr.reconstruct(dev(Po), basis))
@@ -212,7 +226,7 @@ def test_tensor_core_reconstruct_raw(kvf, oracle, H, T, R, ranks):
 
 @pytest.mark.parametrize("dt", [INT8, INT4])
 @pytest.mark.parametrize("shape,thr", [((2, 300, 128), 0.9), ((3, 77, 128), 0.75)])
-def test_tensor_core_reconstruct_codes(kvf, oracle, dt, shape, thr):
+def test_tensor_core_reconstruct_codes(kvf, oracle, tensor_cores, dt, shape, thr):
     """Projected INT8 and INT4 codes, keys per channel and values per token,
     decompressed on the tcgen05 path against the reference pipeline."""
     from kvforge_b200 import _lib as L
@@ -437,3 +451,10 @@ def test_full_size_llama_layer(kvf, oracle):
     kr, vr = oracle.decompress(co, threads=8)
     assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
     assert c.ratio() > 10
+    from kvforge_b200 import _lib as L
+    L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_TENSOR_CORE))
+    try:
+        out = kvf.decompress(c)
+    finally:
+        L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_CUDA_CORE))
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
