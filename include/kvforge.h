@@ -103,6 +103,14 @@ kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
  *   TMEM) with one block per SM; other shapes fall back to CUDA cores. */
 typedef enum { KVF_RECON_CUDA_CORE = 0, KVF_RECON_TENSOR_CORE = 1 } kvf_recon_engine;
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine);
+/* Runs one of the library's bounded device waits against a barrier or status
+ * word that nothing completes, with a 2 ms limit: the wait gives up and the
+ * next kvf_sync on `stream` reports KVF_ERR_DEVICE_TIMEOUT, after which the
+ * context is usable as before. MBARRIER: the wait of the tensor-map copy and
+ * tensor-core pipelines; LOOKBACK: the rANS encoder's wait for the offsets of
+ * earlier chunks. */
+typedef enum { KVF_WAIT_MBARRIER = 0, KVF_WAIT_LOOKBACK = 1 } kvf_wait_kind;
+kvf_status kvf_selftest_wait_timeout(kvf_ctx* ctx, int which, void* stream);
 /* waits for `stream` and reports any error a device kernel recorded
  * (corrupt rANS container, bounded wait expiry) since the last check */
 kvf_status kvf_sync(kvf_ctx* ctx, void* stream);

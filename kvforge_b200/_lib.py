@@ -36,11 +36,12 @@ PER_CHANNEL, PER_TOKEN = 0, 1
 IN_F32, IN_F16 = 0, 1
 CONSERVATIVE, BALANCED, AGGRESSIVE, ADAPTIVE = 0, 1, 2, 3
 RECON_CUDA_CORE, RECON_TENSOR_CORE = 0, 1
+WAIT_MBARRIER, WAIT_LOOKBACK = 0, 1
 
 # every symbol include/kvforge.h declares
 EXPORTS = [
     "kvf_init", "kvf_destroy", "kvf_last_error", "kvf_abi_version", "kvf_set_exact_reconstruct",
-    "kvf_set_reconstruct_engine", "kvf_sync",
+    "kvf_set_reconstruct_engine", "kvf_selftest_wait_timeout", "kvf_sync",
     "kvf_pipeline_config_from_preset", "kvf_calibrate", "kvf_quantize", "kvf_dequantize", "kvf_project",
     "kvf_reconstruct", "kvf_fused_project_quantize", "kvf_rans_max_encoded_len", "kvf_rans_encode",
     "kvf_rans_decode", "kvf_entropy_decode_dequant", "kvf_basis_compute", "kvf_basis_from_host",
@@ -93,6 +94,7 @@ def _declare(L):
         "kvf_abi_version": (C.c_int, []),
         "kvf_set_exact_reconstruct": (st, [p, C.c_int]),
         "kvf_set_reconstruct_engine": (st, [p, C.c_int]),
+        "kvf_selftest_wait_timeout": (st, [p, C.c_int, p]),
         "kvf_sync": (st, [p, p]),
         "kvf_pipeline_config_from_preset": (st, [i32, C.POINTER(PipelineConfig)]),
         "kvf_calibrate": (st, [p, p, i32, sz, sz, sz, sz, p, p]),

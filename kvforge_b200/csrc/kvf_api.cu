@@ -808,6 +808,24 @@ kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact) {
   return KVF_OK;
 }
 
+kvf_status kvf_selftest_wait_timeout(kvf_ctx* ctx, int which, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (which != KVF_WAIT_MBARRIER && which != KVF_WAIT_LOOKBACK)
+    return fail(KVF_ERR_INVALID_CONFIG, "unknown wait kind");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  constexpr unsigned long long kLimitNs = 2000000ull;  // 2 ms
+  if (which == KVF_WAIT_MBARRIER) {
+    KVF_CUDA(launch_selftest_mbar(ctx->d_status, kLimitNs, st));
+  } else {
+    Scratch sc(st, ctx->pool);
+    unsigned long long* lb = sc.get<unsigned long long>(2);
+    if (!lb) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+    KVF_CUDA(launch_selftest_lookback(lb, ctx->d_status, kLimitNs, st));
+  }
+  return KVF_OK;
+}
+
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine) {
   KVF_TRY(check_ctx(ctx));
   if (engine != KVF_RECON_CUDA_CORE && engine != KVF_RECON_TENSOR_CORE)

@@ -118,6 +118,41 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// ---- bounded waits shared by every kernel that waits ----------------------
+// device clock in nanoseconds
+__device__ __forceinline__ unsigned long long dev_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// a wait gives up after this many polls or this much time, whichever is first
+constexpr uint32_t kWaitPolls = 1u << 22;
+constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
+
+// waits until the phase of `parity` of the mbarrier at shared address `bar`
+// has completed. false when the wait gave up: the poll or time limit ran
+// out, or `abort_flag` (optional, shared memory) was raised by another warp.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned long long limit_ns,
+                                                  const volatile int* abort_flag = nullptr) {
+  unsigned long long t0 = 0;
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 255u) == 0u) {  // the clock and the flag are read every 256 polls
+      const unsigned long long t = dev_ns();
+      if (i == 0) t0 = t;
+      else if (t - t0 > limit_ns) return false;
+      if (abort_flag && *abort_flag) return false;
+    }
+  }
+  return false;
+}
+
 __device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
   return __fadd_rn(__fmul_rn((float)q, scale), mn);
 }
@@ -218,5 +253,13 @@ cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, co
 cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint64_t* comp_len_dev,
                                const uint32_t* freq, size_t n, uint8_t* out, unsigned* status,
                                cudaStream_t st);
+
+// self-tests of the bounded waits (kvf_selftest_wait_timeout): each runs the
+// wait the kernels use against a barrier or status word that nothing
+// completes, so it gives up after limit_ns and sets kDevErrTimeout
+cudaError_t launch_selftest_mbar(unsigned* status, unsigned long long limit_ns, cudaStream_t st);
+// lb: two zeroed look-back words
+cudaError_t launch_selftest_lookback(unsigned long long* lb, unsigned* status, unsigned long long limit_ns,
+                                     cudaStream_t st);
 
 }  // namespace kvf

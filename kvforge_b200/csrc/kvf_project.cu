@@ -93,7 +93,6 @@ constexpr int kColBytes = 64;                        // bytes of each row per st
 constexpr int kProjWarps = kProjThreads / 32;
 constexpr int kWarpRows = kProjRows / kProjWarps;    // token rows of a tile streamed by one warp
 constexpr int kWarpStage = kWarpRows * kColBytes;    // bytes of one warp's stage
-constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before a wait gives up
 
 template <typename TIn>
 struct Seg;
@@ -130,19 +129,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 // true once the barrier's phase with the given parity has completed; false
-// when the bounded number of polls ran out
+// when the wait gave up (kWaitPolls polls or kWaitNs)
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_addr(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
+  return mbar_wait_bounded(smem_addr(bar), parity, kWaitNs);
 }
 // 2-D tile copy global -> shared through a tensor map (x: element column, y: row)
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -1176,6 +1165,26 @@ cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t 
   const dim3 rg((unsigned)std::min<size_t>((DD + 255) / 256, 1024), (unsigned)H);
   k_gram_reduce<<<rg, 256, 0, st>>>(partial, (int)tiles, (int)D, gram);
   note_launches(2);
+  return cudaGetLastError();
+}
+
+namespace {
+// one warp waits on an mbarrier that nothing arrives on
+__global__ void k_selftest_mbar(unsigned* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const bool ok = mbar_wait_bounded(smem_addr(&bar), 0, limit_ns);
+  if (__any_sync(0xffffffffu, !ok) && threadIdx.x == 0 && status) atomicOr(status, kDevErrTimeout);
+}
+}  // namespace
+
+cudaError_t launch_selftest_mbar(unsigned* status, unsigned long long limit_ns, cudaStream_t st) {
+  k_selftest_mbar<<<1, 32, 0, st>>>(status, limit_ns);
+  note_launches(1);
   return cudaGetLastError();
 }
 

@@ -218,11 +218,13 @@ __device__ __forceinline__ void st_release(unsigned long long* p, unsigned long 
 }
 
 // bytes of the payloads before chunk c (c > 0); false when the wait gave up
+// (kLbSpinLimit polls of one window, or limit_ns in all)
 __device__ bool look_back(unsigned long long* lb, uint64_t c, unsigned* status, int lane,
-                          unsigned long long& prefix) {
+                          unsigned long long& prefix, unsigned long long limit_ns = kWaitNs) {
   prefix = 0ull;
   int64_t top = (int64_t)c - 1;
   uint32_t spins = 0;
+  const unsigned long long t0 = dev_ns();
   while (true) {
     const int64_t idx = top - lane;
     const unsigned long long v = idx >= 0 ? ld_acquire(lb + idx) : kLbPrefix;  // before chunk 0: prefix 0
@@ -232,7 +234,11 @@ __device__ bool look_back(unsigned long long* lb, uint64_t c, unsigned* status, 
     const int pl = pre ? __ffs(pre) - 1 : 31;  // the window ends at the nearest prefix
     const unsigned used = pl == 31 ? 0xffffffffu : ((2u << pl) - 1u);
     if (empty & used) {  // a predecessor has not published yet
-      if (++spins > kLbSpinLimit || (*reinterpret_cast<volatile unsigned*>(status) & kDevErrTimeout)) return false;
+      // every lane takes the same branch: the clock and the status word are
+      // read per lane, so the decision is a vote
+      const bool give_up = ++spins > kLbSpinLimit || dev_ns() - t0 > limit_ns ||
+                           (*reinterpret_cast<volatile unsigned*>(status) & kDevErrTimeout);
+      if (__any_sync(0xffffffffu, give_up)) return false;
       __nanosleep(64);
       continue;
     }
@@ -583,4 +589,22 @@ cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint6
   note_launches(1);
   return cudaGetLastError();
 }
+namespace {
+// chunk 1 looks back at chunk 0, whose status word nothing publishes
+__global__ void k_selftest_lookback(unsigned long long* lb, unsigned* status, unsigned long long limit_ns) {
+  unsigned long long prefix;
+  const bool ok = look_back(lb, 1, status, threadIdx.x & 31, prefix, limit_ns);
+  if (!ok && threadIdx.x == 0 && status) atomicOr(status, kDevErrTimeout);
+}
+}  // namespace
+
+cudaError_t launch_selftest_lookback(unsigned long long* lb, unsigned* status, unsigned long long limit_ns,
+                                     cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(lb, 0, 2 * sizeof(unsigned long long), st);
+  if (e != cudaSuccess) return e;
+  k_selftest_lookback<<<1, 32, 0, st>>>(lb, status, limit_ns);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
 }  // namespace kvf

@@ -46,7 +46,6 @@ constexpr int kProdWarps = 4;
 constexpr int kTcThreads = 32 * (kEpiWarps + kProdWarps);
 constexpr int kProdThreads = 32 * kProdWarps;
 constexpr int kRowsPerProd = kTcRows / kProdThreads;  // 1
-constexpr uint32_t kTcWaitLimit = 1u << 22;
 constexpr int kSlotBytes = 32 * 128;  // one staging slot: 32 tokens x 32 channels
 constexpr int kSlots = 6;             // staging slots per epilogue warp (even: filled in pairs)
 constexpr int kTmemCols = 2 * kTcD;   // two accumulators
@@ -89,18 +88,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // waits for the phase of `parity` to complete; false when the wait ran out or
 // the other role raised the abort flag
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const uint32_t a = sa(bar);
-  for (uint32_t i = 0; i < kTcWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
-  }
-  return false;
+  return mbar_wait_bounded(sa(bar), parity, kWaitNs, abort_flag);
 }
 
 // x as the sum of two tf32 values: hi = x rounded to 11 significant bits, and

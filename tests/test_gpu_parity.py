@@ -339,6 +339,26 @@ def test_rans_corrupt_is_reported(kvf, oracle):
     assert np.array_equal(host(codec.decode(comp, st)), data)
 
 
+@pytest.mark.parametrize("which", ["mbarrier", "lookback"])
+def test_bounded_wait_timeout_is_reported(kvf, oracle, which):
+    """A device wait on a barrier (or a look-back status word) that nothing
+    completes gives up after its limit; the host reads KVF_ERR_DEVICE_TIMEOUT
+    from the status word, and the same context then compresses bit-exactly."""
+    from kvforge_b200 import _lib as L
+    ctx = L.context(0)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    kind = L.WAIT_MBARRIER if which == "mbarrier" else L.WAIT_LOOKBACK
+    L.check(L.lib().kvf_selftest_wait_timeout(ctx, kind, s))
+    assert L.lib().kvf_sync(ctx, s) == L.ERR_DEVICE_TIMEOUT
+    assert L.lib().kvf_sync(ctx, s) == 0  # reported once, then cleared
+    rng = np.random.default_rng(4)
+    data = rng.integers(0, 60, 70000).astype(np.uint8)
+    codec = kvf.GpuEntropyCodec()
+    comp, st = codec.encode(dev(data))
+    assert np.array_equal(host(comp), oracle.rans_encode(data)[0])
+    assert np.array_equal(host(codec.decode(comp, st)), data)
+
+
 # ---- whole pipeline -----------------------------------------------------------------
 def _pipeline_case(kvf, oracle, k, v, preset):
     import kvforge_b200.synth  # noqa: F401
