@@ -16,7 +16,7 @@ constexpr uint32_t kRansProbBits = 13;
 constexpr uint32_t kRansM = 1u << kRansProbBits;
 constexpr uint32_t kRansL = 1u << 16;
 constexpr uint32_t kRansLanes = 32;
-constexpr uint32_t kRansChunk = 16384;                  // symbols per chunk (encoder default)
+constexpr uint32_t kRansChunk = 8192;                   // symbols per chunk (encoder default)
 constexpr uint32_t kRansMaxChunk = kRansLanes * 65535u;  // lane word counts are u16
 constexpr uint32_t kRansMagic = 0x3252564Bu;             // "KVR2"
 constexpr size_t kRansHeader = 32;

@@ -13,8 +13,11 @@
 //
 // Calibration (crates/kvforge-cpu/src/calibration.rs:25-73): fp64 sum and sum
 // of squares per head; partials per block are combined in a fixed order, so
-// the result is deterministic (it differs from the sequential reference only
-// in fp64 rounding order).
+// the result is deterministic. Inside the key projection each thread first
+// sums 64 elements in f32 (the squares of f16 inputs are exact) and adds that
+// to its fp64 sums; the scores (a ratio of variances) stay within 1e-6 of the
+// sequential fp64 reference, the parity bar for a result the reference
+// pipeline discards (pipeline.rs:106-111).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -300,6 +303,10 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
             sb[rr] = wbuf + (size_t)(u % L.stages) * kWarpStage + wrow[rr] * kColBytes;
             sw[rr] = (int)(smem_addr(sb[rr]) >> 7) & 3;  // the swizzle XORs address bits 4-5 with bits 7-8
           }
+          // calibration sums of this unit's 2 x 32 elements in f32 (squares of
+          // f16 inputs are exact in f32), folded into the f64 sums once per
+          // unit: one conversion per 64 elements instead of one per element
+          float p1 = 0.0f, p2 = 0.0f;
 #pragma unroll
           for (int jj = 0; jj < kColBytes / 16; ++jj) {
             float xv[kProjNR][PV];
@@ -311,9 +318,9 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
               for (int rr = 0; rr < kProjNR; ++rr)
 #pragma unroll
                 for (int k = 0; k < PV; ++k) {
-                  const double v = ok[rr] ? (double)xv[rr][k] : 0.0;
-                  s1 += v;
-                  s2 += v * v;
+                  const float v = ok[rr] ? xv[rr][k] : 0.0f;
+                  p1 = __fadd_rn(p1, v);
+                  p2 = __fmaf_rn(v, v, p2);
                 }
             }
             const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * RG;
@@ -324,6 +331,10 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
               for (int rr = 0; rr < kProjNR; ++rr) xk[rr] = xv[rr][k];
               fma_rows<RG>(acc2, xk, vb + k * RG);
             }
+          }
+          if (CALIB) {
+            s1 += (double)p1;
+            s2 += (double)p2;
           }
         } else {
           for (int c = 0; c < D; ++c) {

@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(const uint8_t* _
                                                                uint64_t nchunks,
                                                                unsigned* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t sbuf[];
-  __shared__ uint32_t q[256], cum[256], qc[256], rcp[256];
+  __shared__ uint32_t q[256], cum[256];
+  __shared__ uint4 mdl[256];  // per symbol: {threshold - 1, reciprocal, q, (M - q) | cum << 16}
   __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t c = (uint64_t)blockIdx.x * kEncWarps + w;
@@ -284,8 +285,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(const uint8_t* _
   // the model is built while the symbols are in flight
   const bool model_ok = build_model(freq, q, cum, ms);
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    qc[i] = q[i] | (cum[i] << 16);
-    rcp[i] = q[i] ? 0xFFFFFFFFu / q[i] : 0u;
+    // a state renormalises first when x >= q << kShift, i.e. x > thr; q = 2^13
+    // (one symbol takes the whole model) never renormalises
+    const uint64_t t = ((uint64_t)q[i] << kShift) - 1ull;
+    const uint32_t thr = q[i] ? (uint32_t)(t > 0xFFFFFFFFull ? 0xFFFFFFFFull : t) : 0u;
+    mdl[i] = make_uint4(thr, q[i] ? 0xFFFFFFFFu / q[i] : 0u, q[i], (kRansM - q[i]) | (cum[i] << 16));
   }
   cp_async_wait_all();
   __syncthreads();
@@ -296,41 +300,46 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(const uint8_t* _
   if (!live) return;
 
   uint32_t x = kRansL, pos = RS;
-  // renormalise (at most one word), then x -> (x / f) * M + x % f + cum; the
-  // quotient comes from the reciprocal floor((2^32 - 1) / f), low by at most one
-  auto step = [&](uint32_t e, uint32_t rc) {
-    const uint32_t f = e & 0xFFFFu;
-    const bool need = (x >> kShift) >= f;
+  // renormalise (at most one word), then x -> (x / f) * M + x % f + cum,
+  // written as floor(xs / f) * (M - f) + xs + cum. The quotient estimate
+  // umulhi(xs, floor((2^32 - 1) / f)) is low by at most one; both candidate
+  // states are formed and the remainder test picks one, so the state's
+  // dependency chain is compare, select, multiply-high, multiply-add, compare,
+  // select.
+  auto step = [&](const uint4& m) {
+    const uint32_t f = m.z, mf = m.w & 0xFFFFu, cm = m.w >> 16;
+    const bool need = x > m.x;
     if (need) region[pos - 1] = (uint16_t)(x & 0xFFFFu);
     pos -= need ? 1u : 0u;
     const uint32_t xs = need ? (x >> 16) : x;
-    uint32_t qq = __umulhi(xs, rc);
-    uint32_t r = xs - qq * f;
-    const bool fix = r >= f;
-    qq += fix ? 1u : 0u;
-    r -= fix ? f : 0u;
-    x = (qq << kRansProbBits) + r + (e >> 16);
+    const uint32_t qq = __umulhi(xs, m.y);
+    const uint32_t xa = qq * mf + xs + cm;
+    x = (xs - qq * f >= f) ? xa + mf : xa;
   };
   const uint32_t steps = (nsym + 31) / 32;
   {  // last (possibly partial) step
     const uint32_t i = (steps - 1) * 32 + lane;
-    if (i < nsym) {
-      const uint32_t s = buf[i];
-      step(qc[s], rcp[s]);
-    }
+    if (i < nsym) step(mdl[buf[i]]);
   }
-  if (steps >= 2) {  // full steps; the next step's model entries load one step ahead
-    uint32_t s = buf[(steps - 2) * 32 + lane];
-    uint32_t e = qc[s], rc = rcp[s];
-#pragma unroll 4
-    for (uint32_t st = steps - 1; st-- > 0;) {
-      const uint32_t e0 = e, r0 = rc;
-      s = buf[(st > 0 ? st - 1 : 0) * 32 + lane];
-      e = qc[s];
-      rc = rcp[s];
-      step(e0, r0);
-    }
+  // full steps, from steps - 2 down to 0, four at a time: each of the four
+  // model entries in registers is used, then reloaded for the step four
+  // further on, so every lookup is issued four steps before the chain needs it
+  auto entry = [&](int t) { return mdl[buf[(t > 0 ? t : 0) * 32 + lane]]; };
+  int t = (int)steps - 2;
+  uint4 m0 = entry(t), m1 = entry(t - 1), m2 = entry(t - 2), m3 = entry(t - 3);
+  for (; t >= 3; t -= 4) {
+    step(m0);
+    m0 = entry(t - 4);
+    step(m1);
+    m1 = entry(t - 5);
+    step(m2);
+    m2 = entry(t - 6);
+    step(m3);
+    m3 = entry(t - 7);
   }
+  if (t >= 0) step(m0);
+  if (t >= 1) step(m1);
+  if (t >= 2) step(m2);
 
   // payload layout: lane streams one after another, in decoding order; the
   // warp copies one lane's stream at a time with coalesced 2-byte stores
@@ -399,7 +408,7 @@ __device__ __forceinline__ uint32_t rd32(const uint8_t* p) {
 // be needed, at an index clamped to the lane's stream, so a corrupt count
 // reads nothing outside the payload. Returns true when the chunk is malformed.
 template <bool FULL_ONLY>
-__device__ __forceinline__ bool decode_chunk(const uint8_t* pay, uint32_t pay_bytes, const uint32_t* ent,
+__device__ __forceinline__ bool decode_chunk(const uint8_t* pay, uint32_t pay_bytes, const uint2* ent,
                                              const uint8_t* sym, uint32_t nsym, uint8_t* __restrict__ o,
                                              int lane) {
   uint32_t x = reinterpret_cast<const uint32_t*>(pay)[lane];
@@ -418,21 +427,23 @@ __device__ __forceinline__ bool decode_chunk(const uint8_t* pay, uint32_t pay_by
   const uint32_t full = nsym / 32;
 #pragma unroll 4
   for (uint32_t st = 0; st < full; ++st) {
+    // chain: mask, one 8-byte lookup, multiply-add, then compare and a byte
+    // permute ((x << 16) | word) side by side, select
     const uint32_t slot = x & (kRansM - 1);
-    const uint32_t e = ent[slot];
+    const uint2 e = ent[slot];
     o[32 * st] = sym[slot];
-    x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+    x = e.x * (x >> kRansProbBits) + e.y;
     const bool need = x < kRansL;
-    x = need ? ((x << 16) | wn) : x;
+    x = need ? __byte_perm(wn, x, 0x5410) : x;
     k += need ? 1u : 0u;
     wn = wl[min(k, last)];
   }
   if (!FULL_ONLY && full * 32 < nsym) {  // last, partial step
     if (full * 32 + lane < nsym) {
       const uint32_t slot = x & (kRansM - 1);
-      const uint32_t e = ent[slot];
+      const uint2 e = ent[slot];
       o[32 * full] = sym[slot];
-      x = (e & 0xFFFFu) * (x >> kRansProbBits) + (e >> 16);
+      x = e.x * (x >> kRansProbBits) + e.y;
       if (x < kRansL) {
         x = (x << 16) | wn;
         ++k;
@@ -443,12 +454,13 @@ __device__ __forceinline__ bool decode_chunk(const uint8_t* pay, uint32_t pay_by
   return __any_sync(0xffffffffu, bad);
 }
 
-// Decoder shared memory: the slot tables ent[slot] = q | (slot - cum) << 16 and
+// Decoder shared memory: the slot tables ent[slot] = {q, slot - cum} and
 // sym[slot], then one staging buffer per warp holding a chunk payload of the
 // default chunk size (with 16 bytes of alignment slack); payloads of larger
 // chunks are read from global memory in place.
 constexpr uint32_t kDecStageBytes = (uint32_t)kRansPayloadHeader + 2u * kRansChunk + 32u;
-constexpr size_t kDecSmem = 5 * (size_t)kRansM + (size_t)kDecWarps * kDecStageBytes;
+constexpr size_t kDecTableBytes = 9 * (size_t)kRansM;  // ent (8 B) + sym (1 B) per slot
+constexpr size_t kDecSmem = kDecTableBytes + (size_t)kDecWarps * kDecStageBytes;
 
 __global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8_t* __restrict__ comp,
                                                               uint64_t comp_len_host,
@@ -457,8 +469,8 @@ __global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8
                                                               uint64_t n, uint8_t* __restrict__ out,
                                                               unsigned* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t dsm[];
-  uint32_t* ent = reinterpret_cast<uint32_t*>(dsm);  // [2^13]
-  uint8_t* sym = dsm + 4 * kRansM;                   // [2^13]
+  uint2* ent = reinterpret_cast<uint2*>(dsm);  // [2^13]
+  uint8_t* sym = dsm + 8 * kRansM;             // [2^13]
   __shared__ uint32_t q[256], cum[256];
   __shared__ ModelSmem ms;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -468,8 +480,9 @@ __global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8
   }
   {  // slot tables: mark the first slot of every coded symbol in sym[], then
      // each warp turns a contiguous span of marks into both tables, a lane
-     // taking four consecutive slots per round (16-byte rows, no bank
-     // conflicts); the symbol of a slot is the last mark at or before it
+     // taking four consecutive slots per round (one 4-byte mark word in,
+     // two 16-byte ent stores and one 4-byte sym store out); the symbol of a
+     // slot is the last mark at or before it
     for (uint32_t i = threadIdx.x; i < kRansM / 16; i += blockDim.x)
       reinterpret_cast<uint4*>(sym)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
@@ -499,17 +512,19 @@ __global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8
       for (int b = 0; b < 4; ++b) {
         const uint32_t mb = (m4 >> (8 * b)) & 0xFFu;
         v = mb ? mb : v;
-        e[b] = q[v] | ((k + b - cum[v]) << 16);
+        e[b] = v;
         sw |= v << (8 * b);
       }
       carry = __shfl_sync(0xffffffffu, v, 31);
-      *reinterpret_cast<uint4*>(ent + k) = make_uint4(e[0], e[1], e[2], e[3]);
+      uint4* ep = reinterpret_cast<uint4*>(ent + k);
+      ep[0] = make_uint4(q[e[0]], k - cum[e[0]], q[e[1]], k + 1 - cum[e[1]]);
+      ep[1] = make_uint4(q[e[2]], k + 2 - cum[e[2]], q[e[3]], k + 3 - cum[e[3]]);
       *reinterpret_cast<uint32_t*>(sym + k) = sw;
     }
   }
   __syncthreads();
   if (w >= kDecWarps) return;
-  uint8_t* stage = dsm + 5 * kRansM + (size_t)w * kDecStageBytes;
+  uint8_t* stage = dsm + kDecTableBytes + (size_t)w * kDecStageBytes;
   const uint64_t comp_len = comp_len_dev ? *comp_len_dev : comp_len_host;
   // header checks (every warp reads the same 32 bytes)
   if (comp_len < kRansHeader) { if (threadIdx.x == 0) atomicOr(status, kDevErrCorrupt); return; }

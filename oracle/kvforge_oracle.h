@@ -51,7 +51,7 @@ enum { ORC_PER_CHANNEL = 0, ORC_PER_TOKEN = 1 };            /* QuantAxis, types.
 /* rANS container constants (this project's format, mirrored on the GPU) */
 #define ORC_RANS_PROB_BITS 13u
 #define ORC_RANS_LANES 32u
-#define ORC_RANS_DEFAULT_CHUNK 16384u
+#define ORC_RANS_DEFAULT_CHUNK 8192u
 #define ORC_RANS_MAX_CHUNK (ORC_RANS_LANES * 65535u) /* lane word counts are u16 */
 #define ORC_RANS_MAGIC 0x3252564Bu /* "KVR2" */
 

@@ -17,7 +17,7 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 INT4, INT8, F32 = 0, 1, 2
 PER_CHANNEL, PER_TOKEN = 0, 1
-DEFAULT_CHUNK = 16384
+DEFAULT_CHUNK = 8192
 
 _lib = None
 

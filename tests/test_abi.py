@@ -74,5 +74,5 @@ def test_init_without_device_is_an_error_not_a_crash():
 def test_rans_capacity_formula():
     from kvforge_b200 import _lib as L
     from oracle import oracle as O
-    for n in (0, 1, 100, 16384, 16385, 10 ** 6):
-        assert L.lib().kvf_rans_max_encoded_len(n) == O.lib().orc_rans_max_encoded_len(n, 16384)
+    for n in (0, 1, 100, 8192, 8193, 16384, 16385, 10 ** 6):
+        assert L.lib().kvf_rans_max_encoded_len(n) == O.lib().orc_rans_max_encoded_len(n, O.DEFAULT_CHUNK)

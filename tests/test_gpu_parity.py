@@ -280,7 +280,7 @@ def test_basis_ranks(kvf, oracle, shape, thr, f16):
 
 
 # ---- rANS --------------------------------------------------------------------------
-@pytest.mark.parametrize("n", [1, 31, 32, 33, 1000, 16383, 16384, 16385, 200000, 1 << 22])
+@pytest.mark.parametrize("n", [1, 31, 32, 33, 1000, 8191, 8192, 8193, 16385, 200000, 1 << 22])
 def test_rans_parity(kvf, oracle, n):
     rng = np.random.default_rng(n)
     data = np.clip(np.round(rng.normal(120, 15, n)), 0, 255).astype(np.uint8)

@@ -216,7 +216,7 @@ def _round_f32(fr):
 
 
 # ---- rANS container ---------------------------------------------------------------
-@pytest.mark.parametrize("n", [1, 31, 32, 33, 1000, 16383, 16384, 16385, 40000])
+@pytest.mark.parametrize("n", [1, 31, 32, 33, 1000, 8191, 8192, 8193, 16384, 16385, 40000])
 def test_rans_roundtrip_sizes(oracle, n):
     rng = np.random.default_rng(n)
     data = np.clip(np.round(rng.normal(100, 20, n)), 0, 255).astype(np.uint8)
