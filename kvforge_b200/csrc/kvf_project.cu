@@ -635,9 +635,20 @@ __global__ void __launch_bounds__(256) k_calib_finalize(const double* __restrict
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int h = w; h < H; h += nw) {
     double s1 = 0.0, s2 = 0.0;
-    for (int k = lane; k < tiles; k += 32) {
-      s1 += cpart[2 * ((size_t)h * tiles + k)];
-      s2 += cpart[2 * ((size_t)h * tiles + k) + 1];
+    for (int k0 = lane; k0 < tiles; k0 += 32 * 8) {  // eight loads in flight, then the adds in order
+      double a[8], b[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int k = k0 + 32 * j;
+        const bool in = k < tiles;
+        a[j] = in ? cpart[2 * ((size_t)h * tiles + k)] : 0.0;
+        b[j] = in ? cpart[2 * ((size_t)h * tiles + k) + 1] : 0.0;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s1 += a[j];
+        s2 += b[j];
+      }
     }
     s1 = warp_sum(s1);
     s2 = warp_sum(s2);
