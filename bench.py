@@ -56,14 +56,12 @@ def _traffic(kernel: str):
         return None
 
 
-def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
+def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
     """Isolated launches of the step's bandwidth-bound kernels on layer 0, timed
     with CUDA events on their own stream: value/key projection (+ per-token INT4
     quantization for values) and value/key reconstruction on both engines.
     Algorithmic bytes per launch: inputs read once plus outputs written once."""
     _, k, v, kb, vb = lay
-    if kb is None:
-        return []
     H, T, D = k.shape
     st = torch.cuda.Stream(device=dev)
     sp = C.c_void_p(st.cuda_stream)
@@ -82,6 +80,27 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
             e1.record(st)
         e1.synchronize()
         return e0.elapsed_time(e1) / reps
+
+    if kb is None:  # no projection (Conservative): KIVI quantize and dequantize of the raw tensors
+        in_code = L.IN_F16 if k.dtype == torch.float16 else L.IN_F32
+        dt = cfg.key_data_type
+        n = H * T * D
+        plen = (n + 1) // 2 if dt == L.INT4 else n
+        packed = torch.empty(plen, dtype=torch.uint8, device=k.device)
+        out = torch.empty((H, T, D), dtype=torch.float32, device=k.device)
+        for name, x, axis in (("quantize_keys_per_channel", k, L.PER_CHANNEL), ("quantize_values_per_token", v, L.PER_TOKEN)):
+            npar = H * D if axis == L.PER_CHANNEL else H * T
+            sc = torch.empty(npar, device=k.device)
+            mn = torch.empty(npar, device=k.device)
+            ms = timed(lambda: L.check(lib.kvf_quantize(ctx, P(x), in_code, H, T, D, dt, axis, P(packed), P(sc), P(mn),
+                                                        sp)))
+            res.append({"name": name, "kernel": "kvf_quantize (KIVI codes + params)", "R": None,
+                        "bytes": x.numel() * x.element_size() + plen + 8 * npar, "ms": ms, "in_step": True})
+            ms = timed(lambda: L.check(lib.kvf_dequantize(ctx, P(packed), plen, P(sc), P(mn), dt, axis, H, T, D,
+                                                          P(out), sp)))
+            res.append({"name": name.replace("quantize", "dequantize"), "kernel": "kvf_dequantize (f32 out)",
+                        "R": None, "bytes": plen + 8 * npar + 4 * n, "ms": ms, "in_step": True})
+        return res
 
     for name, x, b, per_token in (("project_values_int4_per_token", v, vb, True), ("project_keys", k, kb, False)):
         R = b.R
@@ -102,21 +121,25 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, reps=20):
             nbytes = x.numel() * 2 + 4 * H * T * R
             kern = "k_project (MODE 0: coefficients)"
         res.append({"name": name, "kernel": kern, "bytes": nbytes, "ms": ms, "R": R, "in_step": True})
-    # the CUDA-core engine runs in the step; the opt-in tcgen05 engine is timed beside it
-    for engine, suffix, kern in ((L.RECON_CUDA_CORE, "", "k_reconstruct_reg (f32 coefficients)"),
-                                 (L.RECON_TENSOR_CORE, "_tcgen05", "k_reconstruct_tc (tcgen05 split-tf32, opt-in)")):
+    # both reconstruction engines; the step uses the default choice (CUDA cores
+    # up to 16 coefficients, tensor cores above), the other is timed beside it
+    for engine, eng_name in ((L.RECON_CUDA_CORE, "cuda_core"), (L.RECON_TENSOR_CORE, "tcgen05")):
         L.check(lib.kvf_set_reconstruct_engine(ctx, engine))
         try:
             for name, b in (("reconstruct_values", vb), ("reconstruct_keys", kb)):
                 R = b.R
+                in_step = (engine == L.RECON_TENSOR_CORE) == (R > 16)
+                kern = ("k_reconstruct_tc (tcgen05 split-tf32)" if engine == L.RECON_TENSOR_CORE else
+                        "k_reconstruct_reg (basis in registers)" if R <= 16 else
+                        "k_dequant_reconstruct (basis in shared memory)")
                 Pc = torch.zeros((H, T, R), dtype=torch.float32, device=k.device)
                 out = torch.empty((H, T, D), dtype=torch.float32, device=k.device)
                 ms = timed(lambda: L.check(lib.kvf_reconstruct(ctx, P(Pc), H, T, R, D, C.c_void_p(b.device_vt()),
                                                                C.c_void_p(b.device_ranks()), P(out), sp)))
-                res.append({"name": name + suffix, "kernel": kern, "bytes": 4 * H * T * R + 4 * H * T * D,
-                            "ms": ms, "R": R, "in_step": engine == L.RECON_CUDA_CORE})
+                res.append({"name": name + ("" if in_step else f"_{eng_name}"), "kernel": kern + ", f32 coefficients",
+                            "bytes": 4 * H * T * R + 4 * H * T * D, "ms": ms, "R": R, "in_step": in_step})
         finally:
-            L.check(lib.kvf_set_reconstruct_engine(ctx, L.RECON_CUDA_CORE))
+            L.check(lib.kvf_set_reconstruct_engine(ctx, L.RECON_AUTO))
     return res
 
 
@@ -516,7 +539,7 @@ def gpu_arm(args):
                            device=f"cuda:{dev}" if world > 1 else None)
     e2e_tot = reduce_stats(e2e_per)
 
-    kr = kernel_rooflines(lib, L, K, torch, layers[0], dev) if rank == 0 else []
+    kr = kernel_rooflines(lib, L, K, torch, layers[0], dev, cfg) if rank == 0 else []
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

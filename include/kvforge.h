@@ -96,12 +96,15 @@ int kvf_abi_version(void);
  * relative Frobenius error 1e-5 of the reference loop. */
 kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
 /* engine of the non-exact reconstruction (kvf_reconstruct, decompression):
- * CUDA_CORE (default): one fused multiply-add per term in the reference's
- *   order, many small blocks per SM that share the GPU with concurrent work;
- * TENSOR_CORE: for head_dim 128 and at most 16 coefficients, a tcgen05 GEMM
+ * CUDA_CORE: one fused multiply-add per term in the reference's order; up to
+ *   16 coefficients the basis sits in registers and many small blocks per SM
+ *   share the GPU with concurrent work, beyond that a shared-memory kernel
+ *   that is bound by its multiply-adds;
+ * TENSOR_CORE: for head_dim 128 and up to 64 coefficients, a tcgen05 GEMM
  *   (operands split into two tf32 parts, three products, accumulators in
- *   TMEM) with one block per SM; other shapes fall back to CUDA cores. */
-typedef enum { KVF_RECON_CUDA_CORE = 0, KVF_RECON_TENSOR_CORE = 1 } kvf_recon_engine;
+ *   TMEM) with one block per SM; other shapes fall back to CUDA cores;
+ * AUTO (default): CUDA cores up to 16 coefficients, tensor cores above. */
+typedef enum { KVF_RECON_AUTO = 0, KVF_RECON_CUDA_CORE = 1, KVF_RECON_TENSOR_CORE = 2 } kvf_recon_engine;
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine);
 /* Runs one of the library's bounded device waits against a barrier or status
  * word that nothing completes, with a 2 ms limit: the wait gives up and the

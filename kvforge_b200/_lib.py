@@ -35,7 +35,7 @@ INT4, INT8, F32 = 0, 1, 2
 PER_CHANNEL, PER_TOKEN = 0, 1
 IN_F32, IN_F16 = 0, 1
 CONSERVATIVE, BALANCED, AGGRESSIVE, ADAPTIVE = 0, 1, 2, 3
-RECON_CUDA_CORE, RECON_TENSOR_CORE = 0, 1
+RECON_AUTO, RECON_CUDA_CORE, RECON_TENSOR_CORE = 0, 1, 2
 WAIT_MBARRIER, WAIT_LOOKBACK = 0, 1
 
 # every symbol include/kvforge.h declares

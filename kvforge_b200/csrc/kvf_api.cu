@@ -130,7 +130,7 @@ struct TensorC {
 struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
-  int recon_engine = KVF_RECON_CUDA_CORE;
+  int recon_engine = KVF_RECON_AUTO;
   unsigned* d_status = nullptr;
   // the context's own stream-ordered pool: freed blocks stay cached, and a
   // block freed on one stream is reused on another only once its free has
@@ -452,7 +452,7 @@ kvf_status decompress_tensor(kvf_ctx* ctx, const TensorC& t, float* out, cudaStr
     StageTimer tm(ctx, KVF_STAGE_RECONSTRUCT, out_bytes + (double)t.H * t.basis->R * t.D * 4, st);
     KVF_CUDA(launch_dequant_reconstruct(codes, nullptr, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T,
                                         t.qcols, t.D, t.basis->d_vt, t.basis->d_ranks, ctx->exact_reconstruct,
-                                        ctx->recon_engine == KVF_RECON_TENSOR_CORE, out, ctx->d_status, st));
+                                        ctx->recon_engine, out, ctx->d_status, st));
   } else {
     StageTimer tm(ctx, KVF_STAGE_DEQUANTIZE, out_bytes, st);
     KVF_CUDA(launch_dequantize(codes, t.d_scales, t.d_mins, t.data_type, t.axis, t.H, t.T, t.D, out, st));
@@ -828,7 +828,7 @@ kvf_status kvf_selftest_wait_timeout(kvf_ctx* ctx, int which, void* stream) {
 
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine) {
   KVF_TRY(check_ctx(ctx));
-  if (engine != KVF_RECON_CUDA_CORE && engine != KVF_RECON_TENSOR_CORE)
+  if (engine != KVF_RECON_AUTO && engine != KVF_RECON_CUDA_CORE && engine != KVF_RECON_TENSOR_CORE)
     return fail(KVF_ERR_INVALID_CONFIG, "unknown reconstruction engine");
   ctx->recon_engine = engine;
   return KVF_OK;
@@ -1004,7 +1004,7 @@ kvf_status kvf_reconstruct(kvf_ctx* ctx, const float* projected, size_t H, size_
   DeviceGuard g(ctx->device);
   KVF_CUDA(launch_dequant_reconstruct(nullptr, projected, nullptr, nullptr, KVF_F32, KVF_PER_TOKEN, H, T, R, D,
                                       basis_vt, ranks, ctx->exact_reconstruct,
-                                      ctx->recon_engine == KVF_RECON_TENSOR_CORE, out, ctx->d_status, S(stream)));
+                                      ctx->recon_engine, out, ctx->d_status, S(stream)));
   return KVF_OK;
 }
 

@@ -224,7 +224,7 @@ cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t til
                                   size_t D, float* scores, cudaStream_t st);
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable), looked up once
 void* tensor_map_encode_fn();
-// tensor-core reconstruction (kvf_tc.cu): D == 128, R <= 16; cudaErrorNotSupported
+// tensor-core reconstruction (kvf_tc.cu): D == 128, R <= 64; cudaErrorNotSupported
 // when the shape or the driver does not allow it (the caller then uses the
 // CUDA-core kernels)
 cudaError_t launch_reconstruct_tc(const uint8_t* codes, const float* raw, const float* scales, const float* mins,
@@ -233,11 +233,11 @@ cudaError_t launch_reconstruct_tc(const uint8_t* codes, const float* raw, const 
                                   cudaStream_t st);
 // packed codes (or raw f32 when data_type == KVF_F32) + params + basis -> f32 [H,T,D];
 // exact: the reference's separately rounded order on CUDA cores; otherwise
-// tensor_cores selects the tcgen05 kernel where the shape allows it
+// engine (kvf_recon_engine) picks the tcgen05 kernel where the shape allows it
 cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
                                        const float* mins, int data_type, int axis, size_t H,
                                        size_t T, size_t R, size_t D, const float* basis_vt,
-                                       const uint64_t* ranks, int exact, int tensor_cores, float* out,
+                                       const uint64_t* ranks, int exact, int engine, float* out,
                                        unsigned* status, cudaStream_t st);
 size_t gram_num_tiles(size_t T);
 cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t D,

@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -199,7 +200,12 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
   const long long nit = i1 - i0;
   constexpr int kColElems = kColBytes / (int)sizeof(TIn);
   const int ncb = TMA ? D / kColElems : 1;  // column blocks per tile
-  const long long units = nit * ncb;
+  // several passes (r-groups) only with 32-wide groups (24 < R <= 64); below
+  // that one pass, and the basis stride stays a compile-time constant
+  constexpr bool kMulti = RG == 32;
+  const int nrg = kMulti ? (R + RG - 1) / RG : 1;
+  const int vstride = kMulti ? Rpad : RG;  // floats per basis row in shared memory
+  const long long units = nit * nrg * ncb;
   const bool hist_on = (MODE == 2) && o.hist != nullptr;
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
@@ -209,13 +215,14 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
   }
   __syncthreads();
 
-  // unit u = column block (u mod ncb) of item (u / ncb); this warp's 64 rows of
-  // it go to stage u mod stages, copied by lane 0
+  // unit u = column block (u mod ncb) of r-group pass ((u / ncb) mod nrg) of
+  // item (u / (ncb nrg)); this warp's 64 rows of it go to stage u mod stages,
+  // copied by lane 0 (a later pass copies the tile again, from L2)
   long long issued = 0;
   auto issue = [&](long long u) {
     if (!TMA || u >= units) return;
     if (lane == 0) {
-      const long long it = i0 + u / ncb;
+      const long long it = i0 + u / ((long long)ncb * nrg);
       const int cb = (int)(u % ncb);
       const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
       const int s = (int)(u % L.stages);
@@ -281,7 +288,7 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
 #pragma unroll
         for (int r = 0; r < RG / 2; ++r) acc2[rr][r] = 0ull;  // +0.0f in both halves
       for (int cb = 0; cb < ncb; ++cb) {
-        const long long u = li * ncb + cb;
+        const long long u = (li * nrg + rg / RG) * ncb + cb;
         if (TMA) {
           if (!dead) {
             const bool okw = mbar_wait(&wbar[u % L.stages], (uint32_t)((u / L.stages) & 1));
@@ -294,7 +301,7 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
           if (!dead) issue(u + L.stages - 1);
         }
         if (dead) continue;
-        if (TMA) {  // single r-group: vT rows are RG floats
+        if (TMA) {  // vT rows are vstride floats; this pass reads columns rg .. rg + RG - 1
           constexpr int PV = Seg<TIn>::PV;
           const uint8_t* sb[kProjNR];
           int sw[kProjNR];
@@ -313,7 +320,7 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
 #pragma unroll
             for (int rr = 0; rr < kProjNR; ++rr)
               Seg<TIn>::unpack(*reinterpret_cast<const uint4*>(sb[rr] + ((jj ^ sw[rr]) << 4)), xv[rr]);
-            if (CALIB) {
+            if (CALIB && rg == 0) {  // calibration sums in the first pass only
 #pragma unroll
               for (int rr = 0; rr < kProjNR; ++rr)
 #pragma unroll
@@ -323,16 +330,16 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
                   p2 = __fmaf_rn(v, v, p2);
                 }
             }
-            const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * RG;
+            const float* vb = vT + (size_t)(cb * kColElems + jj * PV) * vstride + rg;
 #pragma unroll
             for (int k = 0; k < PV; ++k) {
               float xk[kProjNR];
 #pragma unroll
               for (int rr = 0; rr < kProjNR; ++rr) xk[rr] = xv[rr][k];
-              fma_rows<RG>(acc2, xk, vb + k * RG);
+              fma_rows<RG>(acc2, xk, vb + k * vstride);
             }
           }
-          if (CALIB) {
+          if (CALIB && rg == 0) {
             s1 += (double)p1;
             s2 += (double)p2;
           }
@@ -508,10 +515,12 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   static int opted[kDevs] = {};    // opted in so far
   static int sms[kDevs] = {};
   static LaunchCache cache[kDevs][4];
+  static std::mutex mu;  // the caches above are shared by every host thread that launches
   cudaError_t e;
   int dev = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
+  std::unique_lock<std::mutex> lk(mu);
   if (!max_dyn[dev]) {
     int optin = 0;
     cudaFuncAttributes fa{};
@@ -520,7 +529,7 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
     if ((e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     max_dyn[dev] = std::max(1, optin - (int)fa.sharedSizeBytes);
   }
-  const int Rpad = TMA ? RG : (int)(((R + RG - 1) / RG) * RG);
+  const int Rpad = (int)(((R + RG - 1) / RG) * RG);
   const int Rk = (int)((R + 3) & ~size_t(3));
   ProjSmem L{};
   int off = (int)(D * Rpad * sizeof(float));
@@ -559,8 +568,10 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
         break;
       }
   }
+  const int nsm = sms[dev];
+  lk.unlock();
   const size_t items = H * ((T + kProjRows - 1) / kProjRows);
-  const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * sms[dev]));
+  const size_t grid = std::max<size_t>(1, std::min<size_t>(items, (size_t)per_sm * nsm));
   kern<<<(unsigned)grid, kProjThreads, L.total, st>>>(map, x, (int)H, (int)T, (int)D, bvt, ranks, (int)R, Rpad, L, o);
   note_launches(1);
   return cudaGetLastError();
@@ -589,14 +600,17 @@ cudaError_t project_rg(const CUtensorMap& map, const TIn* x, size_t H, size_t T,
   if (R <= 12) return project_mode<TIn, 12, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
   if (R <= 16) return project_mode<TIn, 16, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
   if (R <= 24) return project_mode<TIn, 24, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
-  return project_mode<TIn, 32, false>(map, x, H, T, D, bvt, ranks, R, o, st);  // several r-groups: generic path
+  // several r-groups: each pass over a tile computes 32 coefficients; the
+  // tensor-copy path streams the tile once per pass (the later passes from L2)
+  if (R <= 64) return project_mode<TIn, 32, TMA>(map, x, H, T, D, bvt, ranks, R, o, st);
+  return project_mode<TIn, 32, false>(map, x, H, T, D, bvt, ranks, R, o, st);
 }
 
 template <typename TIn>
 cudaError_t project_typed(const TIn* x, size_t H, size_t T, size_t D, const float* bvt, const uint64_t* ranks,
                           size_t R, const ProjectOut& o, cudaStream_t st) {
   CUtensorMap map{};
-  const bool tma = (D * sizeof(TIn)) % kColBytes == 0 && aligned(x, 16) && R <= 24 && H * T < (1ull << 31) &&
+  const bool tma = (D * sizeof(TIn)) % kColBytes == 0 && aligned(x, 16) && R <= 64 && H * T < (1ull << 31) &&
                    encode_rows_map(&map, x, H * T, D);
   if (tma) return project_rg<TIn, true>(map, x, H, T, D, bvt, ranks, R, o, st);
   return project_rg<TIn, false>(map, x, H, T, D, bvt, ranks, R, o, st);
@@ -938,25 +952,31 @@ cudaError_t dequant_reconstruct_mode(const uint8_t* codes, const float* raw, con
                                      cudaStream_t st) {
   const size_t smem = ((size_t)R * D + (size_t)R * kRecRows) * sizeof(float);
   if (D % 4 == 0 && D <= 128 && R <= 16 && aligned(out, 16) && aligned(bvt, 16) && H * T < (1ull << 31)) {
-    static int sms[64] = {};
+    // launch facts per device, shared by every host thread: each value is the
+    // same whichever thread computes it, so relaxed atomics suffice
+    static std::atomic<int> sms[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!sms[dev] && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-      return e;
+    int nsm = sms[dev].load(std::memory_order_relaxed);
+    if (!nsm) {
+      if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+      sms[dev].store(nsm, std::memory_order_relaxed);
+    }
     const size_t items = H * ((T + kRecRows - 1) / kRecRows);
     // persistent grid: as many blocks as fit at once, cached per instantiation and device
 #define KVF_RR(RGV)                                                                                           \
   {                                                                                                           \
     auto kern = k_reconstruct_reg<MODE, EXACT, RGV>;                                                          \
-    static int per_sm[64] = {};                                                                               \
-    if (!per_sm[dev]) {                                                                                       \
-      int n = 0;                                                                                              \
-      if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 128, 0)) != cudaSuccess) return e;     \
-      per_sm[dev] = std::max(n, 1);                                                                           \
+    static std::atomic<int> per_sm[64];                                                                       \
+    int nb = per_sm[dev].load(std::memory_order_relaxed);                                                     \
+    if (!nb) {                                                                                                \
+      if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 128, 0)) != cudaSuccess) return e;    \
+      nb = std::max(nb, 1);                                                                                   \
+      per_sm[dev].store(nb, std::memory_order_relaxed);                                                       \
     }                                                                                                         \
-    const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)sms[dev] * per_sm[dev])); \
+    const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)nsm * nb));           \
     kern<<<grid, 128, 0, st>>>(codes, raw, scales, mins, axis, (int)H, (int)T, (int)R, (int)D, bvt, ranks, out); \
   }
     if (R <= 4) KVF_RR(4)
@@ -1148,10 +1168,12 @@ cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t til
 cudaError_t launch_dequant_reconstruct(const uint8_t* codes, const float* raw, const float* scales,
                                        const float* mins, int data_type, int axis, size_t H,
                                        size_t T, size_t R, size_t D, const float* basis_vt,
-                                       const uint64_t* ranks, int exact, int tensor_cores, float* out,
+                                       const uint64_t* ranks, int exact, int engine, float* out,
                                        unsigned* status, cudaStream_t st) {
   if (H == 0 || T == 0 || D == 0) return cudaSuccess;
-  if (!exact && tensor_cores) {  // tensor cores where the shape allows them
+  // tensor cores where chosen and the shape allows them; by default beyond 16
+  // coefficients, where the CUDA-core kernel is bound by its multiply-adds
+  if (!exact && (engine == KVF_RECON_TENSOR_CORE || (engine == KVF_RECON_AUTO && R > 16))) {
     const cudaError_t e = launch_reconstruct_tc(codes, raw, scales, mins, data_type, axis, H, T, R, D, basis_vt,
                                                 ranks, out, status, st);
     if (e != cudaErrorNotSupported) return e;

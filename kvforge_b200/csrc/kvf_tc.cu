@@ -5,7 +5,7 @@
 // (crates/kvforge-cpu/src/projection.rs:142-172); its result is a tolerance
 // check (relative Frobenius error, 1e-4 for fp32), not a bit-exact one, so the
 // default reconstruction runs here as a GEMM: M = 128 tokens, N = D = 128
-// output channels, K = R coefficients (padded to 8 or 16). Each f32 operand is
+// output channels, K = R coefficients (padded to 8, 16, 32 or 64). Each f32 operand is
 // split into two tf32 parts (split_tf32); three kind::tf32 passes
 // (hi·hi + hi·lo + lo·hi) leave a relative error near 2^-21 per product. The
 // separately rounded CPU order stays available bit for bit on the CUDA-core
@@ -16,8 +16,9 @@
 // times. One persistent CTA per SM walks (head, 128-token tile) items with
 // two warp roles that run a tile apart:
 //   producer warps 4-7: dequantize one token row per thread (q * scale + min,
-//     separately rounded as the reference does; codes fetched three tiles ahead)
-//     into the A operands of stage n % 2 (K-major core matrices without
+//     separately rounded as the reference does; inputs fetched three tiles
+//     ahead, one tile for 64 f32 coefficients per row)
+//     into the A operands of stage n % 2 (one stage at K = 64; K-major core matrices without
 //     swizzle; the head's basis sits the same way in the B operands); one
 //     thread issues the MMAs into TMEM accumulator n % 2 and commits them to
 //     acc_full[n % 2];
@@ -33,6 +34,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "kvf_internal.cuh"
 
@@ -47,8 +49,22 @@ constexpr int kTcThreads = 32 * (kEpiWarps + kProdWarps);
 constexpr int kProdThreads = 32 * kProdWarps;
 constexpr int kRowsPerProd = kTcRows / kProdThreads;  // 1
 constexpr int kSlotBytes = 32 * 128;  // one staging slot: 32 tokens x 32 channels
-constexpr int kSlots = 6;             // staging slots per epilogue warp (even: filled in pairs)
 constexpr int kTmemCols = 2 * kTcD;   // two accumulators
+
+// shared-memory plan per K (= 4 KC coefficients): two A-operand stages and
+// six staging slots per epilogue warp up to K = 32; one A stage and four slots
+// at K = 64, where the operands (4 x 32 KB) leave no room for more
+template <int KC>
+struct TcPlan {
+  static constexpr int kAStages = KC <= 8 ? 2 : 1;
+  static constexpr int kSlots = KC <= 8 ? 6 : 4;  // even: filled in pairs
+};
+// tiles ahead that a producer thread's inputs are fetched: three register
+// sets in rotation, or one set for 64 f32 coefficients per row
+template <int MODE, int KC>
+constexpr int tc_depth() {
+  return (MODE == 0 && KC == 16) ? 1 : 3;
+}
 
 __device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -131,7 +147,7 @@ __device__ __forceinline__ bool producer_any(bool p) {
   return r != 0;
 }
 
-// one producer thread's token rows of one item, fetched three tiles ahead
+// one producer thread's token rows of one item, fetched ahead (tc_depth)
 template <int MODE, int KC>
 struct RowsIn {
   uint32_t q[kRowsPerProd][MODE == 0 ? 1 : KC];  // codes, one byte each
@@ -139,7 +155,7 @@ struct RowsIn {
   float sc[kRowsPerProd], mn[kRowsPerProd];
 };
 
-// MODE 0: raw f32 coefficients, 1: INT8 codes, 2: INT4 codes; KC: K in 4-wide chunks (2 or 4)
+// MODE 0: raw f32 coefficients, 1: INT8 codes, 2: INT4 codes; KC: K in 4-wide chunks (2, 4, 8 or 16)
 template <int MODE, int KC>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_reconstruct_tc(const __grid_constant__ CUtensorMap omap, const uint8_t* __restrict__ codes,
@@ -149,13 +165,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      unsigned* __restrict__ status) {
   constexpr int K = 4 * KC;
   constexpr int kOpBytes = kTcRows * K * 4;  // one operand part
+  constexpr int kAStages = TcPlan<KC>::kAStages;
+  constexpr int kSlots = TcPlan<KC>::kSlots;
   extern __shared__ uint8_t sm_raw[];
   // staging slots use the 128-byte swizzle, whose pattern is taken from
   // address bits 7-9: the layout starts on a 1024-byte boundary
   uint8_t* sm = sm_raw + ((1024u - (sa(sm_raw) & 1023u)) & 1023u);
   uint8_t* ring = sm;                                       // [4 warps][kSlots][32 rows][128 B]
-  uint8_t* a_ops = ring + kEpiWarps * kSlots * kSlotBytes;  // [2 stages][hi, lo]
-  uint8_t* b_hi = a_ops + 4 * kOpBytes;
+  uint8_t* a_ops = ring + kEpiWarps * kSlots * kSlotBytes;  // [kAStages][hi, lo]
+  uint8_t* b_hi = a_ops + 2 * kAStages * kOpBytes;
   uint8_t* b_lo = b_hi + kOpBytes;
   float* pscale = reinterpret_cast<float*>(b_lo + kOpBytes);  // per-channel parameters of the head [K]
   float* pmin = pscale + K;
@@ -220,16 +238,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     };
     int cur_h = -1, rank = 0;
+    constexpr int kDepth = tc_depth<MODE, KC>();
     // one tile's work; `in` holds its inputs and is refilled with those of the
-    // tile three ahead. Returns true when the producers stop (together).
+    // tile kDepth ahead. Returns true when the producers stop (together).
     auto step = [&](long long it, RowsIn<MODE, KC>& in) -> bool {
-      const int n = (int)(it - i0), s = n & 1;
+      const int n = (int)(it - i0), s = n & 1, as_ = n % kAStages;
       const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
       // a new head's basis may be written once the MMAs of tile n - 1
-      // completed; stage s once those of tile n - 2 did
+      // completed; A stage as_ once those of tile n - kAStages did
       if (!timed_out && h != cur_h && n >= 1 && !mbar_wait(&acc_full[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag))
         timed_out = true;
-      if (!timed_out && n >= 2 && !mbar_wait(&acc_full[s], ((n - 2) >> 1) & 1, abort_flag)) timed_out = true;
+      const int m = n - kAStages;
+      if (!timed_out && m >= 0 && !mbar_wait(&acc_full[m & 1], (m >> 1) & 1, abort_flag)) timed_out = true;
       if (timed_out) *abort_flag = 1;
       if (producer_any(timed_out || *abort_flag)) return true;
       if (h != cur_h) {
@@ -259,7 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         cur_h = h;
         producer_sync();
       }
-      uint8_t* a_hi = a_ops + (2 * s) * kOpBytes;
+      uint8_t* a_hi = a_ops + (2 * as_) * kOpBytes;
       uint8_t* a_lo = a_hi + kOpBytes;
 #pragma unroll
       for (int j = 0; j < kRowsPerProd; ++j) {  // terms k >= rank are zero
@@ -315,18 +335,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                        : "memory");
         }
       }
-      if (it + 3 < i1) fetch(it + 3, in);  // in flight for the next three tiles
+      if (it + kDepth < i1) fetch(it + kDepth, in);  // in flight for the next kDepth tiles
       return false;
     };
-    // three register sets in rotation, so no set is copied while its loads are in flight
-    RowsIn<MODE, KC> r0, r1, r2;
-    if (i0 < i1) fetch(i0, r0);
-    if (i0 + 1 < i1) fetch(i0 + 1, r1);
-    if (i0 + 2 < i1) fetch(i0 + 2, r2);
-    for (long long it = i0; it < i1; it += 3) {
-      if (step(it, r0)) break;
-      if (it + 1 < i1 && step(it + 1, r1)) break;
-      if (it + 2 < i1 && step(it + 2, r2)) break;
+    if constexpr (kDepth == 3) {
+      // three register sets in rotation, so no set is copied while its loads are in flight
+      RowsIn<MODE, KC> r0, r1, r2;
+      if (i0 < i1) fetch(i0, r0);
+      if (i0 + 1 < i1) fetch(i0 + 1, r1);
+      if (i0 + 2 < i1) fetch(i0 + 2, r2);
+      for (long long it = i0; it < i1; it += 3) {
+        if (step(it, r0)) break;
+        if (it + 1 < i1 && step(it + 1, r1)) break;
+        if (it + 2 < i1 && step(it + 2, r2)) break;
+      }
+    } else {
+      RowsIn<MODE, KC> r0;
+      if (i0 < i1) fetch(i0, r0);
+      for (long long it = i0; it < i1; ++it)
+        if (step(it, r0)) break;
     }
   } else {
     // ---------------- epilogue ----------------
@@ -409,8 +436,8 @@ bool encode_out_map(CUtensorMap* map, float* out, size_t H, size_t T) {
 
 template <int KC>
 constexpr size_t tc_smem() {
-  return 1024 + (size_t)kEpiWarps * kSlots * kSlotBytes + 6 * (size_t)kTcRows * (4 * KC) * 4 +
-         2 * (4 * KC) * 4 + 64;
+  return 1024 + (size_t)kEpiWarps * TcPlan<KC>::kSlots * kSlotBytes +
+         (2 * TcPlan<KC>::kAStages + 2) * (size_t)kTcRows * (4 * KC) * 4 + 2 * (4 * KC) * 4 + 64;
 }
 
 template <int MODE, int KC>
@@ -422,21 +449,23 @@ cudaError_t launch_tc(const CUtensorMap& map, const uint8_t* codes, const float*
   // more than half of the SM's 228 KB of shared memory: at most one CTA of
   // this kernel per SM, so the 256 TMEM columns it allocates are always free
   static_assert(2 * (smem + 1024) > 228 * 1024, "one CTA per SM keeps the TMEM allocation non-blocking");
+  // per device: the SM count once the shared-memory opt-in is done (0 before);
+  // shared by every host thread, and the same whichever thread sets it
   constexpr int kDevs = 64;
-  static int sms[kDevs] = {};
-  static bool attr[kDevs] = {};
+  static std::atomic<int> sms[kDevs];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
-  if (!attr[dev]) {
-    if ((e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  int nsm = sms[dev].load(std::memory_order_acquire);
+  if (!nsm) {
+    if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
-    attr[dev] = true;
+    sms[dev].store(nsm, std::memory_order_release);
   }
   const size_t items = H * ((T + kTcRows - 1) / kTcRows);
-  const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)sms[dev]));
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)nsm));
   kern<<<grid, kTcThreads, smem, st>>>(map, codes, raw, scales, mins, axis, (int)H, (int)T, (int)R, bvt, ranks,
                                        status);
   note_launches(1);
@@ -449,18 +478,22 @@ cudaError_t launch_reconstruct_tc(const uint8_t* codes, const float* raw, const 
                                   int data_type, int axis, size_t H, size_t T, size_t R, size_t D,
                                   const float* basis_vt, const uint64_t* ranks, float* out, unsigned* status,
                                   cudaStream_t st) {
-  if (D != (size_t)kTcD || R == 0 || R > 16 || !aligned(out, 16) || H * T == 0 || T >= (1u << 31) ||
+  if (D != (size_t)kTcD || R == 0 || R > 64 || !aligned(out, 16) || H * T == 0 || T >= (1u << 31) ||
       H >= (1u << 31))
     return cudaErrorNotSupported;
   CUtensorMap map{};
   if (!encode_out_map(&map, out, H, T)) return cudaErrorNotSupported;
   const int mode = raw ? 0 : (data_type == KVF_INT8 ? 1 : 2);
-#define KVF_TC(M)                                                                                           \
-  return (R <= 8) ? launch_tc<M, 2>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st) \
-                  : launch_tc<M, 4>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st)
-  if (mode == 0) { KVF_TC(0); }
-  if (mode == 1) { KVF_TC(1); }
-  KVF_TC(2);
+#define KVF_TC(M)                                                                                          \
+  {                                                                                                        \
+    if (R <= 8) return launch_tc<M, 2>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st); \
+    if (R <= 16) return launch_tc<M, 4>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st); \
+    if (R <= 32) return launch_tc<M, 8>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st); \
+    return launch_tc<M, 16>(map, codes, raw, scales, mins, axis, H, T, R, basis_vt, ranks, status, st);          \
+  }
+  if (mode == 0) KVF_TC(0)
+  if (mode == 1) KVF_TC(1)
+  KVF_TC(2)
 #undef KVF_TC
 }
 

@@ -162,6 +162,46 @@ def test_project_parity(kvf, oracle, shape, thr, f16):
     assert np.array_equal(bits(P), bits(Po))
 
 
+@pytest.mark.parametrize("R", [25, 32, 40, 58, 64])
+@pytest.mark.parametrize("f16", [False, True])
+def test_project_parity_several_passes(kvf, oracle, R, f16):
+    """24 < R <= 64: the tensor-copy projection makes one pass per 32
+    coefficients over every tile; ranks below R, and rank 1, included."""
+    shape = (3, 700, 128)
+    xin, x32 = _x(shape, 100 + R, f16)
+    rng = np.random.default_rng(R)
+    bvt = (rng.standard_normal((3, R, 128)) / np.sqrt(128)).astype(np.float32)
+    ranks = np.array([R, max(1, R - 7), 1], np.uint64)
+    basis = kvf.Basis.from_host(bvt, ranks)
+    P = host(kvf.GpuProjector().project(dev(xin), basis))
+    Po = oracle.project(x32, bvt, ranks, threads=4)
+    assert np.array_equal(bits(P), bits(Po))
+
+
+def test_pipeline_parity_high_rank(kvf, oracle):
+    """A layer whose ranks exceed 32 (per-channel keys with calibration and
+    per-token values, two projection passes per tile, tensor-core
+    reconstruction by default): codes, bitstreams and ratio bit-exact,
+    reconstruction within REC_TOL, and bit-exact in the exact mode."""
+    from kvforge_b200 import _lib as L
+    from kvforge_b200 import synth
+    # a 0.2 noise floor over 128 channels spreads 75 % of the variance over about 46 directions
+    k, v = synth.numpy_layer(2, 640, 128, seed=77, rank=24, noise=0.2, outlier=None, dtype="float16")
+    c, co = _pipeline_case(kvf, oracle, k, v, "aggressive")
+    Rk, Rv = c.tensor_info(0)["R"], c.tensor_info(1)["R"]
+    assert 32 < Rk <= 64 and 32 < Rv <= 64, (Rk, Rv)
+    kr, vr = oracle.decompress(co, threads=4)
+    out = kvf.decompress(c)
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
+    _exact(L, True)
+    try:
+        out = kvf.decompress(c)
+    finally:
+        _exact(L, False)
+    assert np.array_equal(bits(out.keys()), bits(kr)) and np.array_equal(bits(out.values()), bits(vr))
+    assert np.allclose(c.calibration_scores(), co["scores"], rtol=1e-6, atol=1e-7)
+
+
 @pytest.mark.parametrize("shape,thr", [((2, 300, 16), 0.9), ((4, 1000, 128), 0.99), ((2, 77, 13), 0.8)])
 def test_reconstruct_parity(kvf, oracle, shape, thr):
     from kvforge_b200 import _lib as L
@@ -192,14 +232,17 @@ def tensor_cores():
     from kvforge_b200 import _lib as L
     L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_TENSOR_CORE))
     yield
-    L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_CUDA_CORE))
+    L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_AUTO))
 
 
 @pytest.mark.parametrize("H,T,R,ranks", [(1, 1, 1, [1]), (2, 127, 3, [3, 2]), (3, 128, 8, [8, 8, 5]),
-                                         (2, 129, 9, [9, 1]), (2, 1000, 16, [16, 12]), (5, 300, 13, [13, 0, 7, 13, 4])])
+                                         (2, 129, 9, [9, 1]), (2, 1000, 16, [16, 12]), (5, 300, 13, [13, 0, 7, 13, 4]),
+                                         (2, 500, 17, [17, 9]), (3, 260, 32, [32, 31, 1]), (2, 300, 40, [40, 33]),
+                                         (1, 257, 64, [64])])
 def test_tensor_core_reconstruct_raw(kvf, oracle, tensor_cores, H, T, R, ranks):
-    """head_dim 128, R <= 16: the tcgen05 path (partial tiles, ranks below R,
-    rank 0) against the reference loop; the exact mode stays bit-exact."""
+    """head_dim 128, R <= 64: the tcgen05 path (partial tiles, ranks below R,
+    rank 0, one and two A-operand stages) against the reference loop; the
+    exact mode stays bit-exact."""
     from kvforge_b200 import _lib as L
     rng = np.random.default_rng(H * 1000 + T + R)
     D = 128
@@ -225,8 +268,9 @@ def test_tensor_core_reconstruct_raw(kvf, oracle, tensor_cores, H, T, R, ranks):
 
 
 @pytest.mark.parametrize("dt", [INT8, INT4])
-@pytest.mark.parametrize("shape,thr", [((2, 300, 128), 0.9), ((3, 77, 128), 0.75)])
-def test_tensor_core_reconstruct_codes(kvf, oracle, tensor_cores, dt, shape, thr):
+@pytest.mark.parametrize("shape,thr,maxr", [((2, 300, 128), 0.9, 12), ((3, 77, 128), 0.75, 12),
+                                            ((2, 300, 128), 0.99, 40), ((2, 400, 128), 0.999, 64)])
+def test_tensor_core_reconstruct_codes(kvf, oracle, tensor_cores, dt, shape, thr, maxr):
     """Projected INT8 and INT4 codes, keys per channel and values per token,
     decompressed on the tcgen05 path against the reference pipeline."""
     from kvforge_b200 import _lib as L
@@ -236,9 +280,9 @@ def test_tensor_core_reconstruct_codes(kvf, oracle, tensor_cores, dt, shape, thr
     cfg = kvf.config_from_preset("balanced")
     cfg.key_data_type = cfg.value_data_type = dt
     cfg.projection_variance_threshold = thr
-    kb = kvf.Basis.compute(dev(k), thr, max_rank=12)
-    vb = kvf.Basis.compute(dev(v), thr, max_rank=12)
-    assert kb.R <= 12 and vb.R <= 12
+    kb = kvf.Basis.compute(dev(k), thr, max_rank=maxr)
+    vb = kvf.Basis.compute(dev(v), thr, max_rank=maxr)
+    assert kb.R <= maxr and vb.R <= maxr
     c = kvf.CompressionPipeline().compress_with_config(kvf.KVCache(dev(k), dev(v), 0), cfg, kb, vb)
     kr = oracle.decompress_tensor(oracle.compress_tensor(k.astype(np.float32), dt, PC, kb.host()[:2]))
     vr = oracle.decompress_tensor(oracle.compress_tensor(v.astype(np.float32), dt, PT, vb.host()[:2]))
@@ -476,5 +520,5 @@ def test_full_size_llama_layer(kvf, oracle):
     try:
         out = kvf.decompress(c)
     finally:
-        L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_CUDA_CORE))
+        L.check(L.lib().kvf_set_reconstruct_engine(L.context(0), L.RECON_AUTO))
     assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
