@@ -63,20 +63,23 @@ __device__ __forceinline__ void block_sum2(double& a, double& b) {
 
 // ---- projection -------------------------------------------------------------
 // One persistent kernel. The grid walks (head, 256-token tile) items in
-// contiguous ranges per block; thread t owns rows t and t + 128 of every tile
-// and computes their R coefficients. Each coefficient is a fused multiply-add
-// chain over c = 0..D-1 from +0.0; two chains advance per fma.rn.f32x2 (each
-// element rounded once), so values are identical to the CPU oracle's fmaf
-// chain. The basis of head h sits transposed in shared memory, vT[c][RG],
-// read with broadcast 16-byte loads at compile-time offsets; each load feeds
-// both of a thread's rows.
+// contiguous ranges per block; warp w owns rows 64w .. 64w + 63 of every tile
+// and lane l rows l and l + 32 of those, and computes their R coefficients.
+// Each coefficient is a fused multiply-add chain over c = 0..D-1 from +0.0;
+// two chains advance per fma.rn.f32x2 (each element rounded once), so values
+// are identical to the CPU oracle's fmaf chain. The basis of head h sits
+// transposed in shared memory, vT[c][R rounded up to RG], read with broadcast
+// 16-byte loads (at compile-time offsets when one pass covers R); each load
+// feeds both of a thread's rows. Coefficients are computed RG at a time: one
+// pass over a tile up to R = 24, one pass per 32 coefficients up to R = 64.
 //
 // TMA variant (rows a multiple of 64 bytes, 16-byte aligned input): each warp
 // streams its own 64 rows of a tile as column blocks of 64 rows x 64 bytes
 // (4 KB), each one 2-D tensor copy (cp.async.bulk.tensor, no multicast) with
 // the 64-byte swizzle, issued by lane 0 into the warp's own stages and
 // mbarriers, several in flight; the accumulators stay in registers across a
-// tile's column blocks. Warps synchronise with each other only when the head
+// tile's column blocks, and a later pass streams the tile again (from L2).
+// Warps synchronise with each other only when the head
 // (and so the shared basis) changes. The swizzle stores 16-byte chunk j of a
 // 64-byte row at j ^ (bits 7-8 of the row's address), so the reads of eight
 // consecutive rows fall on distinct banks. Small stages keep several CTAs
