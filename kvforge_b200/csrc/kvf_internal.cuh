@@ -153,6 +153,53 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   return false;
 }
 
+// ---- codes of one row, fetched ahead of their use ---------------------------
+// The codes of a row (INT4: nibbles, INT8: bytes, flat index `first` onwards)
+// as the aligned 32-bit words that cover them. Loading only fills registers,
+// so the loads stay in flight until the codes are taken apart, when the row
+// is dequantized; words past the end of the buffer (nbytes) are assembled
+// from the bytes that exist, so nothing outside it is read.
+template <bool INT4, int K>
+constexpr int code_words() {
+  return INT4 ? (K - 1) / 8 + 2 : (K - 1) / 4 + 2;
+}
+template <int NW>
+struct CodeWords {
+  uint32_t w[NW];
+  uint32_t base;  // position of code 0 in the window: nibbles (INT4) or bytes (INT8)
+};
+template <bool INT4, int NW>
+__device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ codes, size_t nbytes, size_t first,
+                                                bool ok, CodeWords<NW>& cw) {
+  const size_t b0 = INT4 ? (first >> 1) : first;
+  const size_t w0 = b0 & ~(size_t)3;
+  cw.base = INT4 ? (uint32_t)(first - 2 * w0) : (uint32_t)(first - w0);
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    const size_t a = w0 + 4 * (size_t)j;
+    uint32_t v = 0u;
+    if (ok) {
+      if (a + 4 <= nbytes) {
+        v = __ldg(reinterpret_cast<const uint32_t*>(codes + a));
+      } else {
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          if (a + b < nbytes) v |= (uint32_t)codes[a + b] << (8 * b);
+      }
+    }
+    cw.w[j] = v;
+  }
+}
+// code k of the row (k a compile-time constant after unrolling, so the word
+// indices are static); low nibble first within a byte, as the packing
+template <bool INT4, int NW>
+__device__ __forceinline__ uint32_t code_at(const CodeWords<NW>& cw, int k) {
+  const int j = INT4 ? (k >> 3) : (k >> 2);
+  const uint32_t p = cw.base + (uint32_t)(INT4 ? (k & 7) : (k & 3));
+  const uint64_t v = ((uint64_t)cw.w[j + 1] << 32) | cw.w[j];
+  return INT4 ? (uint32_t)(v >> (4 * p)) & 0xFu : (uint32_t)(v >> (8 * p)) & 0xFFu;
+}
+
 __device__ __forceinline__ float dq(uint32_t q, float scale, float mn) {
   return __fadd_rn(__fmul_rn((float)q, scale), mn);
 }

@@ -769,7 +769,7 @@ __global__ void __launch_bounds__(128) k_dequant_reconstruct(
 // sum unchanged (it starts at +0.0), so results equal the per-rank loop.
 template <int MODE, bool EXACT, int RG>
 __global__ void __launch_bounds__(128, (RG >= 12 ? 3 : 4)) k_reconstruct_reg(const uint8_t* __restrict__ codes,
-                                                         const float* __restrict__ raw,
+                                                         size_t ncode_bytes, const float* __restrict__ raw,
                                                          const float* __restrict__ scales,
                                                          const float* __restrict__ mins, int axis, int H, int T,
                                                          int R, int D, const float* __restrict__ bvt,
@@ -784,7 +784,7 @@ __global__ void __launch_bounds__(128, (RG >= 12 ? 3 : 4)) k_reconstruct_reg(con
 
   // this thread's row of item `it`: raw inputs fetched now, dequantized later
   struct RowIn {
-    uint32_t q[(RG + 3) / 4];  // codes, one byte each
+    CodeWords<MODE == 0 ? 1 : code_words<MODE == 2, RG>()> cw;  // codes, as loaded
     float raw[MODE == 0 ? RG : 1];
     float sc, mn;
   };
@@ -797,18 +797,11 @@ __global__ void __launch_bounds__(128, (RG >= 12 ? 3 : 4)) k_reconstruct_reg(con
       in.sc = ok ? __ldg(scales + g) : 0.0f;
       in.mn = ok ? __ldg(mins + g) : 0.0f;
     }
+    if (MODE == 0) {
 #pragma unroll
-    for (int k = 0; k < (RG + 3) / 4; ++k) in.q[k] = 0u;
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const size_t fi = g * R + r;
-      if (MODE == 0) {
-        in.raw[r] = (ok && r < R) ? __ldg(raw + fi) : 0.0f;
-      } else if (ok && r < R) {
-        uint32_t q = codes[MODE == 2 ? (fi >> 1) : fi];
-        if (MODE == 2) q = (fi & 1) ? (q >> 4) & 0xFu : q & 0xFu;
-        in.q[r >> 2] |= q << (8 * (r & 3));
-      }
+      for (int r = 0; r < RG; ++r) in.raw[r] = (ok && r < R) ? __ldg(raw + g * R + r) : 0.0f;
+    } else {
+      load_code_words<MODE == 2>(codes, ncode_bytes, g * R, ok, in.cw);
     }
   };
   auto stage = [&](long long it, const RowIn& in, int buf, int rank) {
@@ -826,7 +819,7 @@ __global__ void __launch_bounds__(128, (RG >= 12 ? 3 : 4)) k_reconstruct_reg(con
             sc = __ldg(scales + (size_t)h * R + r);
             mn = __ldg(mins + (size_t)h * R + r);
           }
-          d = __fadd_rn(__fmul_rn((float)((in.q[r >> 2] >> (8 * (r & 3))) & 0xFFu), sc), mn);
+          d = __fadd_rn(__fmul_rn((float)code_at<MODE == 2>(in.cw, r), sc), mn);
         }
       }
       unsigned long long dd;
@@ -954,7 +947,9 @@ cudaError_t dequant_reconstruct_mode(const uint8_t* codes, const float* raw, con
                                      size_t D, const float* bvt, const uint64_t* ranks, float* out,
                                      cudaStream_t st) {
   const size_t smem = ((size_t)R * D + (size_t)R * kRecRows) * sizeof(float);
-  if (D % 4 == 0 && D <= 128 && R <= 16 && aligned(out, 16) && aligned(bvt, 16) && H * T < (1ull << 31)) {
+  if (D % 4 == 0 && D <= 128 && R <= 16 && aligned(out, 16) && aligned(bvt, 16) && H * T < (1ull << 31) &&
+      (MODE == 0 || aligned(codes, 4))) {
+    const size_t ncode = MODE == 2 ? (H * T * R + 1) / 2 : H * T * R;  // bytes of the code buffer
     // launch facts per device, shared by every host thread: each value is the
     // same whichever thread computes it, so relaxed atomics suffice
     static std::atomic<int> sms[64];
@@ -980,7 +975,8 @@ cudaError_t dequant_reconstruct_mode(const uint8_t* codes, const float* raw, con
       per_sm[dev].store(nb, std::memory_order_relaxed);                                                       \
     }                                                                                                         \
     const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)nsm * nb));           \
-    kern<<<grid, 128, 0, st>>>(codes, raw, scales, mins, axis, (int)H, (int)T, (int)R, (int)D, bvt, ranks, out); \
+    kern<<<grid, 128, 0, st>>>(codes, ncode, raw, scales, mins, axis, (int)H, (int)T, (int)R, (int)D, bvt, ranks, \
+                               out);                                                                          \
   }
     if (R <= 4) KVF_RR(4)
     else if (R <= 8) KVF_RR(8)

@@ -150,7 +150,7 @@ __device__ __forceinline__ bool producer_any(bool p) {
 // one producer thread's token rows of one item, fetched ahead (tc_depth)
 template <int MODE, int KC>
 struct RowsIn {
-  uint32_t q[kRowsPerProd][MODE == 0 ? 1 : KC];  // codes, one byte each
+  CodeWords<MODE == 0 ? 1 : code_words<MODE == 2, 4 * KC>()> cw[kRowsPerProd];  // codes, as loaded
   float raw[kRowsPerProd][MODE == 0 ? 4 * KC : 1];
   float sc[kRowsPerProd], mn[kRowsPerProd];
 };
@@ -159,7 +159,7 @@ struct RowsIn {
 template <int MODE, int KC>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_reconstruct_tc(const __grid_constant__ CUtensorMap omap, const uint8_t* __restrict__ codes,
-                     const float* __restrict__ raw, const float* __restrict__ scales,
+                     size_t ncode_bytes, const float* __restrict__ raw, const float* __restrict__ scales,
                      const float* __restrict__ mins, int axis, int H, int T, int R,
                      const float* __restrict__ bvt, const uint64_t* __restrict__ ranks,
                      unsigned* __restrict__ status) {
@@ -221,19 +221,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           in.sc[j] = __ldg(scales + g);
           in.mn[j] = __ldg(mins + g);
         }
+        if (MODE == 0) {
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-          const size_t fi = g * R + k;
-          if (MODE == 0) {
-            in.raw[j][k] = (ok && k < R) ? __ldg(raw + fi) : 0.0f;
-          } else {
-            if ((k & 3) == 0) in.q[j][k >> 2] = 0u;
-            if (ok && k < R) {
-              uint32_t q = codes[MODE == 2 ? (fi >> 1) : fi];
-              if (MODE == 2) q = (fi & 1) ? (q >> 4) & 0xFu : q & 0xFu;
-              in.q[j][k >> 2] |= q << (8 * (k & 3));
-            }
-          }
+          for (int k = 0; k < K; ++k) in.raw[j][k] = (ok && k < R) ? __ldg(raw + g * R + k) : 0.0f;
+        } else {
+          load_code_words<MODE == 2>(codes, ncode_bytes, g * R, ok, in.cw[j]);
         }
       }
     };
@@ -296,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (MODE == 0) {
                 d = in.raw[j][k];
               } else {
-                const float q = (float)((in.q[j][kc] >> (8 * e)) & 0xFFu);
+                const float q = (float)code_at<MODE == 2>(in.cw[j], k);
                 const float sc = (axis == KVF_PER_CHANNEL) ? pscale[k] : in.sc[j];
                 const float mn = (axis == KVF_PER_CHANNEL) ? pmin[k] : in.mn[j];
                 d = __fadd_rn(__fmul_rn(q, sc), mn);  // q * scale + min, separately rounded
@@ -466,8 +458,10 @@ cudaError_t launch_tc(const CUtensorMap& map, const uint8_t* codes, const float*
   }
   const size_t items = H * ((T + kTcRows - 1) / kTcRows);
   const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)nsm));
-  kern<<<grid, kTcThreads, smem, st>>>(map, codes, raw, scales, mins, axis, (int)H, (int)T, (int)R, bvt, ranks,
-                                       status);
+  const size_t n = H * T * R;
+  const size_t ncode = MODE == 2 ? (n + 1) / 2 : n;  // bytes of the code buffer
+  kern<<<grid, kTcThreads, smem, st>>>(map, codes, ncode, raw, scales, mins, axis, (int)H, (int)T, (int)R, bvt,
+                                       ranks, status);
   note_launches(1);
   return cudaGetLastError();
 }
@@ -479,7 +473,7 @@ cudaError_t launch_reconstruct_tc(const uint8_t* codes, const float* raw, const 
                                   const float* basis_vt, const uint64_t* ranks, float* out, unsigned* status,
                                   cudaStream_t st) {
   if (D != (size_t)kTcD || R == 0 || R > 64 || !aligned(out, 16) || H * T == 0 || T >= (1u << 31) ||
-      H >= (1u << 31))
+      H >= (1u << 31) || (codes && !aligned(codes, 4)))
     return cudaErrorNotSupported;
   CUtensorMap map{};
   if (!encode_out_map(&map, out, H, T)) return cudaErrorNotSupported;
