@@ -583,8 +583,10 @@ def gpu_arm(args):
         "config": _config(args, w),
         "ratio": tot["original_bytes"] / tot["compressed_bytes"],
         "rel_err": {"keys": (tot["err2_k"] / tot["ref2_k"]) ** 0.5, "values": (tot["err2_v"] / tot["ref2_v"]) ** 0.5},
-        "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak,
-                          "frac": alg / (step_ms / 1e3) / GB / peak, "peak_kind": peak_kind},
+        # the job's bytes over the job's peak: one GPU's measured peak times the GPU count
+        "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak * world,
+                          "peak_per_gpu": peak, "frac": alg / (step_ms / 1e3) / GB / (peak * world),
+                          "peak_kind": peak_kind},
         "roofline": roof,
         "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac",
                                                    "in_step")} for r in kr],
