@@ -613,6 +613,223 @@ def gpu_arm(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Streaming append workload
+# ---------------------------------------------------------------------------
+STREAM_METRIC = ("KV append compress+decompress GB/s (fp16 K+V bytes of the appended chunks per second), "
+                 "Balanced preset")
+
+
+def stream_arm(args):
+    """Llama-3-70B-shaped streaming cache, Balanced preset: 80 layers, each a
+    16384-token prefix of keys and values [8, T, 128] fp16 (compressed before
+    the timed region, which calibrates the layer's bases), then appends of 64
+    tokens to every layer. Each chunk is compressed as its own CompressedKV and
+    decompressed at once. A timed step is one append to every layer of this
+    rank, projected onto the prefix's bases (basis reuse); the reference's
+    semantics (a fresh eigen-basis per chunk, a synchronising host solve each)
+    are timed beside it on a few steps. Layers are spread over host threads,
+    each with its own stream: a 64-token chunk is launch-bound."""
+    import torch
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = local
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(f"cuda:{dev}"))
+    import kvforge_b200 as K
+    from kvforge_b200 import _lib as L
+    from kvforge_b200 import synth
+    from kvforge_b200.dist import gather_stats, layer_shard, reduce_stats
+
+    w = dict(synth.WORKLOADS[args.workload])
+    n_layers = args.layers or w.get("layers", 1)
+    mine = list(layer_shard(n_layers, world, rank))
+    lib, ctx = L.lib(), L.context(dev)
+    cfg = K.config_from_preset(w["preset"])
+    H, P, D, A = w["H"], w["T"], w["D"], w["append"]
+    in_code = L.IN_F16 if w["dtype"] == "float16" else L.IN_F32
+    n_chunks = max(1, min(w["appends"], args.warmup + args.steps))
+    fresh_steps = max(1, min(args.steps, 3))
+
+    # per layer: prefix compressed once (its bases kept), then a pool of chunks
+    # [n_chunks, H, A, D] drawn from the same generator as the prefix
+    layers = []
+    t_prefix = 0.0
+    for l in mine:
+        x = synth.workload_layer(args.workload, l, backend="torch", device=f"cuda:{dev}", T=P + A * n_chunks)
+        k, v = x
+        kp, vp = k[:, :P].contiguous(), v[:, :P].contiguous()
+        kc = k[:, P:].reshape(H, n_chunks, A, D).permute(1, 0, 2, 3).contiguous()
+        vc = v[:, P:].reshape(H, n_chunks, A, D).permute(1, 0, 2, 3).contiguous()
+        del x, k, v
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        h = C.c_void_p()
+        L.check(lib.kvf_compress_layer(ctx, C.c_void_p(kp.data_ptr()), C.c_void_p(vp.data_ptr()), in_code, H, P, D,
+                                       l, C.byref(cfg), None, None, C.byref(h), None))
+        kb, vb = C.c_void_p(), C.c_void_p()
+        L.check(lib.kvf_compressed_basis(h, 0, C.byref(kb)))
+        L.check(lib.kvf_compressed_basis(h, 1, C.byref(vb)))
+        L.check(lib.kvf_sync(ctx, None))
+        lib.kvf_compressed_free(h)
+        t_prefix += time.perf_counter() - t0
+        del kp, vp
+        layers.append((l, kc, vc, kb if kb.value else None, vb if vb.value else None))
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    nthr = max(1, min(args.streams, len(layers)))
+    tstreams = [torch.cuda.Stream(device=dev) for _ in range(nthr)]
+    touts = [(torch.empty((H, A, D), dtype=torch.float32, device=f"cuda:{dev}"),
+              torch.empty((H, A, D), dtype=torch.float32, device=f"cuda:{dev}")) for _ in range(nthr)]
+    errs = []
+
+    def worker(j, a, reuse, keep):
+        try:
+            sp = C.c_void_p(tstreams[j].cuda_stream)
+            ko, vo = touts[j]
+            for i in range(j, len(layers), nthr):
+                l, kc, vc, kb, vb = layers[i]
+                h = C.c_void_p()
+                L.check(lib.kvf_compress_layer(ctx, C.c_void_p(kc[a].data_ptr()), C.c_void_p(vc[a].data_ptr()),
+                                               in_code, H, A, D, l, C.byref(cfg), kb if reuse else None,
+                                               vb if reuse else None, C.byref(h), sp))
+                L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sp))
+                if keep is not None:
+                    keep(i, h, ko, vo, sp)
+                lib.kvf_compressed_free(h)
+        except Exception as ex:  # reported after the join
+            errs.append(ex)
+
+    def append_step(a, reuse, keep=None):
+        ts = [threading.Thread(target=worker, args=(j, a, reuse, keep)) for j in range(nthr)]
+        for t_ in ts:
+            t_.start()
+        for t_ in ts:
+            t_.join()
+        if errs:
+            raise errs[0]
+
+    def timed(reuse, steps, a0):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for s_ in tstreams:
+            s_.wait_event(e0)
+        for s in range(steps):
+            append_step((a0 + s) % n_chunks, reuse)
+        for s_ in tstreams:
+            ev = torch.cuda.Event()
+            ev.record(s_)
+            stream.wait_event(ev)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    # sizes and reconstruction error of one append (untimed), both modes
+    def measure(reuse):
+        acc = {"comp": 0, "err2_k": 0.0, "ref2_k": 0.0, "err2_v": 0.0, "ref2_v": 0.0}
+
+        def keep(i, h, ko, vo, sp):
+            L.check(lib.kvf_sync(ctx, sp))
+            n, b = C.c_size_t(), C.c_size_t()
+            L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
+            L.check(lib.kvf_compressed_basis_bytes(h, C.byref(b)))
+            acc["comp"] += n.value - (b.value if reuse else 0)
+            kf, vf = layers[i][1][0].float(), layers[i][2][0].float()
+            acc["err2_k"] += float(((ko - kf) ** 2).sum())
+            acc["ref2_k"] += float((kf ** 2).sum())
+            acc["err2_v"] += float(((vo - vf) ** 2).sum())
+            acc["ref2_v"] += float((vf ** 2).sum())
+
+        append_step(0, reuse, keep)
+        torch.cuda.synchronize()
+        return acc
+
+    meas = {r: measure(r) for r in (True, False)}
+    for s in range(args.warmup):
+        append_step(s % n_chunks, True)
+    L.check(lib.kvf_sync(ctx, None))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    n0 = lib.kvf_launch_count()
+    ms = timed(True, args.steps, args.warmup)
+    n1 = lib.kvf_launch_count()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    append_step(0, False)  # warm the fresh-basis path
+    ms_fresh = timed(False, fresh_steps, 0)
+    L.check(lib.kvf_sync(ctx, None))
+
+    in_bytes = len(layers) * 2 * H * A * D * (2 if w["dtype"] == "float16" else 4)
+    orig_bytes = len(layers) * 2 * H * A * D * 4
+    per = {}
+    for name, m, t_ms in (("reuse", meas[True], ms), ("fresh", meas[False], ms_fresh)):
+        st = {"layers": len(layers), "input_bytes": in_bytes, "compressed_bytes": m["comp"],
+              "original_bytes": orig_bytes, "ms": t_ms, **{k2: m[k2] for k2 in ("err2_k", "ref2_k", "err2_v",
+                                                                               "ref2_v")}}
+        per[name] = reduce_stats(gather_stats(st, device=f"cuda:{dev}" if world > 1 else None))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.build()
+        k32 = layers[0][1][0].float().cpu().numpy()
+        v32 = layers[0][2][0].float().cpu().numpy()
+        sec, _ = _oracle_time(O, k32, v32, None, w["preset"], 1, min(args.cpu_seconds, 10.0), 2000)
+        nb = 2 * H * A * D * 2
+        cpu = {"value": nb / sec / GB, "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": f"one {A}-token chunk [{H},{A},{D}] fp16 K+V, compress+decompress with a fresh basis "
+                         f"per chunk (the reference's semantics), 1 thread, {sec * 1e3:.2f} ms per chunk"}
+    for lay in layers:
+        for b in lay[3:]:
+            if b is not None:
+                lib.kvf_basis_free(b)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = _peaks()
+    r, f = per["reuse"], per["fresh"]
+    value = r["input_bytes"] / (r["ms"] / 1e3) / GB
+    alg = r["input_bytes"] + 2 * r["compressed_bytes"] + r["original_bytes"]
+    line = {
+        "metric": STREAM_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded low-rank + noise + outlier channels)",
+        "config": {"workload": args.workload, "preset": w["preset"], "layers": n_layers, "heads": H,
+                   "prefix_tokens": P, "append_tokens": A, "head_dim": D, "input_dtype": w["dtype"],
+                   "output_dtype": "f32", "basis": "the prefix's calibrated basis, reused by every chunk",
+                   "step": "one append to every layer", "chunk_pool": n_chunks,
+                   "l2": "chunks are L2-resident (256 KiB each); the step is launch-bound",
+                   "parallelism": f"layer-sharded x{world}", "host_threads_per_gpu": nthr},
+        "tokens_per_s": A * r["layers"] / (r["ms"] / 1e3),
+        "us_per_layer_append": 1e3 * r["ms"] / max(len(mine), 1),
+        "ratio_amortized": r["original_bytes"] / r["compressed_bytes"],
+        "rel_err": {"keys": (r["err2_k"] / r["ref2_k"]) ** 0.5, "values": (r["err2_v"] / r["ref2_v"]) ** 0.5},
+        "fresh_basis": {"ms_per_step": f["ms"], "value": f["input_bytes"] / (f["ms"] / 1e3) / GB,
+                        "ratio": f["original_bytes"] / f["compressed_bytes"],
+                        "rel_err": {"keys": (f["err2_k"] / f["ref2_k"]) ** 0.5,
+                                    "values": (f["err2_v"] / f["ref2_v"]) ** 0.5}, "steps": fresh_steps},
+        "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (r["ms"] / 1e3) / GB,
+                          "peak": peak * world, "frac": alg / (r["ms"] / 1e3) / GB / (peak * world),
+                          "peak_kind": peak_kind},
+        "prefix_ms_per_layer_untimed": 1e3 * t_prefix / max(len(layers), 1),
+        "gpu_launches": int(n1 - n0),
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -629,6 +846,9 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    from kvforge_b200 import synth
+    if "append" in synth.WORKLOADS.get(args.workload, {}):
+        return stream_arm(args)
     return gpu_arm(args)
 
 

@@ -292,6 +292,21 @@ kvf_status kvf_compressed_tensor_views(const kvf_compressed* c, int32_t which,
                                        const uint8_t** data, const float** scales,
                                        const float** mins, const uint32_t** freq,
                                        const float** basis_vt, const uint64_t** ranks);
+/* ---- streaming append with basis reuse (an extension: the reference has no
+ *      append API and compresses every chunk as its own KVCache, with a fresh
+ *      SVD per chunk, crates/kvforge-cpu/src/pipeline.rs:100-163) ----------
+ * kvf_compressed_basis: the projection state of one tensor (0 = keys,
+ * 1 = values) as a basis handle that shares it, no copy; *out is NULL when
+ * that tensor was not projected. Passed to kvf_compress_layer for the later
+ * chunks of the same layer, it projects them onto the prefix's basis; each
+ * chunk stays a complete CompressedKV in the reference's format.
+ * kvf_compressed_basis_bytes: the bytes of projection state
+ * (ProjectionState::size_bytes, types.rs:131-135) counted in
+ * kvf_compressed_size_bytes. A store that keeps one basis per layer charges a
+ * chunk compressed with it size - basis bytes. */
+kvf_status kvf_compressed_basis(const kvf_compressed* c, int32_t which, kvf_basis** out);
+kvf_status kvf_compressed_basis_bytes(const kvf_compressed* c, size_t* out);
+
 /* calibration scores of the keys (H floats, device), or NULL when calibration
  * was disabled or failed (the reference discards both, pipeline.rs:104-111) */
 const float* kvf_compressed_calibration(const kvf_compressed* c);

@@ -22,7 +22,7 @@ from . import _lib as L
 from ._lib import KvForgeError
 
 __all__ = [
-    "KVCache", "CompressedKV", "CompressionPipeline", "compress", "decompress", "KvForgeError",
+    "KVCache", "CompressedKV", "CompressionPipeline", "StreamingCompressor", "compress", "decompress", "KvForgeError",
     "Basis", "QuantParams", "EntropyState", "GpuQuantizer", "GpuProjector", "GpuSensitivityCalibrator",
     "GpuEntropyCodec", "config_from_preset", "parse_preset", "INT4", "INT8", "F32", "PER_CHANNEL", "PER_TOKEN",
 ]
@@ -234,6 +234,20 @@ class CompressedKV:
         }
         return out
 
+    def basis(self, which: int) -> Optional["Basis"]:
+        """The projection basis of one tensor (0 keys, 1 values) as a Basis that
+        shares it (no copy), or None when that tensor was not projected."""
+        h = C.c_void_p()
+        L.check(L.lib().kvf_compressed_basis(self._h, which, C.byref(h)))
+        return Basis(h, self._dev) if h.value else None
+
+    def basis_size_bytes(self) -> int:
+        """Bytes of projection state (ProjectionState::size_bytes,
+        crates/kvforge-core/src/types.rs:131-135) inside compressed_size_bytes()."""
+        n = C.c_size_t()
+        L.check(L.lib().kvf_compressed_basis_bytes(self._h, C.byref(n)))
+        return n.value
+
     def calibration_scores(self) -> Optional[np.ndarray]:
         """Per-head key sensitivity scores, or None (calibration off or T < 64)."""
         p = L.lib().kvf_compressed_calibration(self._h)
@@ -373,6 +387,60 @@ class CompressionPipeline:
         L.check(L.lib().kvf_decompress_layer(L.context(dev), compressed.handle, _ptr(ko), _ptr(vo), _stream(dev)))
         L.check(L.lib().kvf_sync(L.context(dev), _stream(dev)))
         return KVCache(ko, vo, compressed.layer_idx)
+
+
+class StreamingCompressor:
+    """Append-mode compression of a growing KV cache, one layer at a time.
+
+    The reference has no append API: every chunk is compressed as its own
+    KVCache, with a fresh SVD over the chunk's tokens for projection presets
+    (crates/kvforge-cpu/src/pipeline.rs:100-163). That is this class with
+    reuse_basis=False. With reuse_basis=True (the extension) prefill() keeps the
+    bases calibrated on each layer's prefix and append() projects every later
+    chunk of that layer onto them: no eigen-solve and no host synchronisation
+    per chunk, and the chunk is still a complete CompressedKV in the
+    reference's format (it carries the prefix's basis). A store that keeps one
+    basis per layer charges an appended chunk amortized_size_bytes(): its
+    compressed size without the basis bytes. Without projection both modes
+    are the same."""
+
+    def __init__(self, preset="balanced", reuse_basis: bool = True, device=None):
+        self._pipe = CompressionPipeline(device)
+        self._cfg = config_from_preset(preset)
+        self._reuse = bool(reuse_basis)
+        self._bases = {}
+
+    @property
+    def reuse_basis(self) -> bool:
+        return self._reuse
+
+    def prefill(self, kv: KVCache) -> CompressedKV:
+        """Compress a layer's prefix; with basis reuse, keep its bases for that layer."""
+        c = self._pipe.compress_with_config(kv, self._cfg)
+        if self._reuse and self._cfg.enable_projection:
+            self._bases[kv.layer_idx] = (c.basis(0), c.basis(1))
+        return c
+
+    def append(self, kv: KVCache) -> CompressedKV:
+        """Compress one appended chunk of a layer (any number of tokens >= 1)."""
+        kb = vb = None
+        if self._reuse and self._cfg.enable_projection:
+            if kv.layer_idx not in self._bases:
+                raise KvForgeError(L.ERR_INVALID_CONFIG, f"layer {kv.layer_idx}: append before prefill")
+            kb, vb = self._bases[kv.layer_idx]
+        return self._pipe.compress_with_config(kv, self._cfg, kb, vb)
+
+    def bases(self, layer_idx: int):
+        """(key Basis, value Basis) kept for a layer, or None."""
+        return self._bases.get(layer_idx)
+
+    def amortized_size_bytes(self, c: CompressedKV) -> int:
+        """Compressed size of an appended chunk when its bases are the layer's
+        shared ones (stored once, with the prefix); the full size otherwise."""
+        return c.compressed_size_bytes() - (c.basis_size_bytes() if self._reuse else 0)
+
+    def decompress(self, c: CompressedKV) -> KVCache:
+        return self._pipe.decompress(c)
 
 
 def compress(kv: KVCache, preset="balanced") -> CompressedKV:

@@ -48,8 +48,9 @@ EXPORTS = [
     "kvf_basis_info", "kvf_basis_download", "kvf_basis_device_vt", "kvf_basis_device_ranks", "kvf_basis_free",
     "kvf_compress_layer", "kvf_decompress_layer", "kvf_compress_layer_host", "kvf_decompress_layer_host",
     "kvf_compressed_shape", "kvf_compressed_size_bytes", "kvf_original_size_bytes", "kvf_compression_ratio",
-    "kvf_compressed_tensor_info", "kvf_compressed_tensor_views", "kvf_compressed_calibration",
-    "kvf_compressed_serialize", "kvf_compressed_deserialize", "kvf_compressed_free",
+    "kvf_compressed_tensor_info", "kvf_compressed_tensor_views", "kvf_compressed_basis",
+    "kvf_compressed_basis_bytes", "kvf_compressed_calibration", "kvf_compressed_serialize",
+    "kvf_compressed_deserialize", "kvf_compressed_free",
     "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read", "kvf_calibrate_noalloc",
 ]
 
@@ -126,6 +127,8 @@ def _declare(L):
         "kvf_compressed_tensor_info": (st, [p, i32, szp, szp, szp, C.POINTER(C.c_int32)]),
         "kvf_compressed_tensor_views": (st, [p, i32, C.POINTER(p), C.POINTER(p), C.POINTER(p), C.POINTER(p),
                                              C.POINTER(p), C.POINTER(p)]),
+        "kvf_compressed_basis": (st, [p, i32, C.POINTER(p)]),
+        "kvf_compressed_basis_bytes": (st, [p, szp]),
         "kvf_compressed_calibration": (p, [p]),
         "kvf_compressed_serialize": (st, [p, p, sz, szp]),
         "kvf_compressed_deserialize": (st, [p, p, sz, C.POINTER(p), p]),

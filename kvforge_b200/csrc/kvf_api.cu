@@ -1316,6 +1316,23 @@ kvf_status kvf_compressed_size_bytes(kvf_compressed* c, size_t* out) {
   return KVF_OK;
 }
 
+// ProjectionState::size_bytes (types.rs:131-135) of both tensors
+kvf_status kvf_compressed_basis_bytes(const kvf_compressed* c, size_t* out) {
+  if (!c || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  size_t total = 0;
+  for (const TensorC* t : {&c->key, &c->value})
+    if (t->basis) total += t->H * t->basis->R * t->D * 4 + t->H * 8;
+  *out = total;
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_basis(const kvf_compressed* c, int32_t which, kvf_basis** out) {
+  if (!c || !out || (which != 0 && which != 1)) return fail(KVF_ERR_INVALID_CONFIG, "bad arguments");
+  const TensorC& t = which == 0 ? c->key : c->value;
+  *out = t.basis ? new kvf_basis{t.basis} : nullptr;
+  return KVF_OK;
+}
+
 kvf_status kvf_original_size_bytes(const kvf_compressed* c, size_t* out) {
   if (!c || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
   *out = c->original_size_bytes;
