@@ -143,6 +143,67 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
     return res
 
 
+def decode_attention_leg(lib, L, torch, lay, dev, cfg, in_code, H, T, D, reps=20):
+    """Decode attention of one query row per head on compressed layer 0
+    (kvf_compressed_attention: rANS decode of both tensors into scratch, then
+    attention on the codes), against decompress + f32 attention in torch on
+    the reconstructed layer; error against fp64 attention on the exactly
+    reconstructed layer. CUDA events on the launching stream."""
+    l, k, v, kb, vb = lay
+    st = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(st.cuda_stream)
+    ctx = L.context(dev)
+    h = C.c_void_p()
+    L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), in_code, H, T, D, l,
+                                   C.byref(cfg), kb.handle if kb else None, vb.handle if vb else None, C.byref(h), sp))
+    q = torch.randn((H, D), generator=torch.Generator(device=f"cuda:{dev}").manual_seed(7), device=f"cuda:{dev}")
+    out = torch.empty((H, D), dtype=torch.float32, device=f"cuda:{dev}")
+    ko = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+    vo = torch.empty_like(ko)
+    scale = 1.0 / float(np.sqrt(D))
+
+    def fused():
+        L.check(lib.kvf_compressed_attention(ctx, h, C.c_void_p(q.data_ptr()), C.c_float(scale),
+                                             C.c_void_p(out.data_ptr()), sp))
+
+    def unfused():
+        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sp))
+        p = torch.softmax(torch.einsum("htd,hd->ht", ko, q) * scale, dim=1)
+        return torch.einsum("ht,htd->hd", p, vo)
+
+    res = {}
+    for name, f in (("fused_ms", fused), ("decompress_then_attention_ms", unfused)):
+        for _ in range(3):
+            f()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(reps):
+            f()
+        b.record(st)
+        torch.cuda.synchronize()
+        res[name] = a.elapsed_time(b) / reps
+    fused()
+    L.check(lib.kvf_set_exact_reconstruct(ctx, 1))
+    try:
+        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sp))
+    finally:
+        L.check(lib.kvf_set_exact_reconstruct(ctx, 0))
+    s = torch.einsum("htd,hd->ht", ko.double(), q.double()) * scale
+    ref = torch.einsum("ht,htd->hd", torch.softmax(s, dim=1), vo.double())
+    unf = unfused().double()
+    torch.cuda.synchronize()
+    res["rel_err_fused_vs_fp64"] = float((out.double() - ref).norm() / ref.norm())
+    res["rel_err_decompress_then_f32_attention_vs_fp64"] = float((unf - ref).norm() / ref.norm())
+    n = C.c_size_t()
+    L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
+    res["compressed_bytes_read"] = int(n.value)
+    res["f32_kv_bytes_avoided"] = int(2 * H * T * D * 4)
+    res["query_rows"] = H
+    lib.kvf_compressed_free(h)
+    L.check(lib.kvf_sync(ctx, sp))
+    return res
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 20 ms."""
 
@@ -540,6 +601,7 @@ def gpu_arm(args):
     e2e_tot = reduce_stats(e2e_per)
 
     kr = kernel_rooflines(lib, L, K, torch, layers[0], dev, cfg) if rank == 0 else []
+    attn = decode_attention_leg(lib, L, torch, layers[0], dev, cfg, in_code, H, T, D) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -595,6 +657,7 @@ def gpu_arm(args):
         "decompress_only": {"ms_per_step": tot["decompress_ms"],
                             "gbs": tot["input_bytes"] / (tot["decompress_ms"] / 1e3) / GB,
                             "output_gbs": tot["original_bytes"] / (tot["decompress_ms"] / 1e3) / GB},
+        "decode_attention_layer0": attn,
         "stages_ms_per_step_overlapped": {k: v[0] / prof_steps for k, v in prof.items() if v[1]},
         "basis_ms_per_layer_untimed": 1e3 * t_basis / max(len(layers), 1),
         "gpu_launches": int(n1 - n0),

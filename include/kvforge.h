@@ -228,6 +228,32 @@ kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t 
                                       const float* mins, int32_t data_type, int32_t axis,
                                       size_t H, size_t T, size_t D, float* out, void* stream);
 
+/* ---- fused dequantize + decode attention (KernelLauncher::
+ *      fused_dequant_attention, crates/kvforge-cuda/src/kernel_launcher.rs:43-57;
+ *      the kernel is an empty stub in the reference,
+ *      crates/kvforge-cuda/kernels/fused_dequant_attention.cu:1-53) --------
+ * One query row per head: out[h, :] = softmax(scale * K_h q_h) V_h with K and V
+ * the dequantized (and, with a basis, reconstructed) cache, computed on the
+ * codes without rebuilding K or V. query [H, D] f32, out [H, D] f32, device.
+ * Keys are per-channel codes [H, T, k_cols] with [H, k_cols] scales/mins,
+ * values per-token codes [H, T, v_cols] with [H, T] scales/mins (the
+ * pipeline's layout); k_data_type / v_data_type INT4 or INT8 (packed as the
+ * quantizer packs them). Without a basis the width is head_dim; with one it is
+ * the basis's R (basis [H, R, D] and ranks [H], rows from rank on ignored).
+ * T = 0 writes zeros. Relative error against an fp64 evaluation of the same
+ * formula is at f32 rounding level (the tests bound it by 1e-4). */
+kvf_status kvf_fused_dequant_attention(kvf_ctx* ctx, const uint8_t* k_codes, const uint8_t* v_codes,
+                                       const float* query, const float* k_scales, const float* k_mins,
+                                       const float* v_scales, const float* v_mins, int32_t k_data_type,
+                                       int32_t v_data_type, size_t H, size_t T, size_t D, size_t k_cols,
+                                       size_t v_cols, const float* k_basis_vt, const uint64_t* k_ranks,
+                                       const float* v_basis_vt, const uint64_t* v_ranks, float scale,
+                                       float* out, void* stream);
+/* the same on a compressed layer (entropy-coded codes are decoded into
+ * scratch first); stream-ordered, no host synchronisation */
+kvf_status kvf_compressed_attention(kvf_ctx* ctx, const kvf_compressed* c, const float* query, float scale,
+                                    float* out, void* stream);
+
 /* ---- projection basis (the calibrated basis) ----------------------------
  * The reference takes a full SVD of each head inside project
  * (projection.rs:81-90). Here the basis step is separate: a Gram matrix

@@ -234,6 +234,21 @@ class CompressedKV:
         }
         return out
 
+    def attention(self, query, scale: Optional[float] = None) -> torch.Tensor:
+        """Decode attention of one query row per head on the compressed layer:
+        softmax(scale * K_h q_h) V_h for every head h, computed on the codes
+        (KernelLauncher::fused_dequant_attention, kernel_launcher.rs:43-57).
+        query [H, D] or [H, 1, D]; scale defaults to 1/sqrt(D). -> f32 [H, D] on
+        the device, stream-ordered on the current stream."""
+        H, T, D = self.shape
+        q = _as_device(query, self._dev).to(torch.float32).reshape(H, D).contiguous()
+        out = torch.empty((H, D), dtype=torch.float32, device=f"cuda:{self._dev}")
+        sc = float(scale) if scale is not None else 1.0 / float(np.sqrt(D))
+        L.check(L.lib().kvf_compressed_attention(L.context(self._dev), self._h, _ptr(q), sc, _ptr(out),
+                                                 _stream(self._dev)))
+        out._query = q  # keep the query alive until the stream has consumed it
+        return out
+
     def basis(self, which: int) -> Optional["Basis"]:
         """The projection basis of one tensor (0 keys, 1 values) as a Basis that
         shares it (no copy), or None when that tensor was not projected."""

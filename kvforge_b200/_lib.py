@@ -44,7 +44,8 @@ EXPORTS = [
     "kvf_set_reconstruct_engine", "kvf_selftest_wait_timeout", "kvf_sync",
     "kvf_pipeline_config_from_preset", "kvf_calibrate", "kvf_quantize", "kvf_dequantize", "kvf_project",
     "kvf_reconstruct", "kvf_fused_project_quantize", "kvf_rans_max_encoded_len", "kvf_rans_encode",
-    "kvf_rans_decode", "kvf_entropy_decode_dequant", "kvf_basis_compute", "kvf_basis_from_host",
+    "kvf_rans_decode", "kvf_entropy_decode_dequant", "kvf_fused_dequant_attention", "kvf_compressed_attention",
+    "kvf_basis_compute", "kvf_basis_from_host",
     "kvf_basis_info", "kvf_basis_download", "kvf_basis_device_vt", "kvf_basis_device_ranks", "kvf_basis_free",
     "kvf_compress_layer", "kvf_decompress_layer", "kvf_compress_layer_host", "kvf_decompress_layer_host",
     "kvf_compressed_shape", "kvf_compressed_size_bytes", "kvf_original_size_bytes", "kvf_compression_ratio",
@@ -108,6 +109,9 @@ def _declare(L):
         "kvf_rans_encode": (st, [p, p, sz, p, sz, szp, p, p]),
         "kvf_rans_decode": (st, [p, p, sz, p, sz, p, p]),
         "kvf_entropy_decode_dequant": (st, [p, p, sz, p, p, p, i32, i32, sz, sz, sz, p, p]),
+        "kvf_fused_dequant_attention": (st, [p, p, p, p, p, p, p, p, i32, i32, sz, sz, sz, sz, sz, p, p, p, p,
+                                             C.c_float, p, p]),
+        "kvf_compressed_attention": (st, [p, p, p, C.c_float, p, p]),
         "kvf_basis_compute": (st, [p, p, i32, sz, sz, sz, f64, sz, C.POINTER(p), p]),
         "kvf_basis_from_host": (st, [p, sz, sz, sz, p, p, C.POINTER(p)]),
         "kvf_basis_info": (st, [p, szp, szp, szp]),

@@ -1119,6 +1119,98 @@ kvf_status kvf_entropy_decode_dequant(kvf_ctx* ctx, const uint8_t* comp, size_t 
   return KVF_OK;
 }
 
+// ---- fused dequantize + decode attention ------------------------------------
+namespace {
+kvf_status check_attention(size_t H, size_t T, size_t D, size_t Rk, size_t Rv, int kdt, int vdt, bool kproj,
+                           bool vproj) {
+  KVF_TRY(check_shape(H, T, D));
+  if ((kdt != KVF_INT4 && kdt != KVF_INT8) || (vdt != KVF_INT4 && vdt != KVF_INT8))
+    return fail(KVF_ERR_INVALID_CONFIG, "attention takes INT4 or INT8 codes");
+  if (D == 0 || Rk == 0 || Rv == 0) return fail(KVF_ERR_SHAPE_MISMATCH, "empty head or coefficient width");
+  if ((!kproj && Rk != D) || (!vproj && Rv != D) || Rk > D || Rv > D)
+    return fail(KVF_ERR_SHAPE_MISMATCH, "coefficient width must be head_dim without a basis, at most head_dim with one");
+  if ((attention_tiles(T) + Rv) * sizeof(float) > 200 * 1024)
+    return fail(KVF_ERR_SHAPE_MISMATCH, "sequence too long for one attention call");
+  return KVF_OK;
+}
+}  // namespace
+
+kvf_status kvf_fused_dequant_attention(kvf_ctx* ctx, const uint8_t* k_codes, const uint8_t* v_codes,
+                                       const float* query, const float* k_scales, const float* k_mins,
+                                       const float* v_scales, const float* v_mins, int32_t k_data_type,
+                                       int32_t v_data_type, size_t H, size_t T, size_t D, size_t k_cols,
+                                       size_t v_cols, const float* k_basis_vt, const uint64_t* k_ranks,
+                                       const float* v_basis_vt, const uint64_t* v_ranks, float scale, float* out,
+                                       void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (H && D && (!query || !out)) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  if ((k_basis_vt && !k_ranks) || (v_basis_vt && !v_ranks)) return fail(KVF_ERR_INVALID_CONFIG, "basis without ranks");
+  if (H == 0) return KVF_OK;
+  KVF_TRY(check_attention(H, T, D, k_cols, v_cols, k_data_type, v_data_type, k_basis_vt != nullptr,
+                          v_basis_vt != nullptr));
+  if (T && (!k_codes || !v_codes || !k_scales || !k_mins || !v_scales || !v_mins))
+    return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  Scratch sc(st, ctx->pool);
+  float* part = sc.get<float>(attention_scratch_floats(H, T, v_cols));
+  if (!part) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  KVF_CUDA(launch_attention(k_codes, k_data_type, v_codes, v_data_type, query, k_scales, k_mins, v_scales, v_mins,
+                            k_basis_vt, k_ranks, v_basis_vt, v_ranks, H, T, D, k_cols, v_cols, scale, part, out, st));
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_attention(kvf_ctx* ctx, const kvf_compressed* c, const float* query, float scale,
+                                    float* out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
+  const TensorC& k = c->key;
+  const TensorC& v = c->value;
+  if (k.axis != KVF_PER_CHANNEL || v.axis != KVF_PER_TOKEN)
+    return fail(KVF_ERR_INVALID_CONFIG, "attention takes per-channel keys and per-token values");
+  if (c->H && c->D && (!query || !out)) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  if (c->H == 0) return KVF_OK;
+  KVF_TRY(check_attention(c->H, c->T, c->D, k.qcols, v.qcols, k.data_type, v.data_type, k.basis != nullptr,
+                          v.basis != nullptr));
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  Scratch sc(st, ctx->pool);
+  // entropy-coded tensors are decoded into scratch (allocated on `st` before
+  // the fork, freed on `st` after the join): keys on `st`, values on the
+  // context's side stream, so the two decodes overlap
+  const uint8_t* codes[2] = {k.d_data, v.d_data};
+  const TensorC* ts[2] = {&k, &v};
+  uint8_t* dec[2] = {nullptr, nullptr};
+  for (int i = 0; i < 2; ++i)
+    if (ts[i]->has_freq && !(dec[i] = sc.get<uint8_t>(ts[i]->packed_len)))
+      return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  float* part = sc.get<float>(attention_scratch_floats(c->H, c->T, v.qcols));
+  if (!part) return fail(KVF_ERR_CUDA, "scratch allocation failed");
+  if (dec[0] || dec[1]) {
+    kvf_ctx::Side* sd = nullptr;
+    KVF_CUDA(ctx->side_for(st, &sd));
+    KVF_CUDA(cudaEventRecord(sd->fork, st));
+    KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+      const TensorC& t = *ts[i];
+      if (!dec[i]) continue;
+      e = launch_rans_decode(t.d_data, t.data_len, t.len_known ? nullptr : t.d_len, t.d_freq, t.packed_len, dec[i],
+                             ctx->d_status, i == 0 ? st : sd->s);
+      codes[i] = dec[i];
+    }
+    cudaError_t je = cudaEventRecord(sd->join, sd->s);
+    if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
+    KVF_CUDA(e);
+    KVF_CUDA(je);
+  }
+  KVF_CUDA(launch_attention(codes[0], k.data_type, codes[1], v.data_type, query, k.d_scales, k.d_mins, v.d_scales,
+                            v.d_mins, k.basis ? k.basis->d_vt : nullptr, k.basis ? k.basis->d_ranks : nullptr,
+                            v.basis ? v.basis->d_vt : nullptr, v.basis ? v.basis->d_ranks : nullptr, c->H, c->T,
+                            c->D, k.qcols, v.qcols, scale, part, out, st));
+  return KVF_OK;
+}
+
 // ---- basis ------------------------------------------------------------------
 kvf_status kvf_basis_compute(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
                              double variance_threshold, size_t max_rank, kvf_basis** out, void* stream) {

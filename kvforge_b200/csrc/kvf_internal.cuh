@@ -309,4 +309,16 @@ cudaError_t launch_selftest_mbar(unsigned* status, unsigned long long limit_ns, 
 cudaError_t launch_selftest_lookback(unsigned long long* lb, unsigned* status, unsigned long long limit_ns,
                                      cudaStream_t st);
 
+// ---- fused dequantize + decode attention (kvf_attn.cu) ----------------------
+// keys per channel [H, T, Rk] codes with [H, Rk] params, values per token
+// [H, T, Rv] codes with [H, T] params; kvt / vvt [H, R, D] bases or NULL
+// (then R = D); part: attention_scratch_floats(H, T, Rv) floats; out [H, D]
+size_t attention_tiles(size_t T);
+size_t attention_scratch_floats(size_t H, size_t T, size_t Rv);
+cudaError_t launch_attention(const uint8_t* kc, int kdt, const uint8_t* vc, int vdt, const float* q,
+                             const float* ks, const float* km, const float* vs, const float* vm, const float* kvt,
+                             const uint64_t* kranks, const float* vvt, const uint64_t* vranks, size_t H, size_t T,
+                             size_t D, size_t Rk, size_t Rv, float scale, float* part, float* out,
+                             cudaStream_t st);
+
 }  // namespace kvf

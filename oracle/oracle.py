@@ -306,6 +306,25 @@ def decompress(ckv, threads=1):
     return decompress_tensor(ckv["key"], threads), decompress_tensor(ckv["value"], threads)
 
 
+def decode_attention(keys, values, query, scale):
+    """Single-query attention per head, fp64: out[h] = softmax(scale * K_h q_h) V_h,
+    on the dequantized (and reconstructed) K and V -- the computation the
+    reference's fused_dequant_attention kernel describes and leaves unimplemented
+    (crates/kvforge-cuda/kernels/fused_dequant_attention.cu:1-10, steps at :30-34).
+    keys, values [H, T, D]; query [H, D] -> [H, D] float64 (zeros when T = 0)."""
+    k = np.asarray(keys, np.float64)
+    v = np.asarray(values, np.float64)
+    q = np.asarray(query, np.float64)
+    H, T, D = k.shape
+    if T == 0:
+        return np.zeros((H, D))
+    s = scale * np.einsum("htd,hd->ht", k, q)
+    s -= s.max(axis=1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=1, keepdims=True)
+    return np.einsum("ht,htd->hd", p, v)
+
+
 def compressed_size_bytes(ckv) -> int:
     return tensor_size_bytes(ckv["key"]) + tensor_size_bytes(ckv["value"])
 
