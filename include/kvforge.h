@@ -338,8 +338,13 @@ kvf_status kvf_compressed_basis_bytes(const kvf_compressed* c, size_t* out);
 const float* kvf_compressed_calibration(const kvf_compressed* c);
 
 /* serialisation to host bytes and back (CompressedKV.to_bytes/from_bytes,
- * crates/kvforge-python/src/py_types.rs:98-110); format in the library's
- * documentation. kvf_compressed_serialize with buf == NULL returns the size. */
+ * crates/kvforge-python/src/py_types.rs:98-110) in the reference's wire
+ * format: bincode 1.x of CompressedKV (crates/kvforge-core/src/types.rs:36-148),
+ * field for field. quantized_data carries this library's rANS container when
+ * entropy coding is on (a reference-written entropy payload deserialises but
+ * does not decode: kvf_decompress_layer reports KVF_ERR_CORRUPT_STREAM).
+ * Calibration scores are not part of the format. kvf_compressed_serialize
+ * with buf == NULL returns the size. */
 kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf_host, size_t cap,
                                     size_t* len);
 kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf_host, size_t len,

@@ -635,94 +635,158 @@ struct Reader {
   T v() { T x{}; get(&x, sizeof(T)); return x; }
 };
 
-constexpr uint32_t kSerMagic = 0x4346564Bu;  // "KVFC"
-constexpr uint32_t kSerVersion = 1;
+// The wire format is the reference's: CompressedKV.to_bytes is
+// bincode::serialize (crates/kvforge-python/src/py_types.rs:98-110, bincode
+// 1.x, Cargo.toml:28) of the structs in crates/kvforge-core/src/types.rs:36-148.
+// bincode 1.x with its default options writes little-endian fixed-width
+// integers, usize as u64, a Vec as a u64 length then its elements, an Option
+// as a u8 tag (0 None, 1 Some) then the value, a unit enum variant as its u32
+// declaration index, and struct fields in declaration order:
+//   CompressedKV     { layer_idx, original_shape: Shape {num_heads, seq_len, head_dim},
+//                      key_data, value_data: CompressedTensor, original_size_bytes }
+//   CompressedTensor { quantized_data: Vec<u8>, quant_params: QuantParams,
+//                      projection_state: Option<ProjectionState>, entropy_state: Option<EntropyState> }
+//   QuantParams      { scales: Vec<f32>, mins: Vec<f32>, data_type: DataType {INT4, INT8, F32},
+//                      axis: QuantAxis {PerChannel, PerToken}, shape: Vec<usize> = [H, T, cols] }
+//   ProjectionState  { basis_vt: Vec<f32>, ranks: Vec<usize>, num_heads, head_dim,
+//                      projected_shape: Vec<usize> = [H, T, R] }
+//   EntropyState     { frequencies: Vec<u32> (256, or empty for empty input), original_len }
+// quantized_data holds this library's rANS container when entropy coding is on.
 
 kvf_status ser_tensor(TensorC& t, Writer& w, cudaStream_t st) {
   KVF_TRY(resolve_len(t, st));
-  w.v<int32_t>(t.data_type);
-  w.v<int32_t>(t.axis);
-  w.v<int32_t>(t.basis ? 1 : 0);
-  w.v<int32_t>(t.entropy ? 1 : 0);
-  w.v<int32_t>(t.has_freq ? 1 : 0);
-  w.v<uint64_t>(t.qcols);
-  w.v<uint64_t>(t.packed_len);
-  w.v<uint64_t>(t.data_len);
-  w.v<uint64_t>(t.num_params);
   std::vector<uint8_t> host;
   auto dl = [&](const void* d, size_t n) -> kvf_status {
     host.resize(n);
-    if (n) {
+    if (n && w.buf) {  // the size pass copies nothing
       KVF_CUDA(cudaMemcpyAsync(host.data(), d, n, cudaMemcpyDeviceToHost, st));
       KVF_CUDA(cudaStreamSynchronize(st));
     }
     w.put(host.data(), n);
     return KVF_OK;
   };
-  if (t.basis) {
-    w.put(t.basis->ranks.data(), t.H * sizeof(uint64_t));
-    w.put(t.basis->vt.data(), t.basis->vt.size() * sizeof(float));
-  }
-  KVF_TRY(dl(t.d_scales, t.num_params * 4));
-  KVF_TRY(dl(t.d_mins, t.num_params * 4));
-  if (t.has_freq) KVF_TRY(dl(t.d_freq, 256 * 4));
+  w.v<uint64_t>(t.data_len);  // quantized_data
   KVF_TRY(dl(t.d_data, t.data_len));
+  w.v<uint64_t>(t.num_params);  // quant_params.scales
+  KVF_TRY(dl(t.d_scales, t.num_params * 4));
+  w.v<uint64_t>(t.num_params);  // quant_params.mins
+  KVF_TRY(dl(t.d_mins, t.num_params * 4));
+  w.v<uint32_t>((uint32_t)t.data_type);
+  w.v<uint32_t>((uint32_t)t.axis);
+  w.v<uint64_t>(3);
+  w.v<uint64_t>(t.H);
+  w.v<uint64_t>(t.T);
+  w.v<uint64_t>(t.qcols);
+  if (t.basis) {
+    w.v<uint8_t>(1);
+    w.v<uint64_t>(t.basis->vt.size());
+    w.put(t.basis->vt.data(), t.basis->vt.size() * sizeof(float));
+    w.v<uint64_t>(t.H);
+    w.put(t.basis->ranks.data(), t.H * sizeof(uint64_t));
+    w.v<uint64_t>(t.H);
+    w.v<uint64_t>(t.D);
+    w.v<uint64_t>(3);
+    w.v<uint64_t>(t.H);
+    w.v<uint64_t>(t.T);
+    w.v<uint64_t>(t.qcols);
+  } else {
+    w.v<uint8_t>(0);
+  }
+  if (t.entropy) {
+    w.v<uint8_t>(1);
+    w.v<uint64_t>(t.has_freq ? 256 : 0);
+    if (t.has_freq) KVF_TRY(dl(t.d_freq, 256 * 4));
+    w.v<uint64_t>(t.packed_len);
+  } else {
+    w.v<uint8_t>(0);
+  }
   return KVF_OK;
 }
 
 kvf_status deser_tensor(kvf_compressed* c, TensorC& t, Reader& r, cudaStream_t st) {
+  const auto bad = [](const char* what) { return fail(KVF_ERR_SERIALIZATION, what); };
   t.H = c->H; t.T = c->T; t.D = c->D;
-  t.data_type = r.v<int32_t>();
-  t.axis = r.v<int32_t>();
-  const bool proj = r.v<int32_t>() != 0;
-  t.entropy = r.v<int32_t>() != 0;
-  t.has_freq = r.v<int32_t>() != 0;
-  t.qcols = r.v<uint64_t>();
-  t.packed_len = r.v<uint64_t>();
   t.data_len = r.v<uint64_t>();
-  t.num_params = r.v<uint64_t>();
-  if (!r.ok) return fail(KVF_ERR_SERIALIZATION, "truncated tensor header");
+  if (!r.ok || t.data_len > r.len - r.pos) return bad("truncated quantized data");
+  const size_t data_pos = r.pos;
+  r.pos += t.data_len;
+  const uint64_t ns = r.v<uint64_t>();
+  if (!r.ok || ns > (r.len - r.pos) / 4) return bad("truncated scales");
+  const size_t scales_pos = r.pos;
+  r.pos += ns * 4;
+  const uint64_t nm = r.v<uint64_t>();
+  if (!r.ok || nm != ns || nm > (r.len - r.pos) / 4) return bad("truncated mins");
+  const size_t mins_pos = r.pos;
+  r.pos += nm * 4;
+  const uint32_t dt = r.v<uint32_t>(), ax = r.v<uint32_t>();
+  if (!r.ok || dt > 2 || ax > 1) return bad("unknown data type or axis variant");
+  t.data_type = (int)dt;
+  t.axis = (int)ax;
   KVF_TRY(check_qcfg(t.data_type, t.axis));
-  const size_t n = t.H * t.T * t.qcols;
-  if (t.packed_len != packed_len(n, t.data_type) || t.num_params != num_params(t.H, t.T, t.qcols, t.axis) ||
-      (!t.has_freq && t.data_len != t.packed_len) || (t.has_freq && !t.entropy) || (!proj && t.qcols != t.D))
-    return fail(KVF_ERR_SERIALIZATION, "inconsistent tensor header");
-  if (proj) {
+  if (r.v<uint64_t>() != 3) return bad("quant_params.shape must have 3 entries");
+  const uint64_t qh = r.v<uint64_t>(), qt = r.v<uint64_t>(), qc = r.v<uint64_t>();
+  if (!r.ok || qh != t.H || qt != t.T) return bad("quant_params.shape does not match the layer");
+  t.qcols = qc;
+  const uint8_t ptag = r.v<uint8_t>();
+  if (!r.ok || ptag > 1) return bad("bad projection_state tag");
+  if (ptag == 1) {
+    if (qc == 0 || qc > t.D) return bad("projected width must be in 1..head_dim");
     auto b = std::make_shared<BasisData>();
     b->device = c->device;
-    b->H = t.H; b->R = t.qcols; b->D = t.D;
+    b->H = t.H; b->R = qc; b->D = t.D;
+    if (r.v<uint64_t>() != t.H * qc * t.D) return bad("basis_vt length does not match [H, R, D]");
+    b->vt.resize(t.H * qc * t.D);
+    if (!r.get(b->vt.data(), b->vt.size() * 4)) return bad("truncated basis_vt");
+    if (r.v<uint64_t>() != t.H) return bad("ranks length does not match num_heads");
     b->ranks.resize(t.H);
-    b->vt.resize(t.H * t.qcols * t.D);
-    if (!r.get(b->ranks.data(), t.H * 8) || !r.get(b->vt.data(), b->vt.size() * 4))
-      return fail(KVF_ERR_SERIALIZATION, "truncated projection state");
+    if (!r.get(b->ranks.data(), t.H * 8)) return bad("truncated ranks");
+    if (r.v<uint64_t>() != t.H || r.v<uint64_t>() != t.D) return bad("projection num_heads / head_dim mismatch");
+    if (r.v<uint64_t>() != 3 || r.v<uint64_t>() != t.H || r.v<uint64_t>() != t.T || r.v<uint64_t>() != qc)
+      return bad("projected_shape does not match [H, T, R]");
+    if (!r.ok) return bad("truncated projection state");
     for (uint64_t rk : b->ranks)
-      if (rk > t.qcols) return fail(KVF_ERR_SERIALIZATION, "rank exceeds the projected width");
+      if (rk > qc) return bad("rank exceeds the projected width");
     KVF_TRY(upload_basis(*b));
     t.basis = b;
+  } else if (qc != t.D) {
+    return bad("unprojected width must be head_dim");
   }
-  auto up = [&](void* d, size_t nbytes) -> kvf_status {
-    if (r.pos + nbytes > r.len) return fail(KVF_ERR_SERIALIZATION, "truncated payload");
-    if (nbytes) KVF_CUDA(cudaMemcpyAsync(d, r.buf + r.pos, nbytes, cudaMemcpyHostToDevice, st));
-    r.pos += nbytes;
+  const size_t n = t.H * t.T * t.qcols;
+  t.packed_len = packed_len(n, t.data_type);
+  t.num_params = num_params(t.H, t.T, t.qcols, t.axis);
+  if (ns != t.num_params) return bad("parameter count does not match the shape");
+  const uint8_t etag = r.v<uint8_t>();
+  if (!r.ok || etag > 1) return bad("bad entropy_state tag");
+  t.entropy = etag == 1;
+  size_t freq_pos = 0;
+  if (t.entropy) {
+    const uint64_t nf = r.v<uint64_t>();
+    if (!r.ok || (nf != 0 && nf != 256) || nf * 4 > r.len - r.pos) return bad("frequencies must have 0 or 256 entries");
+    t.has_freq = nf == 256;
+    freq_pos = r.pos;
+    r.pos += nf * 4;
+    if (r.v<uint64_t>() != t.packed_len || !r.ok) return bad("entropy original_len does not match the codes");
+  }
+  if (!t.has_freq && t.data_len != t.packed_len) return bad("quantized data length does not match the shape");
+  if (t.has_freq && t.data_len % 4 != 0) return fail(KVF_ERR_ENTROPY, "Compressed data length not aligned to 4 bytes");
+  auto up = [&](void* d, size_t pos, size_t nbytes) -> kvf_status {
+    if (nbytes) KVF_CUDA(cudaMemcpyAsync(d, r.buf + pos, nbytes, cudaMemcpyHostToDevice, st));
     return KVF_OK;
   };
   t.d_scales = c->alloc<float>(t.num_params);
   t.d_mins = c->alloc<float>(t.num_params);
-  if (!t.d_scales || !t.d_mins) return fail(KVF_ERR_CUDA, "allocation failed");
-  KVF_TRY(up(t.d_scales, t.num_params * 4));
-  KVF_TRY(up(t.d_mins, t.num_params * 4));
+  t.data_cap = t.data_len;
+  t.d_data = c->alloc<uint8_t>(t.data_len);
+  if (!t.d_scales || !t.d_mins || !t.d_data) return fail(KVF_ERR_CUDA, "allocation failed");
+  KVF_TRY(up(t.d_data, data_pos, t.data_len));
+  KVF_TRY(up(t.d_scales, scales_pos, t.num_params * 4));
+  KVF_TRY(up(t.d_mins, mins_pos, t.num_params * 4));
   if (t.has_freq) {
     t.d_freq = c->alloc<uint32_t>(256);
     if (!t.d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
-    KVF_TRY(up(t.d_freq, 256 * 4));
+    KVF_TRY(up(t.d_freq, freq_pos, 256 * 4));
   }
-  t.data_cap = t.data_len;
-  t.d_data = c->alloc<uint8_t>(t.data_len);
-  if (!t.d_data) return fail(KVF_ERR_CUDA, "allocation failed");
-  KVF_TRY(up(t.d_data, t.data_len));
   t.len_known = true;
-  if (t.has_freq && t.data_len % 4 != 0)
-    return fail(KVF_ERR_ENTROPY, "Compressed data length not aligned to 4 bytes");
   return KVF_OK;
 }
 
@@ -1468,19 +1532,32 @@ kvf_status kvf_compressed_tensor_views(const kvf_compressed* c, int32_t which, c
 
 const float* kvf_compressed_calibration(const kvf_compressed* c) { return c ? c->d_scores : nullptr; }
 
-kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf, size_t cap, size_t* len) {
-  if (!c || !len) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
-  DeviceGuard g(c->device);
-  Writer w{buf, buf ? cap : 0};
-  w.v<uint32_t>(kSerMagic);
-  w.v<uint32_t>(kSerVersion);
+namespace {
+kvf_status ser_layer(kvf_compressed* c, Writer& w) {
   w.v<uint64_t>(c->layer_idx);
   w.v<uint64_t>(c->H);
   w.v<uint64_t>(c->T);
   w.v<uint64_t>(c->D);
-  w.v<uint64_t>(c->original_size_bytes);
   KVF_TRY(ser_tensor(c->key, w, c->stream));
   KVF_TRY(ser_tensor(c->value, w, c->stream));
+  w.v<uint64_t>(c->original_size_bytes);
+  return KVF_OK;
+}
+}  // namespace
+
+kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf, size_t cap, size_t* len) {
+  if (!c || !len) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  DeviceGuard g(c->device);
+  Writer w{buf, buf ? cap : 0};
+  if (buf) {  // size first, so nothing is copied into a buffer that is too small
+    Writer sz{nullptr, 0};
+    KVF_TRY(ser_layer(c, sz));
+    if (sz.len > cap) {
+      *len = sz.len;
+      return fail(KVF_ERR_SERIALIZATION, "buffer too small");
+    }
+  }
+  KVF_TRY(ser_layer(c, w));
   *len = w.len;
   if (buf && w.len > cap) return fail(KVF_ERR_SERIALIZATION, "buffer too small");
   return KVF_OK;
@@ -1492,8 +1569,6 @@ kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf, size_t l
   if (!buf || !out) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
   DeviceGuard g(ctx->device);
   Reader r{buf, len};
-  if (r.v<uint32_t>() != kSerMagic || r.v<uint32_t>() != kSerVersion)
-    return fail(KVF_ERR_SERIALIZATION, "not a serialised compressed layer");
   std::unique_ptr<kvf_compressed> c(new kvf_compressed());
   c->ctx = ctx;
   c->device = ctx->device;
@@ -1502,11 +1577,14 @@ kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf, size_t l
   c->H = r.v<uint64_t>();
   c->T = r.v<uint64_t>();
   c->D = r.v<uint64_t>();
-  c->original_size_bytes = r.v<uint64_t>();
   if (!r.ok) return fail(KVF_ERR_SERIALIZATION, "truncated header");
   if (check_shape(c->H, c->T, c->D) != KVF_OK) return fail(KVF_ERR_SERIALIZATION, "bad shape");
   kvf_status s = deser_tensor(c.get(), c->key, r, c->stream);
   if (s == KVF_OK) s = deser_tensor(c.get(), c->value, r, c->stream);
+  if (s == KVF_OK) {
+    c->original_size_bytes = r.v<uint64_t>();
+    if (!r.ok) s = fail(KVF_ERR_SERIALIZATION, "truncated original_size_bytes");
+  }
   if (s == KVF_OK && r.pos != r.len) s = fail(KVF_ERR_SERIALIZATION, "trailing bytes");
   if (s == KVF_OK) {
     cudaError_t e = cudaStreamSynchronize(c->stream);

@@ -325,6 +325,109 @@ def decode_attention(keys, values, query, scale):
     return np.einsum("ht,htd->hd", p, v)
 
 
+# ---------------------------------------------------------------------------
+# Wire format: CompressedKV.to_bytes / from_bytes are bincode::serialize /
+# deserialize (crates/kvforge-python/src/py_types.rs:98-110) with bincode 1.x
+# (Cargo.toml:28) of the structs in crates/kvforge-core/src/types.rs:36-148.
+# bincode 1.x's default encoding, as its specification states it:
+# little-endian fixed-width integers, usize as u64, a sequence as a u64
+# length then its elements, an Option as a u8 tag (0 None, 1 Some) then the
+# value, a unit enum variant as its u32 index, struct fields in order.
+# ---------------------------------------------------------------------------
+def _bc_seq(parts, arr, dtype):
+    a = np.ascontiguousarray(arr, dtype)
+    parts.append(np.uint64(a.size).tobytes())
+    parts.append(a.astype(np.dtype(dtype).newbyteorder("<"), copy=False).tobytes())
+
+
+def _bc_tensor(parts, ct):
+    H, T, cols = (int(x) for x in ct["qshape"])
+    _bc_seq(parts, ct["data"], np.uint8)                      # quantized_data
+    _bc_seq(parts, ct["scales"], np.float32)                  # QuantParams.scales
+    _bc_seq(parts, ct["mins"], np.float32)                    # QuantParams.mins
+    parts.append(np.array([ct["data_type"], ct["axis"]], "<u4").tobytes())  # DataType, QuantAxis
+    _bc_seq(parts, [H, T, cols], np.uint64)                   # QuantParams.shape
+    if ct["proj"] is None:
+        parts.append(b"\x00")
+    else:
+        bvt, ranks = ct["proj"]
+        D = int(np.asarray(bvt).shape[2])
+        parts.append(b"\x01")
+        _bc_seq(parts, np.asarray(bvt).reshape(-1), np.float32)  # ProjectionState.basis_vt
+        _bc_seq(parts, ranks, np.uint64)                           # ranks
+        parts.append(np.array([H, D], "<u8").tobytes())            # num_heads, head_dim
+        _bc_seq(parts, [H, T, cols], np.uint64)                    # projected_shape
+    if ct["entropy"] is None:
+        parts.append(b"\x00")
+    else:
+        freq, original_len = ct["entropy"]
+        parts.append(b"\x01")
+        _bc_seq(parts, freq, np.uint32)                            # EntropyState.frequencies
+        parts.append(np.uint64(original_len).tobytes())            # original_len
+
+
+def to_bincode(ckv) -> bytes:
+    """The reference's CompressedKV.to_bytes of an oracle compressed layer."""
+    H, T, D = (int(x) for x in ckv["shape"])
+    parts = [np.array([ckv["layer_idx"], H, T, D], "<u8").tobytes()]
+    _bc_tensor(parts, ckv["key"])
+    _bc_tensor(parts, ckv["value"])
+    parts.append(np.uint64(ckv["original_size_bytes"]).tobytes())
+    return b"".join(parts)
+
+
+class _BcReader:
+    def __init__(self, b: bytes):
+        self.b, self.p = b, 0
+
+    def take(self, n: int) -> bytes:
+        if self.p + n > len(self.b):
+            raise ValueError("truncated bincode")
+        s = self.b[self.p:self.p + n]
+        self.p += n
+        return s
+
+    def u(self, fmt: str) -> int:
+        d = np.dtype(fmt)
+        return int(np.frombuffer(self.take(d.itemsize), d)[0])
+
+    def seq(self, dtype) -> np.ndarray:
+        n = self.u("<u8")
+        d = np.dtype(dtype).newbyteorder("<")
+        return np.frombuffer(self.take(n * d.itemsize), d).astype(dtype)
+
+
+def _bc_read_tensor(r: _BcReader):
+    data = r.seq(np.uint8)
+    scales, mins = r.seq(np.float32), r.seq(np.float32)
+    dt, ax = r.u("<u4"), r.u("<u4")
+    qshape = tuple(int(x) for x in r.seq(np.uint64))
+    proj = None
+    if r.u("<u1"):
+        bvt = r.seq(np.float32)
+        ranks = r.seq(np.uint64)
+        H, D = r.u("<u8"), r.u("<u8")
+        r.seq(np.uint64)  # projected_shape
+        proj = (bvt.reshape(H, -1, D), ranks)
+    ent = None
+    if r.u("<u1"):
+        freq = r.seq(np.uint32)
+        ent = (freq, r.u("<u8"))
+    return dict(data=data, scales=scales, mins=mins, data_type=dt, axis=ax, qshape=qshape, proj=proj, entropy=ent)
+
+
+def from_bincode(b: bytes):
+    """CompressedKV.from_bytes into an oracle compressed layer (no calibration scores)."""
+    r = _BcReader(b)
+    layer_idx, H, T, D = (r.u("<u8") for _ in range(4))
+    k = _bc_read_tensor(r)
+    v = _bc_read_tensor(r)
+    orig = r.u("<u8")
+    if r.p != len(b):
+        raise ValueError("trailing bytes")
+    return dict(layer_idx=layer_idx, shape=(H, T, D), key=k, value=v, original_size_bytes=orig, scores=None)
+
+
 def compressed_size_bytes(ckv) -> int:
     return tensor_size_bytes(ckv["key"]) + tensor_size_bytes(ckv["value"])
 

@@ -485,6 +485,33 @@ def test_serialize_roundtrip(kvf):
     assert e.value.status == 6
 
 
+@pytest.mark.parametrize("preset", ["conservative", "balanced", "aggressive", "adaptive"])
+def test_serialize_is_reference_wire_format(kvf, oracle, preset):
+    """to_bytes is the reference's CompressedKV.to_bytes (bincode 1.x of
+    types.rs:36-148): byte-identical to the oracle's encoding of the same
+    layer, and bytes the oracle writes load and decompress on the GPU."""
+    from kvforge_b200 import synth
+    k, v = synth.numpy_layer(3, 257, 64, seed=21, rank=8, dtype="float16")
+    c, co = _pipeline_case(kvf, oracle, k, v, preset)
+    blob = c.to_bytes()
+    co["layer_idx"] = c.layer_idx
+    assert blob == oracle.to_bincode(co)
+    c2 = kvf.CompressedKV.from_bytes(oracle.to_bincode(co))
+    kr, vr = oracle.decompress(co, threads=4)
+    out = kvf.decompress(c2)
+    assert rel(out.keys(), kr) < REC_TOL and rel(out.values(), vr) < REC_TOL
+    assert c2.ratio() == oracle.ratio(co)
+    bad = bytearray(blob)
+    key_data_len = int(np.frombuffer(blob[32:40], "<u8")[0])
+    nsc = int(np.frombuffer(blob[40 + key_data_len:48 + key_data_len], "<u8")[0])
+    tag = 48 + key_data_len + 4 * nsc + 8 + 4 * nsc + 8 + 32  # key_data.projection_state tag
+    assert blob[tag] in (0, 1)
+    bad[tag] = 2
+    with pytest.raises(kvf.KvForgeError) as e:
+        kvf.CompressedKV.from_bytes(bytes(bad))
+    assert e.value.status == 6
+
+
 def test_host_buffer_entry_points(kvf):
     from kvforge_b200 import _lib as L
     from kvforge_b200 import synth

@@ -297,3 +297,47 @@ def test_conservative_ratio_formula(oracle):
     k, v = _kv((2, 16, 8), 11)
     c = oracle.compress(k, v, "conservative")
     assert oracle.compressed_size_bytes(c) == (2 * 16 * 8 + 2 * 4 * 2 * 8) + (2 * 16 * 8 + 2 * 4 * 2 * 16)
+
+
+def test_bincode_known_answer(oracle):
+    """The oracle's CompressedKV.to_bytes against bytes written out by hand from
+    bincode 1.x's default encoding (little-endian, u64 lengths and usize, u8
+    Option tags, u32 enum variants) of types.rs:36-148."""
+    import struct
+    key = dict(data=np.array([3, 250], np.uint8), scales=np.array([0.5], np.float32),
+               mins=np.array([-1.0], np.float32), data_type=1, axis=0, qshape=(1, 2, 1),
+               proj=(np.array([[[1.0]]], np.float32), np.array([1], np.uint64)), entropy=None)
+    val = dict(data=np.array([1, 2], np.uint8), scales=np.array([0.25, 2.0], np.float32),
+               mins=np.array([0.0, 1.5], np.float32), data_type=1, axis=1, qshape=(1, 2, 1), proj=None,
+               entropy=(np.zeros(0, np.uint32), 2))
+    ckv = dict(layer_idx=7, shape=(1, 2, 1), key=key, value=val, original_size_bytes=16)
+    want = (struct.pack("<QQQQ", 7, 1, 2, 1)
+            # key_data: quantized_data, scales, mins, DataType::INT8, QuantAxis::PerChannel, shape
+            + struct.pack("<Q", 2) + bytes([3, 250]) + struct.pack("<Qf", 1, 0.5) + struct.pack("<Qf", 1, -1.0)
+            + struct.pack("<II", 1, 0) + struct.pack("<QQQQ", 3, 1, 2, 1)
+            # Some(ProjectionState { basis_vt, ranks, num_heads, head_dim, projected_shape }), None
+            + b"\x01" + struct.pack("<Qf", 1, 1.0) + struct.pack("<QQ", 1, 1) + struct.pack("<QQ", 1, 1)
+            + struct.pack("<QQQQ", 3, 1, 2, 1) + b"\x00"
+            # value_data: ..., QuantAxis::PerToken, None, Some(EntropyState { [], 2 })
+            + struct.pack("<Q", 2) + bytes([1, 2]) + struct.pack("<Qff", 2, 0.25, 2.0)
+            + struct.pack("<Qff", 2, 0.0, 1.5) + struct.pack("<II", 1, 1) + struct.pack("<QQQQ", 3, 1, 2, 1)
+            + b"\x00" + b"\x01" + struct.pack("<Q", 0) + struct.pack("<Q", 2)
+            + struct.pack("<Q", 16))
+    assert oracle.to_bincode(ckv) == want
+    back = oracle.from_bincode(want)
+    assert oracle.to_bincode(back) == want and back["layer_idx"] == 7
+
+
+def test_bincode_roundtrip_of_compressed_layers(oracle):
+    rng = np.random.default_rng(4)
+    k = rng.standard_normal((2, 40, 16)).astype(np.float32)
+    v = rng.standard_normal((2, 40, 16)).astype(np.float32)
+    for preset in ("conservative", "balanced", "aggressive"):
+        co = oracle.compress(k, v, preset, 3)
+        b = oracle.to_bincode(co)
+        back = oracle.from_bincode(b)
+        assert oracle.to_bincode(back) == b
+        assert oracle.compressed_size_bytes(back) == oracle.compressed_size_bytes(co)
+        kr, vr = oracle.decompress(co)
+        kb, vb = oracle.decompress(back)
+        assert np.array_equal(kr, kb) and np.array_equal(vr, vb)
