@@ -337,6 +337,51 @@ kvf_status kvf_compressed_basis_bytes(const kvf_compressed* c, size_t* out);
  * was disabled or failed (the reference discards both, pipeline.rs:104-111) */
 const float* kvf_compressed_calibration(const kvf_compressed* c);
 
+/* ---- cost model with measured GPU costs (CostModel, crates/kvforge-core/src/cost.rs;
+ *      the reference's CpuCostModel is a fixed table, crates/kvforge-cpu/src/cost.rs:9-115)
+ * A table row per preset: expected ratio, microseconds per original (f32)
+ * byte to compress and to decompress, quality in [0, 1] (1 = lossless). */
+typedef struct {
+  int32_t preset;
+  double compression_ratio;
+  double compress_us_per_byte;
+  double decompress_us_per_byte;
+  double quality;
+} kvf_preset_cost;
+/* CostEstimate (crates/kvforge-core/src/cost.rs) */
+typedef struct {
+  int32_t preset;
+  double compress_us, transfer_us, decompress_us, total_us, compression_ratio;
+} kvf_estimate;
+/* BandwidthTier, in declaration order; kvf_bandwidth_bytes_per_us gives
+ * BandwidthTier::bytes_per_us (negative for an unknown tier) */
+typedef enum {
+  KVF_BW_LOCAL = 0,
+  KVF_BW_RDMA = 1,
+  KVF_BW_ETHERNET_100G = 2,
+  KVF_BW_ETHERNET_25G = 3,
+  KVF_BW_ETHERNET_10G = 4,
+  KVF_BW_WAN = 5
+} kvf_bandwidth_tier;
+double kvf_bandwidth_bytes_per_us(int32_t tier);
+/* Measures Conservative, Balanced and Aggressive on one sample layer (device
+ * keys and values [H,T,D] of in_dtype) and writes three rows: per-byte costs
+ * from CUDA events over `reps` compress calls and `reps` decompress calls on
+ * `stream` (bases calibrated once, outside the timing), the layer's
+ * compression ratio, and quality = 1 - the larger relative Frobenius error of
+ * keys and values. Allocates its output buffers; SYNCHRONISES. */
+kvf_status kvf_cost_measure(kvf_ctx* ctx, const void* keys, const void* values, int32_t in_dtype, size_t H,
+                            size_t T, size_t D, int reps, kvf_preset_cost* rows_out, void* stream);
+/* CostModel::estimate: the row of `preset` (the first row for a preset the
+ * table lacks, as the reference falls back to its first entry); host only */
+kvf_status kvf_cost_estimate(const kvf_preset_cost* rows, size_t n, size_t original_bytes, int32_t preset,
+                             double bytes_per_us, kvf_estimate* out);
+/* CostModel::select_codec: estimates of the rows with quality >= min_quality,
+ * by total time, fastest first (ties keep table order); `out` holds n entries,
+ * *count gets the number written; host only */
+kvf_status kvf_cost_select(const kvf_preset_cost* rows, size_t n, size_t original_bytes, double bytes_per_us,
+                           double min_quality, kvf_estimate* out, size_t* count);
+
 /* serialisation to host bytes and back (CompressedKV.to_bytes/from_bytes,
  * crates/kvforge-python/src/py_types.rs:98-110) in the reference's wire
  * format: bincode 1.x of CompressedKV (crates/kvforge-core/src/types.rs:36-148),

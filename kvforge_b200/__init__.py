@@ -22,7 +22,8 @@ from . import _lib as L
 from ._lib import KvForgeError
 
 __all__ = [
-    "KVCache", "CompressedKV", "CompressionPipeline", "StreamingCompressor", "compress", "decompress", "KvForgeError",
+    "KVCache", "CompressedKV", "CompressionPipeline", "StreamingCompressor", "GpuCostModel", "BandwidthTier",
+    "CostEstimate", "compress_adaptive", "compress", "decompress", "KvForgeError",
     "Basis", "QuantParams", "EntropyState", "GpuQuantizer", "GpuProjector", "GpuSensitivityCalibrator",
     "GpuEntropyCodec", "config_from_preset", "parse_preset", "INT4", "INT8", "F32", "PER_CHANNEL", "PER_TOKEN",
 ]
@@ -456,6 +457,110 @@ class StreamingCompressor:
 
     def decompress(self, c: CompressedKV) -> KVCache:
         return self._pipe.decompress(c)
+
+
+# ---------------------------------------------------------------------------
+# Cost model (CostModel, crates/kvforge-core/src/cost.rs) with measured GPU costs
+# ---------------------------------------------------------------------------
+class BandwidthTier:
+    """BandwidthTier (crates/kvforge-core/src/cost.rs), in declaration order."""
+    LOCAL, RDMA, ETHERNET_100G, ETHERNET_25G, ETHERNET_10G, WAN = range(6)
+
+    @staticmethod
+    def bytes_per_us(tier: int) -> float:
+        v = L.lib().kvf_bandwidth_bytes_per_us(int(tier))
+        if v < 0:
+            raise ValueError(f"unknown bandwidth tier {tier}")
+        return v
+
+
+@dataclass
+class CostEstimate:
+    preset: int
+    compress_us: float
+    transfer_us: float
+    decompress_us: float
+    total_us: float
+    compression_ratio: float
+
+
+_PRESET_NAMES = {v: k for k, v in _PRESETS.items()}
+
+
+class GpuCostModel:
+    """CostModel whose table is measured on this GPU.
+
+    The reference's CpuCostModel (crates/kvforge-cpu/src/cost.rs:9-115) holds a
+    fixed table of ratio, microseconds per byte and quality per preset and ranks
+    presets by compress + transfer + decompress time on a bandwidth tier. Here
+    measure() times the GPU pipeline on a sample layer (bases calibrated once,
+    outside the timing), takes the sample's ratio and scores quality as
+    1 - the larger relative Frobenius error of keys and values. estimate() and
+    select_codec() are the reference's arithmetic (through the C ABI); any
+    table, the reference's own included, can be given to the constructor.
+    select_preset() picks the preset the Adaptive preset stands for
+    (crates/kvforge-core/src/pipeline.rs:14-15)."""
+
+    def __init__(self, rows):
+        self._rows = (L.PresetCost * len(rows))()
+        for i, r in enumerate(rows):
+            if isinstance(r, L.PresetCost):
+                self._rows[i] = r
+            else:
+                self._rows[i] = L.PresetCost(int(r["preset"]), float(r["compression_ratio"]),
+                                             float(r["compress_us_per_byte"]), float(r["decompress_us_per_byte"]),
+                                             float(r["quality"]))
+
+    @staticmethod
+    def measure(kv: KVCache, reps: int = 5, device=None) -> "GpuCostModel":
+        dev = _device_index(device)
+        k = _as_device(kv.keys_tensor, dev)
+        v = _as_device(kv.values_tensor, dev)
+        if k.dtype != v.dtype:
+            v = v.to(k.dtype)
+        H, T, D = k.shape
+        rows = (L.PresetCost * 3)()
+        L.check(L.lib().kvf_cost_measure(L.context(dev), _ptr(k), _ptr(v), _dtype_code(k), H, T, D, int(reps),
+                                         rows, _stream(dev)))
+        return GpuCostModel(list(rows))
+
+    def rows(self) -> list:
+        return [dict(preset=_PRESET_NAMES[r.preset], compression_ratio=r.compression_ratio,
+                     compress_us_per_byte=r.compress_us_per_byte, decompress_us_per_byte=r.decompress_us_per_byte,
+                     quality=r.quality) for r in self._rows]
+
+    @staticmethod
+    def _bw(bandwidth) -> float:
+        return float(bandwidth) if isinstance(bandwidth, float) else BandwidthTier.bytes_per_us(bandwidth)
+
+    def estimate(self, original_bytes: int, preset, bandwidth) -> CostEstimate:
+        """bandwidth: a BandwidthTier value, or bytes per microsecond as a float."""
+        e = L.CostEstimate()
+        L.check(L.lib().kvf_cost_estimate(self._rows, len(self._rows), int(original_bytes), parse_preset(preset),
+                                          self._bw(bandwidth), C.byref(e)))
+        return CostEstimate(e.preset, e.compress_us, e.transfer_us, e.decompress_us, e.total_us, e.compression_ratio)
+
+    def select_codec(self, original_bytes: int, bandwidth, min_quality: Optional[float] = None) -> list:
+        out = (L.CostEstimate * len(self._rows))()
+        n = C.c_size_t()
+        L.check(L.lib().kvf_cost_select(self._rows, len(self._rows), int(original_bytes), self._bw(bandwidth),
+                                        float(min_quality or 0.0), out, C.byref(n)))
+        return [CostEstimate(e.preset, e.compress_us, e.transfer_us, e.decompress_us, e.total_us,
+                             e.compression_ratio) for e in out[: n.value]]
+
+    def select_preset(self, original_bytes: int, bandwidth, min_quality: Optional[float] = None) -> str:
+        est = self.select_codec(original_bytes, bandwidth, min_quality)
+        if not est:
+            raise KvForgeError(L.ERR_INVALID_CONFIG, "no preset meets the quality floor")
+        return _PRESET_NAMES[est[0].preset]
+
+
+def compress_adaptive(kv: KVCache, model: GpuCostModel, bandwidth, min_quality: Optional[float] = None,
+                      device=None):
+    """Compress with the preset the cost model ranks fastest end to end for
+    this layer's size on `bandwidth`. -> (CompressedKV, preset name)."""
+    preset = model.select_preset(kv.size_bytes(), bandwidth, min_quality)
+    return CompressionPipeline(device).compress(kv, preset), preset
 
 
 def compress(kv: KVCache, preset="balanced") -> CompressedKV:

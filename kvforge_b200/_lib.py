@@ -52,6 +52,7 @@ EXPORTS = [
     "kvf_compressed_tensor_info", "kvf_compressed_tensor_views", "kvf_compressed_basis",
     "kvf_compressed_basis_bytes", "kvf_compressed_calibration", "kvf_compressed_serialize",
     "kvf_compressed_deserialize", "kvf_compressed_free",
+    "kvf_bandwidth_bytes_per_us", "kvf_cost_measure", "kvf_cost_estimate", "kvf_cost_select",
     "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read", "kvf_calibrate_noalloc",
 ]
 
@@ -70,6 +71,29 @@ class PipelineConfig(C.Structure):
         ("projection_variance_threshold", C.c_double),
         ("enable_entropy_coding", C.c_int32),
         ("enable_calibration", C.c_int32),
+    ]
+
+
+class PresetCost(C.Structure):
+    """kvf_preset_cost: one row of the cost table (crates/kvforge-cpu/src/cost.rs:15-24)."""
+    _fields_ = [
+        ("preset", C.c_int32),
+        ("compression_ratio", C.c_double),
+        ("compress_us_per_byte", C.c_double),
+        ("decompress_us_per_byte", C.c_double),
+        ("quality", C.c_double),
+    ]
+
+
+class CostEstimate(C.Structure):
+    """kvf_estimate: CostEstimate (crates/kvforge-core/src/cost.rs)."""
+    _fields_ = [
+        ("preset", C.c_int32),
+        ("compress_us", C.c_double),
+        ("transfer_us", C.c_double),
+        ("decompress_us", C.c_double),
+        ("total_us", C.c_double),
+        ("compression_ratio", C.c_double),
     ]
 
 
@@ -137,6 +161,11 @@ def _declare(L):
         "kvf_compressed_serialize": (st, [p, p, sz, szp]),
         "kvf_compressed_deserialize": (st, [p, p, sz, C.POINTER(p), p]),
         "kvf_compressed_free": (st, [p]),
+        "kvf_bandwidth_bytes_per_us": (C.c_double, [i32]),
+        "kvf_cost_measure": (st, [p, p, p, i32, sz, sz, sz, C.c_int, C.POINTER(PresetCost), p]),
+        "kvf_cost_estimate": (st, [C.POINTER(PresetCost), sz, sz, i32, C.c_double, C.POINTER(CostEstimate)]),
+        "kvf_cost_select": (st, [C.POINTER(PresetCost), sz, sz, C.c_double, C.c_double, C.POINTER(CostEstimate),
+                                 szp]),
         "kvf_launch_count": (C.c_uint64, []),
         "kvf_stage_name": (C.c_char_p, [i32]),
         "kvf_profile_enable": (st, [p, C.c_int]),

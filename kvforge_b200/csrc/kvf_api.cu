@@ -1610,4 +1610,147 @@ kvf_status kvf_compressed_free(kvf_compressed* c) {
   return KVF_OK;
 }
 
+// ---- cost model with measured GPU costs --------------------------------------
+// CostModel (crates/kvforge-core/src/cost.rs) with rows measured on this GPU;
+// the reference's CpuCostModel holds a fixed table (crates/kvforge-cpu/src/cost.rs:26-50)
+// and uses the same arithmetic (cost.rs:64-115), restated here.
+double kvf_bandwidth_bytes_per_us(int32_t tier) {
+  // BandwidthTier::bytes_per_us (crates/kvforge-core/src/cost.rs)
+  static const double kBw[] = {25000.0, 12500.0, 10000.0, 2500.0, 1000.0, 100.0};
+  return (tier >= 0 && tier < 6) ? kBw[tier] : -1.0;
+}
+
+kvf_status kvf_cost_estimate(const kvf_preset_cost* rows, size_t n, size_t original_bytes, int32_t preset,
+                             double bytes_per_us, kvf_estimate* out) {
+  if (!rows || n == 0 || !out) return fail(KVF_ERR_INVALID_CONFIG, "empty cost table");
+  if (!(bytes_per_us > 0.0)) return fail(KVF_ERR_INVALID_CONFIG, "bandwidth must be positive");
+  const kvf_preset_cost* e = &rows[0];  // an unknown preset takes the first row, as the reference does
+  for (size_t i = 0; i < n; ++i)
+    if (rows[i].preset == preset) { e = &rows[i]; break; }
+  if (!(e->compression_ratio > 0.0)) return fail(KVF_ERR_INVALID_CONFIG, "compression ratio must be positive");
+  const double bytes = (double)original_bytes;
+  out->preset = e->preset;
+  out->compress_us = bytes * e->compress_us_per_byte;
+  out->transfer_us = bytes / e->compression_ratio / bytes_per_us;
+  out->decompress_us = bytes * e->decompress_us_per_byte;
+  out->total_us = out->compress_us + out->transfer_us + out->decompress_us;
+  out->compression_ratio = e->compression_ratio;
+  return KVF_OK;
+}
+
+kvf_status kvf_cost_select(const kvf_preset_cost* rows, size_t n, size_t original_bytes, double bytes_per_us,
+                           double min_quality, kvf_estimate* out, size_t* count) {
+  if (!rows || !out || !count) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  std::vector<kvf_estimate> est;
+  for (size_t i = 0; i < n; ++i) {
+    if (!(rows[i].quality >= min_quality)) continue;
+    kvf_estimate e;
+    KVF_TRY(kvf_cost_estimate(&rows[i], 1, original_bytes, rows[i].preset, bytes_per_us, &e));
+    est.push_back(e);
+  }
+  std::stable_sort(est.begin(), est.end(),
+                   [](const kvf_estimate& a, const kvf_estimate& b) { return a.total_us < b.total_us; });
+  std::copy(est.begin(), est.end(), out);
+  *count = est.size();
+  return KVF_OK;
+}
+
+kvf_status kvf_cost_measure(kvf_ctx* ctx, const void* keys, const void* values, int32_t in_dtype, size_t H,
+                            size_t T, size_t D, int reps, kvf_preset_cost* rows, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (!keys || !values || !rows || H * T * D == 0) return fail(KVF_ERR_INVALID_CONFIG, "empty sample");
+  if (reps < 1 || reps > 1000) return fail(KVF_ERR_INVALID_CONFIG, "reps must be in 1..1000");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  const size_t n = H * T * D, esz = in_dtype == KVF_IN_F16 ? 2 : 4;
+  const double orig = (double)(2 * n * 4);  // KVCache::size_bytes (types.rs:30-32)
+  // the sample on the host as f32, for the quality score
+  std::vector<float> ref[2];
+  const void* src[2] = {keys, values};
+  for (int i = 0; i < 2; ++i) {
+    std::vector<uint8_t> raw(n * esz);
+    KVF_CUDA(cudaMemcpyAsync(raw.data(), src[i], n * esz, cudaMemcpyDeviceToHost, st));
+    KVF_CUDA(cudaStreamSynchronize(st));
+    ref[i].resize(n);
+    if (esz == 2) {
+      const __half* hp = reinterpret_cast<const __half*>(raw.data());
+      for (size_t j = 0; j < n; ++j) ref[i][j] = __half2float(hp[j]);
+    } else {
+      std::memcpy(ref[i].data(), raw.data(), n * 4);
+    }
+  }
+  float* dout[2] = {nullptr, nullptr};
+  cudaEvent_t ev[4] = {};
+  kvf_status s = KVF_OK;
+  auto cuda = [&](cudaError_t e) {
+    if (e != cudaSuccess && s == KVF_OK) s = fail(KVF_ERR_CUDA, cudaGetErrorString(e));
+    return s == KVF_OK;
+  };
+  for (int i = 0; i < 2; ++i) cuda(cudaMalloc(&dout[i], n * 4));
+  for (int i = 0; i < 4; ++i) cuda(cudaEventCreate(&ev[i]));
+  const int32_t presets[3] = {KVF_CONSERVATIVE, KVF_BALANCED, KVF_AGGRESSIVE};
+  for (int pi = 0; pi < 3 && s == KVF_OK; ++pi) {
+    kvf_pipeline_config cfg;
+    kvf_pipeline_config_from_preset(presets[pi], &cfg);
+    kvf_basis *kb = nullptr, *vb = nullptr;  // calibrated once, outside the timing
+    if (cfg.enable_projection) {
+      s = kvf_basis_compute(ctx, keys, in_dtype, H, T, D, cfg.projection_variance_threshold, 0, &kb, stream);
+      if (s == KVF_OK)
+        s = kvf_basis_compute(ctx, values, in_dtype, H, T, D, cfg.projection_variance_threshold, 0, &vb, stream);
+    }
+    kvf_compressed* c = nullptr;
+    double ratio = 0.0;
+    if (s == KVF_OK) s = kvf_compress_layer(ctx, keys, values, in_dtype, H, T, D, 0, &cfg, kb, vb, &c, stream);
+    if (s == KVF_OK) s = kvf_compression_ratio(c, &ratio);
+    if (s == KVF_OK) s = kvf_decompress_layer(ctx, c, dout[0], dout[1], stream);
+    if (s == KVF_OK) s = kvf_sync(ctx, stream);
+    double err = 0.0;
+    for (int i = 0; i < 2 && s == KVF_OK; ++i) {  // relative Frobenius error of each tensor
+      std::vector<float> got(n);
+      if (!cuda(cudaMemcpyAsync(got.data(), dout[i], n * 4, cudaMemcpyDeviceToHost, st)) ||
+          !cuda(cudaStreamSynchronize(st)))
+        break;
+      double e2 = 0.0, r2 = 0.0;
+      for (size_t j = 0; j < n; ++j) {
+        const double d = (double)got[j] - (double)ref[i][j];
+        e2 += d * d;
+        r2 += (double)ref[i][j] * ref[i][j];
+      }
+      err = std::max(err, r2 > 0.0 ? std::sqrt(e2 / r2) : std::sqrt(e2));
+    }
+    float ms_c = 0.f, ms_d = 0.f;
+    if (s == KVF_OK && cuda(cudaEventRecord(ev[0], st))) {
+      for (int r = 0; r < reps && s == KVF_OK; ++r) {
+        kvf_compressed* t = nullptr;
+        s = kvf_compress_layer(ctx, keys, values, in_dtype, H, T, D, 0, &cfg, kb, vb, &t, stream);
+        kvf_compressed_free(t);
+      }
+      if (cuda(cudaEventRecord(ev[1], st)) && cuda(cudaEventRecord(ev[2], st))) {
+        for (int r = 0; r < reps && s == KVF_OK; ++r) s = kvf_decompress_layer(ctx, c, dout[0], dout[1], stream);
+        if (cuda(cudaEventRecord(ev[3], st)) && cuda(cudaEventSynchronize(ev[3])))
+          if (cuda(cudaEventElapsedTime(&ms_c, ev[0], ev[1]))) cuda(cudaEventElapsedTime(&ms_d, ev[2], ev[3]));
+      }
+    }
+    if (s == KVF_OK) s = kvf_sync(ctx, stream);
+    if (s == KVF_OK) {
+      rows[pi].preset = presets[pi];
+      rows[pi].compression_ratio = ratio;
+      rows[pi].compress_us_per_byte = 1e3 * ms_c / reps / orig;
+      rows[pi].decompress_us_per_byte = 1e3 * ms_d / reps / orig;
+      rows[pi].quality = std::min(1.0, std::max(0.0, 1.0 - err));
+    }
+    kvf_compressed_free(c);
+    kvf_basis_free(kb);
+    kvf_basis_free(vb);
+  }
+  cudaStreamSynchronize(st);
+  for (int i = 0; i < 4; ++i)
+    if (ev[i]) cudaEventDestroy(ev[i]);
+  for (int i = 0; i < 2; ++i)
+    if (dout[i]) cudaFree(dout[i]);
+  return s;
+}
+
 }  // extern "C"
