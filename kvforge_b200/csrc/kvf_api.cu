@@ -70,20 +70,44 @@ struct DeviceGuard {
 };
 
 // per-call scratch, released in stream order when the call returns
+// Requests up to kSmallScratch bytes are carved, 256-byte aligned, from one
+// shared block of kScratchBlock bytes, so a call on a small layer makes one
+// pool allocation and one free for all its small buffers; larger requests get
+// their own allocation.
+constexpr size_t kScratchAlign = 256;
+constexpr size_t kSmallScratch = 64 * 1024;
+constexpr size_t kScratchBlock = 256 * 1024;
+inline size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
 struct Scratch {
   cudaStream_t st;
   cudaMemPool_t pool;
   std::vector<void*> ptrs;
+  uint8_t* block = nullptr;
+  size_t used = 0;
   Scratch(cudaStream_t s, cudaMemPool_t p) : st(s), pool(p) {}
   ~Scratch() {
     for (void* p : ptrs) cudaFreeAsync(p, st);
   }
+  void* raw(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMallocFromPoolAsync(&p, std::max<size_t>(bytes, 1), pool, st) != cudaSuccess) return nullptr;
+    ptrs.push_back(p);
+    return p;
+  }
   template <class T>
   T* get(size_t count) {
-    void* p = nullptr;
-    if (cudaMallocFromPoolAsync(&p, std::max<size_t>(count, 1) * sizeof(T), pool, st) != cudaSuccess) return nullptr;
-    ptrs.push_back(p);
-    return static_cast<T*>(p);
+    const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+    if (bytes > kSmallScratch) return static_cast<T*>(raw(bytes));
+    const size_t need = align_up(bytes, kScratchAlign);
+    if (!block || used + need > kScratchBlock) {
+      block = static_cast<uint8_t*>(raw(kScratchBlock));
+      used = 0;
+      if (!block) return nullptr;
+    }
+    T* p = reinterpret_cast<T*>(block + used);
+    used += need;
+    return p;
   }
 };
 
@@ -331,17 +355,26 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
   out->qcols = qcols;
   out->packed_len = plen;
   out->num_params = np;
-  out->d_scales = owner->alloc<float>(np, st);
-  out->d_mins = owner->alloc<float>(np, st);
-  if (!out->d_scales || !out->d_mins) return fail(KVF_ERR_CUDA, "allocation failed");
   const bool do_ent = entropy && plen > 0;
   out->has_freq = do_ent;
-  uint8_t* packed = do_ent ? sc.get<uint8_t>(plen) : owner->alloc<uint8_t>(plen, st);
+  // the tensor's own buffers (scales, mins, then the 256 counts, the rANS
+  // container and its length, or the packed codes) in one allocation
+  const size_t sp = align_up(np * 4, kScratchAlign);
+  const size_t data_cap = do_ent ? rans_max_len(plen, kRansChunk) : plen;
+  const size_t owned = 2 * sp + (do_ent ? align_up(1024, kScratchAlign) + align_up(data_cap, kScratchAlign) + 8
+                                        : std::max<size_t>(plen, 1));
+  uint8_t* base = owner->alloc<uint8_t>(owned, st);
+  if (!base) return fail(KVF_ERR_CUDA, "allocation failed");
+  out->d_scales = reinterpret_cast<float*>(base);
+  out->d_mins = reinterpret_cast<float*>(base + sp);
+  uint8_t* packed = do_ent ? sc.get<uint8_t>(plen) : base + 2 * sp;
   if (!packed) return fail(KVF_ERR_CUDA, "allocation failed");
   uint32_t* hist = nullptr;
   if (do_ent) {
-    out->d_freq = owner->alloc<uint32_t>(256, st);
-    if (!out->d_freq) return fail(KVF_ERR_CUDA, "allocation failed");
+    out->d_freq = reinterpret_cast<uint32_t*>(base + 2 * sp);
+    out->data_cap = data_cap;
+    out->d_data = base + 2 * sp + align_up(1024, kScratchAlign);
+    out->d_len = reinterpret_cast<uint64_t*>(out->d_data + align_up(data_cap, kScratchAlign));
     KVF_CUDA(cudaMemsetAsync(out->d_freq, 0, 256 * sizeof(uint32_t), st));
     hist = out->d_freq;
   }
@@ -419,10 +452,6 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
   if (cpart) KVF_CUDA(launch_calib_finalize(cpart, H, ctiles, T, D, d_scores, st));
 
   if (do_ent) {
-    out->data_cap = rans_max_len(plen, kRansChunk);
-    out->d_data = owner->alloc<uint8_t>(out->data_cap, st);
-    out->d_len = owner->alloc<uint64_t>(1, st);
-    if (!out->d_data || !out->d_len) return fail(KVF_ERR_CUDA, "allocation failed");
     StageTimer tm(ctx, KVF_STAGE_ENTROPY_ENCODE, (double)plen, st);
     KVF_TRY(rans_encode_into(ctx, sc, packed, plen, out->d_freq, out->d_data, out->d_len, st));
     out->len_known = false;
