@@ -791,23 +791,22 @@ def stream_arm(args):
 
     # sizes and reconstruction error of one append (untimed), both modes
     def measure(reuse):
-        acc = {"comp": 0, "err2_k": 0.0, "ref2_k": 0.0, "err2_v": 0.0, "ref2_v": 0.0}
+        per_layer = []  # one tuple per layer from the worker threads (list.append is atomic)
 
         def keep(i, h, ko, vo, sp):
             L.check(lib.kvf_sync(ctx, sp))
             n, b = C.c_size_t(), C.c_size_t()
             L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
             L.check(lib.kvf_compressed_basis_bytes(h, C.byref(b)))
-            acc["comp"] += n.value - (b.value if reuse else 0)
             kf, vf = layers[i][1][0].float(), layers[i][2][0].float()
-            acc["err2_k"] += float(((ko - kf) ** 2).sum())
-            acc["ref2_k"] += float((kf ** 2).sum())
-            acc["err2_v"] += float(((vo - vf) ** 2).sum())
-            acc["ref2_v"] += float((vf ** 2).sum())
+            per_layer.append((i, n.value - (b.value if reuse else 0), float(((ko - kf) ** 2).sum()),
+                              float((kf ** 2).sum()), float(((vo - vf) ** 2).sum()), float((vf ** 2).sum())))
 
         append_step(0, reuse, keep)
         torch.cuda.synchronize()
-        return acc
+        per_layer.sort()
+        keys_ = ("comp", "err2_k", "ref2_k", "err2_v", "ref2_v")
+        return {k2: sum(r[j + 1] for r in per_layer) for j, k2 in enumerate(keys_)}
 
     meas = {r: measure(r) for r in (True, False)}
     for s in range(args.warmup):

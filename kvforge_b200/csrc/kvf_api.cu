@@ -1365,6 +1365,13 @@ kvf_status kvf_basis_free(kvf_basis* b) {
 }
 
 // ---- whole layer --------------------------------------------------------------
+namespace {
+// a layer of at most this many elements per tensor runs keys and values on
+// one stream (a 64-token chunk of 8 heads is 65536)
+constexpr size_t kSmallLayerElems = size_t(1) << 20;
+bool small_layer(size_t H, size_t T, size_t D) { return H * T * D <= kSmallLayerElems; }
+}  // namespace
+
 kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values, int32_t in_dtype, size_t H,
                               size_t T, size_t D, size_t layer_idx, const kvf_pipeline_config* cfg,
                               const kvf_basis* k_basis, const kvf_basis* v_basis, kvf_compressed** out,
@@ -1393,19 +1400,28 @@ kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values
     c->d_scores = c->alloc<float>(H);
     if (!c->d_scores) return fail(KVF_ERR_CUDA, "allocation failed");
   }
-  // keys on the caller's stream, values on its side stream, joined before return
+  // keys on the caller's stream, values on its side stream, joined before
+  // return; a small layer keeps both on the caller's stream (its kernels are
+  // too short to gain from overlapping, and the fork and join cost API calls)
   kvf_ctx::Side* sd = nullptr;
-  KVF_CUDA(ctx->side_for(st, &sd));
-  KVF_CUDA(cudaEventRecord(sd->fork, st));
-  KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+  cudaStream_t vst = st;
+  if (!small_layer(H, T, D)) {
+    KVF_CUDA(ctx->side_for(st, &sd));
+    KVF_CUDA(cudaEventRecord(sd->fork, st));
+    KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+    vst = sd->s;
+  }
   kvf_status s = compress_tensor(ctx, c.get(), keys, in_dtype, H, T, D, cfg->key_data_type, KVF_PER_CHANNEL, kb,
                                  cfg->enable_entropy_coding != 0, cfg->enable_calibration != 0, c->d_scores,
                                  &c->key, st);
   if (s == KVF_OK)
     s = compress_tensor(ctx, c.get(), values, in_dtype, H, T, D, cfg->value_data_type, KVF_PER_TOKEN, vb,
-                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, sd->s);
-  cudaError_t je = cudaEventRecord(sd->join, sd->s);
-  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
+                        cfg->enable_entropy_coding != 0, false, nullptr, &c->value, vst);
+  cudaError_t je = cudaSuccess;
+  if (sd) {
+    je = cudaEventRecord(sd->join, sd->s);
+    if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
+  }
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   if (s != KVF_OK) {
     std::string msg = g_err;
@@ -1424,13 +1440,20 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
   kvf_ctx::Side* sd = nullptr;
-  KVF_CUDA(ctx->side_for(st, &sd));
-  KVF_CUDA(cudaEventRecord(sd->fork, st));
-  KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+  cudaStream_t vst = st;
+  if (!small_layer(c->H, c->T, c->D)) {  // as in kvf_compress_layer
+    KVF_CUDA(ctx->side_for(st, &sd));
+    KVF_CUDA(cudaEventRecord(sd->fork, st));
+    KVF_CUDA(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+    vst = sd->s;
+  }
   kvf_status s = decompress_tensor(ctx, c->key, keys_out, st);
-  if (s == KVF_OK) s = decompress_tensor(ctx, c->value, values_out, sd->s);
-  cudaError_t je = cudaEventRecord(sd->join, sd->s);
-  if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
+  if (s == KVF_OK) s = decompress_tensor(ctx, c->value, values_out, vst);
+  cudaError_t je = cudaSuccess;
+  if (sd) {
+    je = cudaEventRecord(sd->join, sd->s);
+    if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
+  }
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   return s;
 }
