@@ -808,6 +808,8 @@ def stream_arm(args):
         keys_ = ("comp", "err2_k", "ref2_k", "err2_v", "ref2_v")
         return {k2: sum(r[j + 1] for r in per_layer) for j, k2 in enumerate(keys_)}
 
+    engines = {"auto": L.RECON_AUTO, "cuda": L.RECON_CUDA_CORE, "tc": L.RECON_TENSOR_CORE}
+    L.check(lib.kvf_set_reconstruct_engine(ctx, engines[args.recon_engine]))
     meas = {r: measure(r) for r in (True, False)}
     for s in range(args.warmup):
         append_step(s % n_chunks, True)
@@ -848,6 +850,7 @@ def stream_arm(args):
         cpu = {"value": nb / sec / GB, "unit": UNIT, "cores": 1, "kind": "port",
                "sample": f"one {A}-token chunk [{H},{A},{D}] fp16 K+V, compress+decompress with a fresh basis "
                          f"per chunk (the reference's semantics), 1 thread, {sec * 1e3:.2f} ms per chunk"}
+    L.check(lib.kvf_set_reconstruct_engine(ctx, L.RECON_AUTO))
     for lay in layers:
         for b in lay[3:]:
             if b is not None:
@@ -869,8 +872,9 @@ def stream_arm(args):
                    "prefix_tokens": P, "append_tokens": A, "head_dim": D, "input_dtype": w["dtype"],
                    "output_dtype": "f32", "basis": "the prefix's calibrated basis, reused by every chunk",
                    "step": "one append to every layer", "chunk_pool": n_chunks,
-                   "l2": "chunks are L2-resident (256 KiB each); the step is launch-bound",
-                   "parallelism": f"layer-sharded x{world}", "host_threads_per_gpu": nthr},
+                   "l2": "chunks are L2-resident (256 KiB each); the step is latency-bound",
+                   "parallelism": f"layer-sharded x{world}", "host_threads_per_gpu": nthr,
+                   "reconstruct_engine": args.recon_engine},
         "tokens_per_s": A * r["layers"] / (r["ms"] / 1e3),
         "us_per_layer_append": 1e3 * r["ms"] / max(len(mine), 1),
         "ratio_amortized": r["original_bytes"] / r["compressed_bytes"],
@@ -905,6 +909,8 @@ def main():
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--recon-engine", default="auto", choices=["auto", "cuda", "tc"],
+                    help="reconstruction engine of the streaming workload")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
