@@ -271,9 +271,21 @@ __global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
       const uint64_t rk = ranks[h];
       rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
       const float* B = bvt + (size_t)h * R * D;
-      for (int i = tid; i < D * Rpad; i += blockDim.x) {
-        const int c = i / Rpad, r = i - c * Rpad;
-        vT[i] = (r < rank) ? B[(size_t)r * D + c] : 0.0f;
+      // read row by row (consecutive threads, consecutive channels: coalesced)
+      // with 4 loads in flight per thread, and write transposed, vT[c][r]
+      const int nv = D * Rpad;
+      for (int i0 = tid; i0 < nv; i0 += 4 * (int)blockDim.x) {
+        float bv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = i0 + u * (int)blockDim.x, r = i / D, c = i - r * D;
+          bv[u] = (i < nv && r < rank) ? __ldg(B + (size_t)r * D + c) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = i0 + u * (int)blockDim.x, r = i / D, c = i - r * D;
+          if (i < nv) vT[c * Rpad + r] = bv[u];
+        }
       }
       if (MODE == 1)
         for (int r = tid; r < R; r += blockDim.x) {
