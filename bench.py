@@ -205,7 +205,8 @@ def decode_attention_leg(lib, L, torch, lay, dev, cfg, in_code, H, T, D, reps=20
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 20 ms."""
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms (faster polling stalls
+    the launches of this process)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -219,7 +220,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "20",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
