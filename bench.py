@@ -205,23 +205,71 @@ def decode_attention_leg(lib, L, torch, lay, dev, cfg, in_code, H, T, D, reps=20
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms (faster polling stalls
-    the launches of this process)."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, sampled
+    in-process with read-only NVML queries every `period` seconds on a
+    background thread; nvidia-smi polling (200 ms) when NVML is not importable.
+    The device is matched to the CUDA ordinal by UUID."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, period: float = 0.01):
         self.device = device
+        self.period = period
+        self.samples = []  # (sm_mhz, power_w, reasons bitmask)
         self.lines = []
         self.proc = None
+        self.nv = None
+        self.handle = None
+        self.max_mhz = None
+        self.stop_flag = threading.Event()
+        self.t = None
+        self.source = None
+
+    def _open_nvml(self):
+        import pynvml as nv
+        import torch
+        nv.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        try:
+            h = nv.nvmlDeviceGetHandleByUUID(uuid)
+        except Exception:
+            h = nv.nvmlDeviceGetHandleByIndex(self.device)
+        self.nv, self.handle = nv, h
+        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+    def _sample_nvml(self):
+        nv, h = self.nv, self.handle
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                     nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+            except Exception:
+                pass
+            self.stop_flag.wait(self.period)
 
     def start(self):
+        try:
+            self._open_nvml()
+            self.source = f"NVML in-process, every {self.period * 1e3:.0f} ms"
+            self.t = threading.Thread(target=self._sample_nvml, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi, every 200 ms"
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
             t0 = time.time()
@@ -236,8 +284,25 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nv is not None:
+            self.stop_flag.set()
+            self.t.join(timeout=2)
+            sm = [a for a, _, _ in self.samples]
+            pw = [b for _, b, _ in self.samples]
+            reasons = set()
+            for _, _, bits in self.samples:
+                for name, attr in self.REASONS:
+                    if bits & int(getattr(self.nv, attr, 0)):
+                        reasons.add(name)
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+            return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons),
+                    "source": self.source}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -260,7 +325,37 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons)}
+                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons),
+                "source": self.source}
+
+
+def entropy_accounting(lib, L, K, h, dev) -> dict:
+    """Bytes of the entropy-coded data of one compressed layer (both tensors):
+    this library's chunked multi-lane container (KVR2) as written, against
+    what the reference's one serial rANS stream would take for the same codes
+    (crates/kvforge-cpu/src/entropy.rs:24-86): the cross-entropy of the codes
+    under the reference's model p_s = (f_s + 1) / sum(f + 1) in whole 32-bit
+    words plus the coder's 64-bit final state (an estimate: constriction 0.4,
+    which the reference calls, is not available to run), and the codes'
+    empirical entropy (the Shannon bound of any order-0 coder)."""
+    out = {"kvr2": 0, "single_stream": 0, "shannon": 0.0}
+    for which in (0, 1):
+        R, pl, dl, he = C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_int32()
+        L.check(lib.kvf_compressed_tensor_info(h, which, C.byref(R), C.byref(pl), C.byref(dl), C.byref(he)))
+        ptrs = [C.c_void_p() for _ in range(6)]
+        L.check(lib.kvf_compressed_tensor_views(h, which, *[C.byref(p) for p in ptrs]))
+        if not he.value or not ptrs[3].value:
+            continue
+        f = K._view(ptrs[3].value, (256,), "<u4", dev).cpu().numpy().astype(np.float64)
+        n = f.sum()
+        p_ref = (f + 1.0) / (f.sum() + 256.0)
+        xent = float(-(f * np.log2(p_ref)).sum())
+        nz = f > 0
+        shannon = float(-(f[nz] * np.log2(f[nz] / n)).sum())
+        out["kvr2"] += dl.value
+        out["single_stream"] += 4 * int(np.ceil(xent / 32.0)) + 8
+        out["shannon"] += shannon / 8.0
+    return out
 
 
 def _dist_env():
@@ -445,12 +540,15 @@ def gpu_arm(args):
     # ratio, sizes and reconstruction error of this rank's layers (untimed)
     comp_bytes = 0
     err = {"err2_k": 0.0, "ref2_k": 0.0, "err2_v": 0.0, "ref2_v": 0.0}
+    ent = {"kvr2": 0, "single_stream": 0, "shannon": 0.0}
     for lay in layers:
         h = run_layer(*lay, keep=True)
         torch.cuda.synchronize()
         n = C.c_size_t()
         L.check(lib.kvf_compressed_size_bytes(h, C.byref(n)))
         comp_bytes += n.value
+        for k2, v2 in entropy_accounting(lib, L, K, h, dev).items():
+            ent[k2] += v2
         kf, vf = lay[1].float(), lay[2].float()
         err["err2_k"] += float(((ko - kf) ** 2).sum())
         err["ref2_k"] += float((kf ** 2).sum())
@@ -594,7 +692,8 @@ def gpu_arm(args):
 
     stats = {"layers": len(layers), "input_bytes": in_bytes, "compressed_bytes": comp_bytes,
              "original_bytes": orig_bytes, "ms": ms, "compress_ms": float(split_ms[0]),
-             "decompress_ms": float(split_ms[1]), **err}
+             "decompress_ms": float(split_ms[1]), **err, "ent_kvr2": ent["kvr2"],
+             "ent_single": ent["single_stream"], "ent_shannon": ent["shannon"]}
     per = gather_stats(stats, device=f"cuda:{dev}" if world > 1 else None)
     tot = reduce_stats(per)
     e2e_per = gather_stats({"ms": e2e_ms, "input_bytes": in_bytes, "original_bytes": orig_bytes},
@@ -646,6 +745,17 @@ def gpu_arm(args):
         "config": _config(args, w),
         "ratio": tot["original_bytes"] / tot["compressed_bytes"],
         "rel_err": {"keys": (tot["err2_k"] / tot["ref2_k"]) ** 0.5, "values": (tot["err2_v"] / tot["ref2_v"]) ** 0.5},
+        "entropy_coder": None if not tot["ent_kvr2"] else {
+            "kvr2_bytes": int(tot["ent_kvr2"]),
+            "single_stream_estimate_bytes": int(tot["ent_single"]),
+            "shannon_bound_bytes": float(tot["ent_shannon"]),
+            "ratio_single_stream": tot["original_bytes"] / (tot["compressed_bytes"] - tot["ent_kvr2"]
+                                                             + tot["ent_single"]),
+            "ratio_shannon_bound": tot["original_bytes"] / (tot["compressed_bytes"] - tot["ent_kvr2"]
+                                                             + tot["ent_shannon"]),
+            "note": "ratio with this library's chunked 32-lane rANS container (ratio) against the same layers with "
+                    "the codes in the reference's single serial stream (estimated from the codes' cross-entropy "
+                    "under its (f+1)-smoothed model) and at the order-0 Shannon bound"},
         # the job's bytes over the job's peak: one GPU's measured peak times the GPU count
         "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (step_ms / 1e3) / GB, "peak": peak * world,
                           "peak_per_gpu": peak, "frac": alg / (step_ms / 1e3) / GB / (peak * world),
@@ -905,7 +1015,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama3_8b_32k")
     ap.add_argument("--layers", type=int, default=0, help="number of layers (default: the workload's)")
-    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--e2e-threads", type=int, default=4, help="host threads (one stream each) for the e2e leg")
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

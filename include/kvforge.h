@@ -19,12 +19,24 @@
  *    function documents (sizes that must reach the host, and the one-off basis
  *    step, which runs its eigen-solve on the host).
  *  - One kvf_ctx per device. Calls on one context may come from several host
- *    threads at once, each issuing on its own stream; all scratch memory is
- *    taken per call from the context's stream-ordered pool, so calls on
- *    different streams share no scratch and never wait for one another. The
- *    context has one device status word: a device-side error (corrupt stream,
- *    expired wait) is reported by the next call that reads it, which may be
- *    another thread's.
+ *    threads at once, each issuing on its own stream; scratch memory is taken
+ *    per call from the context's stream-ordered pool, so calls on different
+ *    streams share no scratch and never wait for one another. The one
+ *    exception is kvf_calibrate_noalloc, whose calls all share one file-scope
+ *    device array (see its entry: calls of it that overlap on the GPU race).
+ *    The context has one device status word: a device-side error (corrupt
+ *    stream, expired wait) is reported by the next call that reads it, which
+ *    may be another thread's.
+ *  - A compressed layer (kvf_compressed) may be read on any stream:
+ *    kvf_decompress_layer and kvf_compressed_attention on a stream other than
+ *    the one that built the object first wait (stream-ordered, no host
+ *    synchronisation) until the object is complete, and kvf_compressed_free
+ *    returns its buffers to the pool only after the last read issued on every
+ *    stream before the free. The building stream (the `stream` of
+ *    kvf_compress_layer or kvf_compressed_deserialize) must outlive the
+ *    object, and the context must outlive every object made with it. The raw
+ *    device views of kvf_compressed_tensor_views carry no such ordering:
+ *    order their use after the building stream yourself.
  *  - Layout: tensors are [num_heads, seq_len, head_dim] row-major, as in the
  *    reference KVCache (crates/kvforge-core/src/types.rs:5-12).
  */

@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <deque>
+#include <exception>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -198,6 +199,24 @@ struct kvf_ctx {
   int profile = 0;
   std::vector<Rec> recs;
   std::vector<cudaEvent_t> spare;
+  // ordering events (no timing) of compressed objects, reused across objects
+  std::vector<cudaEvent_t> order_spare;
+  cudaError_t order_event(cudaEvent_t* out) {
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (!order_spare.empty()) {
+        *out = order_spare.back();
+        order_spare.pop_back();
+        return cudaSuccess;
+      }
+    }
+    return cudaEventCreateWithFlags(out, cudaEventDisableTiming);
+  }
+  // a waiter that was enqueued before the event goes back keeps the record it saw
+  void order_event_release(cudaEvent_t e) {
+    std::lock_guard<std::mutex> lock(mu);
+    order_spare.push_back(e);
+  }
   cudaEvent_t event() {
     std::lock_guard<std::mutex> lock(mu);
     if (!spare.empty()) {
@@ -248,6 +267,15 @@ struct kvf_compressed {
   TensorC key, value;
   float* d_scores = nullptr;
   std::vector<void*> owned;
+  // Cross-stream lifetime: `ready` is recorded on `stream` once the object's
+  // buffers are complete, and a reader on another stream waits for it first;
+  // each reader stream records its own event after its last use, and
+  // kvf_compressed_free makes `stream` wait for all of them before the
+  // buffers go back to the pool. Readers take a const object, so the use list
+  // is mutable and guarded.
+  cudaEvent_t ready = nullptr;
+  mutable std::mutex use_mu;
+  mutable std::vector<std::pair<cudaStream_t, cudaEvent_t>> uses;
 
   // owned buffers are allocated in the order of the stream that first uses
   // them (a layer's value tensor is built on the context's side stream)
@@ -287,7 +315,35 @@ kvf_status check_dtype(int in_dtype) {
 kvf_status check_shape(size_t H, size_t T, size_t D) {
   if (D > 1024) return fail(KVF_ERR_SHAPE_MISMATCH, "head_dim > 1024 is not supported");
   if (H > 65535) return fail(KVF_ERR_SHAPE_MISMATCH, "num_heads > 65535 is not supported");
-  if (H * T * D > (size_t(1) << 40)) return fail(KVF_ERR_SHAPE_MISMATCH, "tensor too large");
+  // H * D <= 2^26, so the division keeps the product check free of overflow
+  if (H && D && T > (size_t(1) << 40) / (H * D)) return fail(KVF_ERR_SHAPE_MISMATCH, "tensor too large");
+  return KVF_OK;
+}
+
+// a reader of `c` on stream `st`: waits for the object's buffers to be
+// complete when `st` is not the stream that built them
+kvf_status reader_enter(const kvf_compressed* c, cudaStream_t st) {
+  if (c->ready && st != c->stream) KVF_CUDA(cudaStreamWaitEvent(st, c->ready, 0));
+  return KVF_OK;
+}
+// ... and after its last use: records on `st` what kvf_compressed_free waits for
+kvf_status reader_leave(const kvf_compressed* c, cudaStream_t st) {
+  if (st == c->stream) return KVF_OK;
+  std::lock_guard<std::mutex> lock(c->use_mu);
+  cudaEvent_t ev = nullptr;
+  for (auto& u : c->uses)
+    if (u.first == st) ev = u.second;
+  if (!ev) {
+    KVF_CUDA(c->ctx->order_event(&ev));
+    c->uses.emplace_back(st, ev);
+  }
+  KVF_CUDA(cudaEventRecord(ev, st));
+  return KVF_OK;
+}
+// marks `c` complete on its own stream (end of compress / deserialize)
+kvf_status mark_ready(kvf_compressed* c) {
+  if (!c->ready) KVF_CUDA(c->ctx->order_event(&c->ready));
+  KVF_CUDA(cudaEventRecord(c->ready, c->stream));
   return KVF_OK;
 }
 
@@ -318,7 +374,7 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
 kvf_status rans_encode_into(kvf_ctx* ctx, Scratch& sc, const uint8_t* packed, size_t plen,
                             const uint32_t* freq, uint8_t* out, uint64_t* d_len, cudaStream_t st) {
   const size_t nc = rans_num_chunks(plen, kRansChunk);
-  unsigned long long* lookback = sc.get<unsigned long long>(nc);
+  unsigned long long* lookback = sc.get<unsigned long long>(nc + 1);  // status words + block ticket
   if (!lookback) return fail(KVF_ERR_CUDA, "scratch allocation failed");
   KVF_CUDA(launch_rans_encode(packed, plen, kRansChunk, freq, lookback, out, d_len, ctx->d_status, st));
   return KVF_OK;
@@ -764,9 +820,13 @@ kvf_status deser_tensor(kvf_compressed* c, TensorC& t, Reader& r, cudaStream_t s
     b->device = c->device;
     b->H = t.H; b->R = qc; b->D = t.D;
     if (r.v<uint64_t>() != t.H * qc * t.D) return bad("basis_vt length does not match [H, R, D]");
+    // sizes come from the wire: check them against the bytes left before
+    // allocating anything for them
+    if (!r.ok || t.H * qc * t.D > (r.len - r.pos) / 4) return bad("truncated basis_vt");
     b->vt.resize(t.H * qc * t.D);
     if (!r.get(b->vt.data(), b->vt.size() * 4)) return bad("truncated basis_vt");
     if (r.v<uint64_t>() != t.H) return bad("ranks length does not match num_heads");
+    if (!r.ok || t.H > (r.len - r.pos) / 8) return bad("truncated ranks");
     b->ranks.resize(t.H);
     if (!r.get(b->ranks.data(), t.H * 8)) return bad("truncated ranks");
     if (r.v<uint64_t>() != t.H || r.v<uint64_t>() != t.D) return bad("projection num_heads / head_dim mismatch");
@@ -881,6 +941,7 @@ kvf_status kvf_destroy(kvf_ctx* ctx) {
     cudaEventDestroy(r.b);
   }
   for (auto e : ctx->spare) cudaEventDestroy(e);
+  for (auto e : ctx->order_spare) cudaEventDestroy(e);
   for (auto& kv : ctx->sides) {
     cudaStreamSynchronize(kv.second.s);
     cudaStreamDestroy(kv.second.s);
@@ -1253,6 +1314,11 @@ kvf_status kvf_fused_dequant_attention(kvf_ctx* ctx, const uint8_t* k_codes, con
   return KVF_OK;
 }
 
+namespace {
+kvf_status compressed_attention_body(kvf_ctx* ctx, const kvf_compressed* c, const float* query, float scale,
+                                     float* out, cudaStream_t st);
+}  // namespace
+
 kvf_status kvf_compressed_attention(kvf_ctx* ctx, const kvf_compressed* c, const float* query, float scale,
                                     float* out, void* stream) {
   KVF_TRY(check_ctx(ctx));
@@ -1267,6 +1333,17 @@ kvf_status kvf_compressed_attention(kvf_ctx* ctx, const kvf_compressed* c, const
                           v.basis != nullptr));
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
+  KVF_TRY(reader_enter(c, st));
+  const kvf_status s = compressed_attention_body(ctx, c, query, scale, out, st);
+  const kvf_status ls = reader_leave(c, st);
+  return s != KVF_OK ? s : ls;
+}
+
+namespace {
+kvf_status compressed_attention_body(kvf_ctx* ctx, const kvf_compressed* c, const float* query, float scale,
+                                     float* out, cudaStream_t st) {
+  const TensorC& k = c->key;
+  const TensorC& v = c->value;
   Scratch sc(st, ctx->pool);
   // entropy-coded tensors are decoded into scratch (allocated on `st` before
   // the fork, freed on `st` after the join): keys on `st`, values on the
@@ -1303,6 +1380,7 @@ kvf_status kvf_compressed_attention(kvf_ctx* ctx, const kvf_compressed* c, const
                             c->D, k.qcols, v.qcols, scale, part, out, st));
   return KVF_OK;
 }
+}  // namespace
 
 // ---- basis ------------------------------------------------------------------
 kvf_status kvf_basis_compute(kvf_ctx* ctx, const void* data, int32_t in_dtype, size_t H, size_t T, size_t D,
@@ -1423,6 +1501,7 @@ kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values
     if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
   }
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
+  if (s == KVF_OK) s = mark_ready(c.get());
   if (s != KVF_OK) {
     std::string msg = g_err;
     kvf_compressed_free(c.release());
@@ -1439,6 +1518,7 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
   if (!c) return fail(KVF_ERR_INVALID_CONFIG, "null compressed object");
   DeviceGuard g(ctx->device);
   cudaStream_t st = S(stream);
+  KVF_TRY(reader_enter(c, st));
   kvf_ctx::Side* sd = nullptr;
   cudaStream_t vst = st;
   if (!small_layer(c->H, c->T, c->D)) {  // as in kvf_compress_layer
@@ -1455,7 +1535,8 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
     if (je == cudaSuccess) je = cudaStreamWaitEvent(st, sd->join, 0);
   }
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
-  return s;
+  const kvf_status ls = reader_leave(c, st);  // even after a failure: launched kernels may still read
+  return s != KVF_OK ? s : ls;
 }
 
 kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host, int32_t in_dtype,
@@ -1631,8 +1712,13 @@ kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf, size_t l
   c->D = r.v<uint64_t>();
   if (!r.ok) return fail(KVF_ERR_SERIALIZATION, "truncated header");
   if (check_shape(c->H, c->T, c->D) != KVF_OK) return fail(KVF_ERR_SERIALIZATION, "bad shape");
-  kvf_status s = deser_tensor(c.get(), c->key, r, c->stream);
-  if (s == KVF_OK) s = deser_tensor(c.get(), c->value, r, c->stream);
+  kvf_status s = KVF_OK;
+  try {  // no exception leaves the C ABI: a host allocation that fails is a serialisation error
+    s = deser_tensor(c.get(), c->key, r, c->stream);
+    if (s == KVF_OK) s = deser_tensor(c.get(), c->value, r, c->stream);
+  } catch (const std::exception& ex) {
+    s = fail(KVF_ERR_SERIALIZATION, std::string("deserialisation failed: ") + ex.what());
+  }
   if (s == KVF_OK) {
     c->original_size_bytes = r.v<uint64_t>();
     if (!r.ok) s = fail(KVF_ERR_SERIALIZATION, "truncated original_size_bytes");
@@ -1642,6 +1728,7 @@ kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf, size_t l
     cudaError_t e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(e));
   }
+  if (s == KVF_OK) s = mark_ready(c.get());
   if (s != KVF_OK) {
     std::string msg = g_err;
     kvf_compressed_free(c.release());
@@ -1656,6 +1743,13 @@ kvf_status kvf_compressed_free(kvf_compressed* c) {
   if (!c) return KVF_OK;
   {
     DeviceGuard g(c->device);
+    // the buffers go back to the pool on the building stream, after every
+    // reader stream's last recorded use
+    for (auto& u : c->uses) {
+      cudaStreamWaitEvent(c->stream, u.second, 0);
+      c->ctx->order_event_release(u.second);
+    }
+    if (c->ready) c->ctx->order_event_release(c->ready);
     for (void* p : c->owned) cudaFreeAsync(p, c->stream);
   }
   delete c;

@@ -267,7 +267,8 @@ cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t 
 // pairs in a file-scope device array; its address for `device` (current)
 constexpr size_t kCalibStaticSlots = 65536;
 cudaError_t calib_static_scratch(int device, double** out);
-cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t tiles, size_t T,
+// the partials are consumed: each head's first slot is overwritten
+cudaError_t launch_calib_finalize(double* calib_part, size_t H, size_t tiles, size_t T,
                                   size_t D, float* scores, cudaStream_t st);
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable), looked up once
 void* tensor_map_encode_fn();
@@ -293,7 +294,7 @@ cudaError_t launch_gram(const void* x, int in_dtype, size_t H, size_t T, size_t 
 // rANS (kvf_rans.cu)
 // encode and decode build the model from the 256 counts themselves
 // container of n symbols into out (capacity rans_max_len), its length into
-// out_len; lookback: one zeroed-here word per chunk
+// out_len; lookback: one zeroed-here word per chunk plus one (the block ticket)
 cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
                                unsigned long long* lookback, uint8_t* out, uint64_t* out_len, unsigned* status,
                                cudaStream_t st);

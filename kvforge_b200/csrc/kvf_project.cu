@@ -657,10 +657,12 @@ __global__ void __launch_bounds__(256) k_calib_partials(const TIn* __restrict__ 
 // (uniform 0.5 when the max is below 1e-12). One block; warp w sums the
 // partials of heads w, w + 8, ...: lane l adds every 32nd partial in order,
 // then a fixed shuffle tree combines the lanes, so the result does not depend
-// on scheduling.
-__global__ void __launch_bounds__(256) k_calib_finalize(const double* __restrict__ cpart, int H, int tiles,
-                                                        double n, float* __restrict__ scores) {
-  extern __shared__ double var[];
+// on scheduling. A head's variance is kept in its own first partial slot
+// (only the warp that read the head's partials writes there), so the kernel
+// needs no shared memory per head and takes any number of heads.
+__global__ void __launch_bounds__(256) k_calib_finalize(double* __restrict__ cpart, int H, int tiles, double n,
+                                                        float* __restrict__ scores) {
+  __shared__ double wmax[8];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int h = w; h < H; h += nw) {
     double s1 = 0.0, s2 = 0.0;
@@ -684,14 +686,26 @@ __global__ void __launch_bounds__(256) k_calib_finalize(const double* __restrict
     if (lane == 0) {
       const double mean = s1 / n;
       const double v = (s2 / n) - (mean * mean);
-      var[h] = (isnan(v) || v < 0.0) ? 0.0 : v;  // variance.max(0.0)
+      cpart[2 * (size_t)h * tiles] = (isnan(v) || v < 0.0) ? 0.0 : v;  // variance.max(0.0)
     }
   }
   __syncthreads();
   double m = 0.0;
-  for (int h = 0; h < H; ++h) m = var[h] > m ? var[h] : m;
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    const double v = cpart[2 * (size_t)h * tiles];
+    m = v > m ? v : m;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double u = __shfl_xor_sync(0xffffffffu, m, o);
+    m = u > m ? u : m;
+  }
+  if (lane == 0) wmax[w] = m;
+  __syncthreads();
+  m = 0.0;
+  for (int k = 0; k < nw; ++k) m = wmax[k] > m ? wmax[k] : m;
   for (int h = threadIdx.x; h < H; h += blockDim.x)
-    scores[h] = (m < 1e-12) ? 0.5f : (float)(var[h] / m);
+    scores[h] = (m < 1e-12) ? 0.5f : (float)(cpart[2 * (size_t)h * tiles] / m);
 }
 
 // ---- dequantize + reconstruct ------------------------------------------------
@@ -1166,12 +1180,10 @@ cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t 
   return cudaGetLastError();
 }
 
-cudaError_t launch_calib_finalize(const double* calib_part, size_t H, size_t tiles, size_t T,
+cudaError_t launch_calib_finalize(double* calib_part, size_t H, size_t tiles, size_t T,
                                   size_t D, float* scores, cudaStream_t st) {
   if (H == 0) return cudaSuccess;
-  const size_t smem = H * sizeof(double);
-  if (smem > kSmemOptIn) return cudaErrorInvalidValue;
-  k_calib_finalize<<<1, 256, smem, st>>>(calib_part, (int)H, (int)tiles, (double)(T * D), scores);
+  k_calib_finalize<<<1, 256, 0, st>>>(calib_part, (int)H, (int)tiles, (double)(T * D), scores);
   note_launches(1);
   return cudaGetLastError();
 }

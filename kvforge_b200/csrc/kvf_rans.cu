@@ -201,10 +201,12 @@ __host__ __device__ inline size_t enc_warp_smem(uint32_t chunk) {
 // chunk (zeroed before the launch): flag in the top two bits (1: the chunk's
 // payload size, 2: the inclusive prefix of payload sizes), value below. A warp
 // publishes its size, then reads its predecessors' words 32 at a time, adding
-// sizes back to the nearest published prefix. Predecessors of a chunk belong
-// to earlier or the same block, and blocks start in index order, so the wait
-// ends; it is bounded all the same, and a warp that gives up reports a device
-// timeout instead of writing.
+// sizes back to the nearest published prefix. A block takes its chunks from
+// a ticket counter (one more zeroed word after the status words) when it
+// starts, so the predecessors of a chunk belong to the same block or to a
+// block that started earlier and is running or done: the wait ends whatever
+// order the hardware dispatches blocks in. It is bounded all the same, and a
+// warp that gives up reports a device timeout instead of writing.
 constexpr unsigned long long kLbSize = 1ull << 62, kLbPrefix = 2ull << 62, kLbValue = (1ull << 62) - 1;
 constexpr uint32_t kLbSpinLimit = 1u << 16;
 
@@ -267,8 +269,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(const uint8_t* _
   __shared__ uint32_t q[256], cum[256];
   __shared__ uint4 mdl[256];  // per symbol: {threshold - 1, reciprocal, q, (M - q) | cum << 16}
   __shared__ ModelSmem ms;
+  __shared__ unsigned long long ticket;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t c = (uint64_t)blockIdx.x * kEncWarps + w;
+  if (threadIdx.x == 0) ticket = atomicAdd(lb + nchunks, 1ull);  // blocks in the order they started
+  __syncthreads();
+  const uint64_t c = (uint64_t)ticket * kEncWarps + w;
   const bool live = c < nchunks;
   const uint64_t start = live ? c * chunk : 0;
   const uint32_t nsym = live ? (uint32_t)((n - start < chunk) ? (n - start) : chunk) : 0;
@@ -580,7 +585,7 @@ cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, co
     cudaError_t e = cudaFuncSetAttribute(k_rans_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  cudaError_t e = cudaMemsetAsync(lookback, 0, nc * sizeof(unsigned long long), st);
+  cudaError_t e = cudaMemsetAsync(lookback, 0, (nc + 1) * sizeof(unsigned long long), st);  // + the ticket
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((nc + kEncWarps - 1) / kEncWarps);
   k_rans_encode<<<grid, kEncWarps * 32, smem, st>>>(data, n, chunk, freq, lookback, out, out_len, nc, status);

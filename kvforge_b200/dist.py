@@ -8,7 +8,7 @@ squared error, reference energy, times), over NCCL on GPUs or gloo on CPUs.
 from __future__ import annotations
 
 STAT_KEYS = ("layers", "input_bytes", "compressed_bytes", "original_bytes", "err2_k", "ref2_k", "err2_v",
-             "ref2_v", "ms", "compress_ms", "decompress_ms")
+             "ref2_v", "ms", "compress_ms", "decompress_ms", "ent_kvr2", "ent_single", "ent_shannon")
 TIME_KEYS = ("ms", "compress_ms", "decompress_ms")
 
 

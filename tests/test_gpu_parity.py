@@ -144,6 +144,17 @@ def test_calibrate_parity(kvf, oracle, shape, f16):
     assert e.value.status == 2
 
 
+def test_calibrate_many_heads(kvf, oracle):
+    """More heads than one block's shared memory could hold as doubles
+    (6000 x 8 B > 40 KB): the per-head variances live in the partial slots."""
+    xin, x32 = _x((6000, 64, 8), 12, True)
+    x32 = x32 * np.linspace(0.1, 3.0, 6000, dtype=np.float32)[:, None, None]
+    xin = x32.astype(np.float16)
+    s = host(kvf.GpuSensitivityCalibrator().calibrate(dev(xin)))
+    so = oracle.calibrate(xin.astype(np.float32))
+    assert np.allclose(s, so, rtol=1e-6, atol=1e-7)
+
+
 # ---- projection ------------------------------------------------------------------
 def _basis(oracle, x32, thr, max_rank=None):
     bf, sv = oracle.compute_basis(x32, threads=4)
@@ -510,6 +521,74 @@ def test_serialize_is_reference_wire_format(kvf, oracle, preset):
     with pytest.raises(kvf.KvForgeError) as e:
         kvf.CompressedKV.from_bytes(bytes(bad))
     assert e.value.status == 6
+
+
+def test_deserialize_rejects_lengths_beyond_the_buffer(kvf):
+    """A few-byte layer whose header claims a huge basis (H = 65535, R = D =
+    1024: 275 GB of basis_vt) is a serialisation error, not a host allocation
+    of that size; so is a rank list longer than the bytes that remain."""
+    import struct
+    H, T, D, R = 65535, 1, 1024, 1024
+    u64 = lambda *v: struct.pack("<" + "Q" * len(v), *v)
+    head = u64(0, H, T, D)
+    tensor = (u64(0)            # quantized_data: empty
+              + u64(0) + u64(0)  # scales, mins: empty
+              + struct.pack("<II", INT4, PC) + u64(3, H, T, R)
+              + b"\x01" + u64(H * R * D))  # projection_state: Some, basis_vt length
+    with pytest.raises(kvf.KvForgeError) as e:
+        kvf.CompressedKV.from_bytes(head + tensor + b"\x00" * 64)
+    assert e.value.status == 6
+    H, D, R = 2, 4, 1
+    head = u64(0, H, T, D)
+    tensor = (u64(0) + u64(0) + u64(0) + struct.pack("<II", INT4, PC) + u64(3, H, T, R)
+              + b"\x01" + u64(H * R * D) + b"\x00" * (4 * H * R * D)
+              + u64(H))  # ranks: H entries claimed, none present
+    with pytest.raises(kvf.KvForgeError) as e:
+        kvf.CompressedKV.from_bytes(head + tensor)
+    assert e.value.status == 6
+
+
+def test_compress_decompress_free_across_streams(kvf):
+    """Compress on stream A, decompress on stream B with no host
+    synchronisation in between, free at once, and let stream A compress other
+    layers that may take the freed buffers from the pool: B's output is
+    bit-identical to a same-stream decompression of the same layer."""
+    from kvforge_b200 import _lib as L
+    from kvforge_b200 import synth
+    lib, ctx = L.lib(), L.context(0)
+    cfg = kvf.config_from_preset("aggressive")
+    k, v = synth.workload_layer("llama3_8b_32k", 3, backend="torch")
+    k, v = k[:, :8192].contiguous(), v[:, :8192].contiguous()
+    H, T, D = k.shape
+    kb = kvf.Basis.compute(k, cfg.projection_variance_threshold)
+    vb = kvf.Basis.compute(v, cfg.projection_variance_threshold)
+    ref = kvf.CompressionPipeline().compress(kvf.KVCache(k, v, 0), "aggressive", kb, vb)
+    ref_out = kvf.decompress(ref)
+    sa, sb = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for rep in range(3):
+        ko = torch.empty((H, T, D), dtype=torch.float32, device="cuda")
+        vo = torch.empty_like(ko)
+        torch.cuda.synchronize()
+        h = C.c_void_p()
+        L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), L.IN_F16, H, T, D,
+                                       rep, C.byref(cfg), kb.handle, vb.handle, C.byref(h),
+                                       C.c_void_p(sa.cuda_stream)))
+        L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()),
+                                         C.c_void_p(sb.cuda_stream)))
+        L.check(lib.kvf_compressed_free(h))
+        for j in range(2):  # new objects on A reuse the pool's blocks once the free is ordered
+            h2 = C.c_void_p()
+            L.check(lib.kvf_compress_layer(ctx, C.c_void_p(v.data_ptr()), C.c_void_p(k.data_ptr()), L.IN_F16, H, T,
+                                           D, j, C.byref(cfg), vb.handle, kb.handle, C.byref(h2),
+                                           C.c_void_p(sa.cuda_stream)))
+            L.check(lib.kvf_compressed_free(h2))
+        outs.append((ko, vo))
+    torch.cuda.synchronize()
+    L.check(lib.kvf_sync(ctx, None))
+    for ko, vo in outs:
+        assert np.array_equal(ko.cpu().numpy(), ref_out.keys())
+        assert np.array_equal(vo.cpu().numpy(), ref_out.values())
 
 
 def test_host_buffer_entry_points(kvf):

@@ -55,6 +55,27 @@ def test_calibrate_noalloc_matches_allocating_entry_point():
     assert np.allclose(got_s.cpu().numpy(), ref_s.cpu().numpy(), rtol=1e-6, atol=1e-7)
 
 
+def test_calibrate_noalloc_many_heads():
+    """6000 heads: the finishing step keeps each head's variance in the
+    static scratch itself, so the head count is bounded only by the slots."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from kvforge_b200 import _lib as L
+    lib, ctx = L.lib(), L.context(0)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rng = np.random.default_rng(78)
+    H, T, D = 6000, 64, 8
+    x = (rng.standard_normal((H, T, D)) * np.linspace(0.5, 2.0, H)[:, None, None]).astype(np.float16)
+    xt = torch.from_numpy(x).cuda()
+    st, ref = _calibrate(lib, ctx, "kvf_calibrate", xt, H, T, D, stream)
+    L.check(st)
+    for _ in range(2):
+        st, got = _calibrate(lib, ctx, "kvf_calibrate_noalloc", xt, H, T, D, stream)
+        L.check(st)
+        torch.cuda.synchronize()
+        assert np.allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=1e-6, atol=1e-7)
+
+
 def test_calibrate_noalloc_rejects_sizes_beyond_its_scratch():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
