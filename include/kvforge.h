@@ -118,6 +118,20 @@ kvf_status kvf_set_exact_reconstruct(kvf_ctx* ctx, int exact);
  * AUTO (default): CUDA cores up to 16 coefficients, tensor cores above. */
 typedef enum { KVF_RECON_AUTO = 0, KVF_RECON_CUDA_CORE = 1, KVF_RECON_TENSOR_CORE = 2 } kvf_recon_engine;
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine);
+/* engine of the projection inside quantization (the pipeline's value path,
+ * kvf_fused_project_quantize with per-token axis; kvf_project always runs the
+ * CUDA-core chain and returns its coefficients):
+ * CUDA_CORE / AUTO (default): each coefficient as one fused multiply-add
+ *   chain over the channels in the reference's order (up to 32 coefficients
+ *   fused with the quantization, beyond that a separate quantization pass);
+ * TENSOR_CORE: for f16 input, head_dim 128 and up to 64 coefficients, a
+ *   tcgen05 GEMM computes every coefficient with a bounded error, and the
+ *   coefficients that decide a code (each row's minimum and maximum, and any
+ *   value within that bound of a rounding boundary) are recomputed with the
+ *   exact chain, so codes, scales and mins are identical to the CUDA-core
+ *   engine's; other shapes use the CUDA-core engine. */
+typedef enum { KVF_PROJ_AUTO = 0, KVF_PROJ_CUDA_CORE = 1, KVF_PROJ_TENSOR_CORE = 2 } kvf_proj_engine;
+kvf_status kvf_set_projection_engine(kvf_ctx* ctx, int engine);
 /* Runs one of the library's bounded device waits against a barrier or status
  * word that nothing completes, with a 2 ms limit: the wait gives up and the
  * next kvf_sync on `stream` reports KVF_ERR_DEVICE_TIMEOUT, after which the

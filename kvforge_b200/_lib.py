@@ -36,6 +36,7 @@ PER_CHANNEL, PER_TOKEN = 0, 1
 IN_F32, IN_F16 = 0, 1
 CONSERVATIVE, BALANCED, AGGRESSIVE, ADAPTIVE = 0, 1, 2, 3
 RECON_AUTO, RECON_CUDA_CORE, RECON_TENSOR_CORE = 0, 1, 2
+PROJ_AUTO, PROJ_CUDA_CORE, PROJ_TENSOR_CORE = 0, 1, 2
 WAIT_MBARRIER, WAIT_LOOKBACK = 0, 1
 
 # every symbol include/kvforge.h declares
@@ -54,6 +55,7 @@ EXPORTS = [
     "kvf_compressed_deserialize", "kvf_compressed_free",
     "kvf_bandwidth_bytes_per_us", "kvf_cost_measure", "kvf_cost_estimate", "kvf_cost_select",
     "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read", "kvf_calibrate_noalloc",
+    "kvf_set_projection_engine",
 ]
 
 NUM_STAGES = 8
@@ -120,6 +122,7 @@ def _declare(L):
         "kvf_abi_version": (C.c_int, []),
         "kvf_set_exact_reconstruct": (st, [p, C.c_int]),
         "kvf_set_reconstruct_engine": (st, [p, C.c_int]),
+        "kvf_set_projection_engine": (st, [p, C.c_int]),
         "kvf_selftest_wait_timeout": (st, [p, C.c_int, p]),
         "kvf_sync": (st, [p, p]),
         "kvf_pipeline_config_from_preset": (st, [i32, C.POINTER(PipelineConfig)]),

@@ -156,6 +156,7 @@ struct kvf_ctx {
   int device = 0;
   int exact_reconstruct = 0;
   int recon_engine = KVF_RECON_AUTO;
+  int proj_engine = KVF_PROJ_AUTO;
   unsigned* d_status = nullptr;
   // the context's own stream-ordered pool: freed blocks stay cached, and a
   // block freed on one stream is reused on another only once its free has
@@ -347,6 +348,27 @@ kvf_status mark_ready(kvf_compressed* c) {
   return KVF_OK;
 }
 
+// per-token projection + quantization (ProjectOut mode 2) on the tensor-core
+// engine when the context allows it and the shape fits, on CUDA cores
+// otherwise (R <= 32 there); both give identical codes, scales and mins
+bool token_tc(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, size_t T, size_t D, const float* bvt, size_t R) {
+  return ctx->proj_engine == KVF_PROJ_TENSOR_CORE && project_tc_fits(x, in_dtype, H, T, D, bvt, R);
+}
+cudaError_t project_token(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, size_t T, size_t D,
+                          const float* bvt, const uint64_t* ranks, size_t R, const ProjectOut& po, cudaStream_t st) {
+  if (token_tc(ctx, x, in_dtype, H, T, D, bvt, R)) {
+    const cudaError_t e = launch_project_tc(x, in_dtype, H, T, D, bvt, ranks, R, po, st);
+    if (e != cudaErrorNotSupported || R > 32) return e;
+  }
+  return launch_project(x, in_dtype, H, T, D, bvt, ranks, R, po, st);
+}
+// INT4 codes are packed inside the projection kernel when each row's codes
+// start on a byte (R even); the CUDA-core kernel also packs pairs that run
+// across rows when every 256-token tile starts on a byte (T even)
+bool token_fuse_pack(bool tc, int dt, size_t R, size_t T) {
+  return dt == KVF_INT4 && (R % 2 == 0 || (!tc && T % 2 == 0));
+}
+
 // quantize (from f32/f16 input) into `packed`, optional histogram of the packed bytes
 kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t T, size_t D, int dt,
                          int axis, uint8_t* packed, float* scales, float* mins, uint32_t* hist,
@@ -465,10 +487,8 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
       StageTimer tm(ctx, KVF_STAGE_QUANTIZE, 4.0 * n + (double)plen + 8.0 * np, st);
       KVF_CUDA(launch_quantpack_channel(P, H, T, qcols, po.kmin, po.kmax, dt, out->d_scales, out->d_mins, packed,
                                         hist, st));
-    } else if (qcols <= 32) {
-      // INT4 bytes are packed inside the projection kernel when every
-      // 128-token tile starts at an even flat index (R or T even)
-      const bool fuse_pack = dt == KVF_INT4 && (qcols % 2 == 0 || T % 2 == 0);
+    } else if (qcols <= 32 || token_tc(ctx, x, in_dtype, H, T, D, basis->d_vt, qcols)) {
+      const bool fuse_pack = token_fuse_pack(token_tc(ctx, x, in_dtype, H, T, D, basis->d_vt, qcols), dt, qcols, T);
       uint8_t* codes = (dt == KVF_INT8) ? packed : (fuse_pack ? nullptr : sc.get<uint8_t>(n));
       if (dt == KVF_INT4 && !fuse_pack && !codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
       po.mode = 2;
@@ -479,7 +499,7 @@ kvf_status compress_tensor(kvf_ctx* ctx, kvf_compressed* owner, const void* x, i
       po.mins = out->d_mins;
       {
         StageTimer tm(ctx, KVF_STAGE_PROJECT, (double)in_bytes + (double)plen + 8.0 * np, st);
-        KVF_CUDA(launch_project(x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
+        KVF_CUDA(project_token(ctx, x, in_dtype, H, T, D, basis->d_vt, basis->d_ranks, qcols, po, st));
       }
       if (dt == KVF_INT4 && !fuse_pack) {
         StageTimer tm(ctx, KVF_STAGE_QUANTIZE, (double)n + (double)plen, st);
@@ -980,6 +1000,13 @@ kvf_status kvf_selftest_wait_timeout(kvf_ctx* ctx, int which, void* stream) {
   return KVF_OK;
 }
 
+kvf_status kvf_set_projection_engine(kvf_ctx* ctx, int engine) {
+  KVF_TRY(check_ctx(ctx));
+  if (engine < KVF_PROJ_AUTO || engine > KVF_PROJ_TENSOR_CORE) return fail(KVF_ERR_INVALID_CONFIG, "unknown projection engine");
+  ctx->proj_engine = engine;
+  return KVF_OK;
+}
+
 kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine) {
   KVF_TRY(check_ctx(ctx));
   if (engine != KVF_RECON_AUTO && engine != KVF_RECON_CUDA_CORE && engine != KVF_RECON_TENSOR_CORE)
@@ -1192,8 +1219,8 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
     KVF_CUDA(launch_quantpack_channel(P, H, T, R, po.kmin, po.kmax, data_type, scales, mins, packed, nullptr, st));
     return KVF_OK;
   }
-  if (R <= 32) {
-    const bool fuse_pack = data_type == KVF_INT4 && (R % 2 == 0 || T % 2 == 0);
+  if (R <= 32 || token_tc(ctx, data, in_dtype, H, T, D, basis_vt, R)) {
+    const bool fuse_pack = token_fuse_pack(token_tc(ctx, data, in_dtype, H, T, D, basis_vt, R), data_type, R, T);
     uint8_t* codes = (data_type == KVF_INT8) ? packed : (fuse_pack ? nullptr : sc.get<uint8_t>(n));
     if (data_type == KVF_INT4 && !fuse_pack && !codes) return fail(KVF_ERR_CUDA, "scratch allocation failed");
     po.mode = 2;
@@ -1201,7 +1228,7 @@ kvf_status kvf_fused_project_quantize(kvf_ctx* ctx, const void* data, int32_t in
     po.packed = fuse_pack ? packed : nullptr;
     po.scales = scales;
     po.mins = mins;
-    KVF_CUDA(launch_project(data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
+    KVF_CUDA(project_token(ctx, data, in_dtype, H, T, D, basis_vt, ranks, R, po, st));
     if (data_type == KVF_INT4 && !fuse_pack) KVF_CUDA(launch_pack_int4(codes, n, packed, nullptr, st));
     return KVF_OK;
   }
