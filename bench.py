@@ -441,7 +441,7 @@ def _config(args, w):
             "heads": w["H"], "tokens": w["T"], "head_dim": w["D"], "input_dtype": w["dtype"],
             "output_dtype": "f32", "basis": "calibrated per layer, computed before the timed region",
             "l2": "inputs larger than L2 (no flush)", "parallelism": f"layer-sharded x{args.gpus}",
-            "streams_per_gpu": getattr(args, "streams", 1)}
+            "streams_per_gpu": getattr(args, "streams", 1), "order": getattr(args, "order", "interleaved")}
 
 
 # ---------------------------------------------------------------------------
@@ -529,8 +529,18 @@ def gpu_arm(args):
 
     def step():
         fork()
-        for i, lay in enumerate(layers):
-            run_layer(*lay, wi=i % nstreams)
+        if args.order == "phased":
+            # every layer's compression is issued before any decompression:
+            # with few layers per stream the rANS coders of one layer no longer
+            # wait behind another layer's reconstruction
+            hs = [compress(*lay, wi=i % nstreams) for i, lay in enumerate(layers)]
+            for i, h in enumerate(hs):
+                decompress(h, wi=i % nstreams)
+            for h in hs:
+                lib.kvf_compressed_free(h)
+        else:
+            for i, lay in enumerate(layers):
+                run_layer(*lay, wi=i % nstreams)
         join()
 
     for _ in range(args.warmup):
@@ -1018,6 +1028,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--e2e-threads", type=int, default=4, help="host threads (one stream each) for the e2e leg")
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
+    ap.add_argument("--order", default="interleaved", choices=["interleaved", "phased"],
+                    help="per layer compress then decompress, or all compressions then all decompressions")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--recon-engine", default="auto", choices=["auto", "cuda", "tc"],

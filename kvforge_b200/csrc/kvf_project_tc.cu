@@ -64,11 +64,17 @@ constexpr int kRows = 128;                       // tokens per tile: MMA M, TMEM
 constexpr int kD = 128;                          // head_dim: MMA K
 constexpr int kTileBytes = kRows * kD * 2;       // one f16 tile
 constexpr int kRegionBytes = kTileBytes / 2;     // 64 channels x 128 rows (one 128-byte swizzle span)
-constexpr int kStages = 4;
-constexpr int kGroups = 2;                       // epilogue groups
-constexpr int kAcc = 2 * kGroups;                // accumulator slots
-constexpr int kEpiWarps = 4 * kGroups;
-constexpr int kThreads = 32 * (2 + kEpiWarps);
+// per coefficient width: epilogue groups of four warps (alternating tiles),
+// token-tile stages and TMEM accumulator slots, sized to the shared memory
+// and the 512 TMEM columns
+template <int RG>
+struct PtCfg {
+  static constexpr int kGroups = 3;
+  static constexpr int kStages = RG <= 16 ? 5 : 4;
+  static constexpr int kAcc = RG <= 32 ? 6 : 4;
+  static constexpr int kEpiWarps = 4 * kGroups;
+  static constexpr int kThreads = 32 * (2 + kEpiWarps);
+};
 constexpr float kLoScale = 2048.0f;              // lo = f16((v - hi) * 2^11)
 constexpr float kLoInv = 1.0f / 2048.0f;
 constexpr float kTcRelF = 1.0f / 8192.0f;        // bound of the MMA's accumulation error / sum |products|
@@ -142,17 +148,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                : "r"(taddr));
 }
-// the thread's 8 coefficients r0 .. r0 + 7: hi at column r0, lo at column RG + r0
-template <int RG>
-__device__ __forceinline__ void load_coeffs(uint32_t tacc, int r0, float* q) {
-  uint32_t hv[8], lv[8];
-  tmem_ld8(tacc + (uint32_t)r0, hv);
-  tmem_ld8(tacc + (uint32_t)(RG + r0), lv);
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int k = 0; k < 8; ++k) q[k] = __fmaf_rn(__uint_as_float(lv[k]), kLoInv, __uint_as_float(hv[k]));
-}
-
 __device__ __forceinline__ void unpack_h8(const uint4& u, float* o) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -175,7 +170,7 @@ __device__ __forceinline__ uint4 x_chunk(const uint8_t* xrow, int swz, int j) {
 __device__ __noinline__ float3 exact2_norm(const uint8_t* x, int sw, const float* va, const float* vb) {
   float pa = 0.0f, pb = 0.0f;
   unsigned long long ss2 = 0ull;
-#pragma unroll 4
+#pragma unroll 2
   for (int j = 0; j < 16; ++j) {
     const uint4 u = x_chunk(x, sw, j);
     const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
@@ -227,19 +222,29 @@ __device__ __noinline__ float2 exact2_glb(const __half* __restrict__ x, const fl
   return make_float2(pa, pb);
 }
 
-// replaces coefficient `r` (a run-time index) of the register array
+// replaces coefficient `r` (a run-time index) of the register array: one
+// predicated select per element, written out so that the array stays in
+// registers (a compare-and-assign loop compiles to an indexed access)
 template <int RG>
 __device__ __forceinline__ void set_at(float* P, int r, float v) {
 #pragma unroll
   for (int k = 0; k < RG; ++k)
-    if (k == r) P[k] = v;
+    asm("{\n .reg .pred p;\n setp.eq.s32 p, %1, %2;\n selp.f32 %0, %3, %0, p;\n}" : "+f"(P[k]) : "r"(r), "r"(k), "f"(v));
 }
 
 // one quantized row out: scale and min, then the codes (INT4 bytes packed
 // within the row, R even; or one byte per code), counted in the histogram
+struct RowOut {  // where quantized rows go (the ProjectOut fields the epilogue writes)
+  float* scales;
+  float* mins;
+  uint8_t* packed;
+  uint8_t* codes;
+  float levels;
+};
+
 template <int RG>
 __device__ __forceinline__ void write_row(const uint32_t* cd, size_t grow, int R, float scale, float mn,
-                                          const ProjectOut& o, uint32_t* shist, bool hist_on) {
+                                          const RowOut& o, uint32_t* shist, bool hist_on) {
   o.scales[grow] = scale;
   o.mins[grow] = mn;
   if (o.packed) {
@@ -267,7 +272,9 @@ __device__ __forceinline__ void write_row(const uint32_t* cd, size_t grow, int R
 template <int RG>
 __device__ __noinline__ void finish_row(const __half* __restrict__ x, size_t grow, int T, int R,
                                         const float* __restrict__ bvt, const uint64_t* __restrict__ ranks,
-                                        const ProjectOut& o, uint32_t* shist, bool hist_on) {
+                                        float* scales, float* mins, uint8_t* packed, uint8_t* codes, float levels,
+                                        uint32_t* shist, bool hist_on) {
+  const RowOut o{scales, mins, packed, codes, levels};
   const int h = (int)(grow / (size_t)T);
   const uint64_t rk = ranks[h];
   const int rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
@@ -295,9 +302,11 @@ __device__ __noinline__ void finish_row(const __half* __restrict__ x, size_t gro
 }
 
 template <int RG>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
     k_project_tc(const __grid_constant__ CUtensorMap xmap, const __half* __restrict__ x, int H, int T,
                  const float* __restrict__ bvt, const uint64_t* __restrict__ ranks, int R, PtLayout L, ProjectOut o) {
+  constexpr int kStages = PtCfg<RG>::kStages, kAcc = PtCfg<RG>::kAcc, kGroups = PtCfg<RG>::kGroups;
+  constexpr int kEpiWarps = PtCfg<RG>::kEpiWarps;
   constexpr int N = 2 * RG;                 // MMA N: RG hi columns, then RG lo columns
   constexpr int kSlotBytes = 2 * N * 128;   // two K regions of N rows x 128 B
   constexpr uint32_t kTmemCols = (kAcc * N <= 32) ? 32 : (kAcc * N <= 64) ? 64 : (kAcc * N <= 128) ? 128
@@ -535,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = 32 * q + lane;     // the thread's token row in a tile
     const int swz = row & 7;
     const float levels = o.levels;
+    const RowOut ro{o.scales, o.mins, o.packed, o.codes, o.levels};
     for (int n = g; n < nit; n += kGroups) {
       const long long it = i0 + n;
       const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
@@ -552,23 +562,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t tacc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * N);
       const int rank = info[b].rank;
+      // coefficients: Q = hi + lo * 2^-11, columns from the rank on +0.0
+      // exactly (projection.rs:96); every loop below is branch-free over RG
+      // columns, with the columns from R on masked
       float P[RG];
+      {
+        constexpr int kC = RG < 32 ? RG : 32;  // columns per TMEM wait
 #pragma unroll
-      for (int r0 = 0; r0 < RG; r0 += 8) load_coeffs<RG>(tacc, r0, P + r0);
+        for (int c0 = 0; c0 < RG; c0 += kC) {
+          uint32_t hv[kC], lv[kC];
+#pragma unroll
+          for (int r0 = 0; r0 < kC; r0 += 8) {
+            tmem_ld8(tacc + (uint32_t)(c0 + r0), hv + r0);
+            tmem_ld8(tacc + (uint32_t)(RG + c0 + r0), lv + r0);
+          }
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int k = 0; k < kC; ++k) {
+            const float v = __fmaf_rn(__uint_as_float(lv[k]), kLoInv, __uint_as_float(hv[k]));
+            P[c0 + k] = (c0 + k < rank) ? v : 0.0f;
+          }
+        }
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
-      // the smallest and largest approximate coefficients (columns from the
-      // rank on are +0.0 exactly, projection.rs:96)
+      // the smallest and largest approximate coefficients
       int rA = 0, rB = 0;
-      float qa = INFINITY, qb = -INFINITY;
+      float qa = P[0], qb = P[0];
 #pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        if (r >= rank) P[r] = 0.0f;
-        if (r < R) {
-          if (P[r] < qa) { qa = P[r]; rA = r; }
-          if (P[r] > qb) { qb = P[r]; rB = r; }
-        }
+      for (int r = 1; r < RG; ++r) {
+        const bool lt = r < R && P[r] < qa, gt = r < R && P[r] > qb;
+        qa = lt ? P[r] : qa;
+        rA = lt ? r : rA;
+        qb = gt ? P[r] : qb;
+        rB = gt ? r : rB;
       }
       const uint8_t* xrow = xs + (size_t)s * kTileBytes + row * 128;
       const float* B = bf + (size_t)b * RG * kBStride;
@@ -578,46 +606,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool defer = info[b].exact_only || !(xn <= 3.0e38f);
       set_at<RG>(P, rA, e.x);
       set_at<RG>(P, rB, e.y);
+      // Delta_r of the coefficients still approximate (0 for the exact ones);
+      // no other coefficient may lie below the exact minimum or above the
+      // exact maximum
       const float* bn = info[b].bn;
-      // Delta_r of the coefficients still approximate (0 for the exact ones)
-      auto delta = [&](int r, float p) {
-        return (r == rA || r == rB || r >= rank) ? 0.0f
-                                                 : __fmaf_ru(xn, bn[r], __fmul_ru(fabsf(p), 1.0f / 4194304.0f));
+      auto delta = [&](int r) {
+        const bool exact = r == rA || r == rB || r >= rank;
+        return exact ? 0.0f : __fmaf_ru(xn, bn[r], __fmul_ru(fabsf(P[r]), 1.0f / 4194304.0f));
       };
-      // no other coefficient can lie below the exact minimum or above the exact maximum
 #pragma unroll
-      for (int r = 0; r < RG; ++r)
-        if (r < R) {
-          const float d = delta(r, P[r]);
-          if ((r != rA && __fsub_rd(P[r], d) < e.x) || (r != rB && __fadd_ru(P[r], d) > e.y)) defer = true;
-        }
+      for (int r = 0; r < RG; ++r) {
+        const float d = delta(r);
+        const bool below = r != rA && __fsub_rd(P[r], d) < e.x;
+        const bool above = r != rB && __fadd_ru(P[r], d) > e.y;
+        defer = defer || (r < R && (below || above));
+      }
       const float mn = __fadd_rn(e.x, 0.0f), mx = __fadd_rn(e.y, 0.0f);  // -0.0 as +0.0, as mm_update
       const float scale = make_scale(mn, mx, levels);
       const float inv = __frcp_rn(scale);
       // codes; one whose value interval reaches within the margin of a
       // rounding boundary (a half-integer of the quotient) defers the row
+      const float invm = __fmul_ru(inv, 1.001f);
       uint32_t cd[RG];
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
-        cd[r] = 0u;
-        if (r < R) {
-          const float z = __fmul_rn(__fsub_rn(P[r], mn), inv);
-          const float tz = __fadd_rn(z, 0.5f);
-          const float fl = floorf(tz);
-          const float fr = __fsub_rn(tz, fl);
-          const float m = __fmaf_ru(delta(r, P[r]), __fmul_ru(inv, 1.001f),
-                                    __fmaf_ru(fabsf(z), 1.0f / 524288.0f, 1.0f / 262144.0f));
-          if (fr < m || fr > 1.0f - m) defer = true;
-          cd[r] = (uint32_t)fminf(fmaxf(fl, 0.0f), levels);
-        }
+        const float z = __fmul_rn(__fsub_rn(P[r], mn), inv);
+        const float tz = __fadd_rn(z, 0.5f);
+        const float fl = floorf(tz);
+        const float fr = __fsub_rn(tz, fl);
+        const float m = __fmaf_ru(delta(r), invm, __fmaf_ru(fabsf(z), 1.0f / 524288.0f, 1.0f / 262144.0f));
+        defer = defer || (r < R && (fr < m || fr > 1.0f - m));
+        cd[r] = (uint32_t)fminf(fmaxf(fl, 0.0f), levels);
       }
       if (ok) {
         if (!defer) {
-          write_row<RG>(cd, grow, R, scale, mn, o, shist, hist_on);
+          write_row<RG>(cd, grow, R, scale, mn, ro, shist, hist_on);
         } else {
           const int slot = atomicAdd(dcount, 1);
           if (slot < kDefCap) dlist[slot] = (uint32_t)grow;
-          else finish_row<RG>(x, grow, T, R, bvt, ranks, o, shist, hist_on);  // list full: now
+          else finish_row<RG>(x, grow, T, R, bvt, ranks, ro.scales, ro.mins, ro.packed, ro.codes, ro.levels, shist,
+                              hist_on);  // list full: now
         }
       }
       __syncwarp();  // every lane is done with the stage and the slot
@@ -633,7 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!*abort_flag) {
       const int nd = min(*reinterpret_cast<volatile int*>(dcount), kDefCap);
       for (int i = tid - 64; i < nd; i += kEpiWarps * 32)
-        finish_row<RG>(x, (size_t)dlist[i], T, R, bvt, ranks, o, shist, hist_on);
+        finish_row<RG>(x, (size_t)dlist[i], T, R, bvt, ranks, ro.scales, ro.mins, ro.packed, ro.codes, ro.levels,
+                       shist, hist_on);
     }
   }
   if (timed_out) {
@@ -651,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int RG>
 constexpr PtLayout pt_layout() {
+  constexpr int kStages = PtCfg<RG>::kStages, kAcc = PtCfg<RG>::kAcc;
   PtLayout L{};
   int off = 0;
   L.xs = off;
@@ -709,7 +739,7 @@ cudaError_t launch_tc_rg(const CUtensorMap& map, const __half* x, size_t H, size
   }
   const size_t items = H * ((T + kRows - 1) / kRows);
   const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(items, (size_t)nsm));
-  kern<<<grid, kThreads, L.total, st>>>(map, x, (int)H, (int)T, bvt, ranks, (int)R, L, o);
+  kern<<<grid, PtCfg<RG>::kThreads, L.total, st>>>(map, x, (int)H, (int)T, bvt, ranks, (int)R, L, o);
   note_launches(1);
   return cudaGetLastError();
 }
