@@ -143,6 +143,60 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
     return res
 
 
+def stage_rooflines(lib, L, torch, lay, dev, cfg, in_code, H, T, D, reps=10):
+    """Per-stage device time of one layer's compress + decompress (layer 0,
+    one caller stream; the library runs the value tensor on a side stream),
+    from the library's stage events, against each stage's algorithmic bytes:
+    the rANS coders read the packed codes and write the container (encode) or
+    the reverse (decode); the other stages use the library's own byte counts."""
+    l, k, v, kb, vb = lay
+    st = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    ctx = L.context(dev)
+
+    def compress():
+        h = C.c_void_p()
+        L.check(lib.kvf_compress_layer(ctx, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), in_code, H, T, D, l,
+                                       C.byref(cfg), kb.handle if kb else None, vb.handle if vb else None,
+                                       C.byref(h), sp))
+        return h
+
+    ko = torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}")
+    vo = torch.empty_like(ko)
+    h = compress()
+    ent_bytes = 0
+    for which in (0, 1):
+        R, pl, dl, he = C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_int32()
+        L.check(lib.kvf_compressed_tensor_info(h, which, C.byref(R), C.byref(pl), C.byref(dl), C.byref(he)))
+        if he.value:
+            ent_bytes += pl.value + dl.value
+    lib.kvf_compressed_free(h)
+    L.check(lib.kvf_sync(ctx, sp))
+    L.check(lib.kvf_profile_enable(ctx, 1))
+    L.profile_read(dev)
+    try:
+        for _ in range(reps):
+            h = compress()
+            L.check(lib.kvf_decompress_layer(ctx, h, C.c_void_p(ko.data_ptr()), C.c_void_p(vo.data_ptr()), sp))
+            lib.kvf_compressed_free(h)
+        st.synchronize()
+        prof = L.profile_read(dev)
+    finally:
+        L.check(lib.kvf_profile_enable(ctx, 0))
+    L.check(lib.kvf_sync(ctx, sp))
+    peak, _ = _peaks()
+    out = []
+    for name, (ms, cnt, nbytes) in prof.items():
+        if not cnt:
+            continue
+        ms /= reps
+        nb = ent_bytes if name.startswith("entropy") else nbytes / reps
+        out.append({"stage": name, "ms_per_layer": ms, "launch_groups_per_layer": cnt / reps, "bytes": nb,
+                    "achieved_gbs": nb / (ms / 1e3) / GB if ms > 0 else None,
+                    "frac": nb / (ms / 1e3) / GB / peak if ms > 0 else None})
+    return out
+
+
 def decode_attention_leg(lib, L, torch, lay, dev, cfg, in_code, H, T, D, reps=20):
     """Decode attention of one query row per head on compressed layer 0
     (kvf_compressed_attention: rANS decode of both tensors into scratch, then
@@ -711,6 +765,7 @@ def gpu_arm(args):
     e2e_tot = reduce_stats(e2e_per)
 
     kr = kernel_rooflines(lib, L, K, torch, layers[0], dev, cfg) if rank == 0 else []
+    sr = stage_rooflines(lib, L, torch, layers[0], dev, cfg, in_code, H, T, D) if rank == 0 else []
     attn = decode_attention_leg(lib, L, torch, layers[0], dev, cfg, in_code, H, T, D) if rank == 0 else None
 
     cpu = None
@@ -773,6 +828,7 @@ def gpu_arm(args):
         "roofline": roof,
         "kernel_rooflines": [{k2: r[k2] for k2 in ("name", "kernel", "R", "bytes", "ms", "achieved_gbs", "frac",
                                                    "in_step")} for r in kr],
+        "stage_rooflines_layer0": sr,
         "compress_only": {"ms_per_step": tot["compress_ms"],
                           "gbs": tot["input_bytes"] / (tot["compress_ms"] / 1e3) / GB},
         "decompress_only": {"ms_per_step": tot["decompress_ms"],

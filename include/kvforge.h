@@ -129,8 +129,18 @@ kvf_status kvf_set_reconstruct_engine(kvf_ctx* ctx, int engine);
  *   coefficients that decide a code (each row's minimum and maximum, and any
  *   value within that bound of a rounding boundary) are recomputed with the
  *   exact chain, so codes, scales and mins are identical to the CUDA-core
- *   engine's; other shapes use the CUDA-core engine. */
-typedef enum { KVF_PROJ_AUTO = 0, KVF_PROJ_CUDA_CORE = 1, KVF_PROJ_TENSOR_CORE = 2 } kvf_proj_engine;
+ *   engine's; other shapes use the CUDA-core engine;
+ * TENSOR_CORE_APPROX: the same GEMM without the exact recomputation: codes,
+ *   scales and mins of the tensor-core coefficients, whose relative error
+ *   against the exact chain is near 2^-22 (a code can differ by one level
+ *   where a coefficient lies that close to a rounding boundary, and a row's
+ *   scale and min in their last bits). */
+typedef enum {
+  KVF_PROJ_AUTO = 0,
+  KVF_PROJ_CUDA_CORE = 1,
+  KVF_PROJ_TENSOR_CORE = 2,
+  KVF_PROJ_TENSOR_CORE_APPROX = 3
+} kvf_proj_engine;
 kvf_status kvf_set_projection_engine(kvf_ctx* ctx, int engine);
 /* Runs one of the library's bounded device waits against a barrier or status
  * word that nothing completes, with a 2 ms limit: the wait gives up and the

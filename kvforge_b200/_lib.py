@@ -36,7 +36,7 @@ PER_CHANNEL, PER_TOKEN = 0, 1
 IN_F32, IN_F16 = 0, 1
 CONSERVATIVE, BALANCED, AGGRESSIVE, ADAPTIVE = 0, 1, 2, 3
 RECON_AUTO, RECON_CUDA_CORE, RECON_TENSOR_CORE = 0, 1, 2
-PROJ_AUTO, PROJ_CUDA_CORE, PROJ_TENSOR_CORE = 0, 1, 2
+PROJ_AUTO, PROJ_CUDA_CORE, PROJ_TENSOR_CORE, PROJ_TENSOR_CORE_APPROX = 0, 1, 2, 3
 WAIT_MBARRIER, WAIT_LOOKBACK = 0, 1
 
 # every symbol include/kvforge.h declares

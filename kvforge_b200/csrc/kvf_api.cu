@@ -352,12 +352,14 @@ kvf_status mark_ready(kvf_compressed* c) {
 // engine when the context allows it and the shape fits, on CUDA cores
 // otherwise (R <= 32 there); both give identical codes, scales and mins
 bool token_tc(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, size_t T, size_t D, const float* bvt, size_t R) {
-  return ctx->proj_engine == KVF_PROJ_TENSOR_CORE && project_tc_fits(x, in_dtype, H, T, D, bvt, R);
+  return (ctx->proj_engine == KVF_PROJ_TENSOR_CORE || ctx->proj_engine == KVF_PROJ_TENSOR_CORE_APPROX) &&
+         project_tc_fits(x, in_dtype, H, T, D, bvt, R);
 }
 cudaError_t project_token(kvf_ctx* ctx, const void* x, int in_dtype, size_t H, size_t T, size_t D,
                           const float* bvt, const uint64_t* ranks, size_t R, const ProjectOut& po, cudaStream_t st) {
   if (token_tc(ctx, x, in_dtype, H, T, D, bvt, R)) {
-    const cudaError_t e = launch_project_tc(x, in_dtype, H, T, D, bvt, ranks, R, po, st);
+    const cudaError_t e =
+        launch_project_tc(x, in_dtype, H, T, D, bvt, ranks, R, ctx->proj_engine != KVF_PROJ_TENSOR_CORE_APPROX, po, st);
     if (e != cudaErrorNotSupported || R > 32) return e;
   }
   return launch_project(x, in_dtype, H, T, D, bvt, ranks, R, po, st);
@@ -1002,7 +1004,8 @@ kvf_status kvf_selftest_wait_timeout(kvf_ctx* ctx, int which, void* stream) {
 
 kvf_status kvf_set_projection_engine(kvf_ctx* ctx, int engine) {
   KVF_TRY(check_ctx(ctx));
-  if (engine < KVF_PROJ_AUTO || engine > KVF_PROJ_TENSOR_CORE) return fail(KVF_ERR_INVALID_CONFIG, "unknown projection engine");
+  if (engine < KVF_PROJ_AUTO || engine > KVF_PROJ_TENSOR_CORE_APPROX)
+    return fail(KVF_ERR_INVALID_CONFIG, "unknown projection engine");
   ctx->proj_engine = engine;
   return KVF_OK;
 }

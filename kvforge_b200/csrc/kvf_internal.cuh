@@ -271,11 +271,12 @@ cudaError_t calib_static_scratch(int device, double** out);
 cudaError_t launch_calib_finalize(double* calib_part, size_t H, size_t tiles, size_t T,
                                   size_t D, float* scores, cudaStream_t st);
 // tensor-core projection with the per-token quantization epilogue (mode 2 of
-// ProjectOut) and codes identical to launch_project's (kvf_project_tc.cu): f16
-// input, D == 128, R <= 64; cudaErrorNotSupported otherwise (the caller then
-// uses launch_project)
+// ProjectOut; kvf_project_tc.cu): f16 input, D == 128, R <= 64;
+// cudaErrorNotSupported otherwise (the caller then uses launch_project).
+// exact: codes identical to launch_project's; otherwise codes of the
+// tensor-core coefficients (relative error near 2^-22 of the exact ones)
 cudaError_t launch_project_tc(const void* x, int in_dtype, size_t H, size_t T, size_t D, const float* basis_vt,
-                              const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st);
+                              const uint64_t* ranks, size_t R, bool exact, const ProjectOut& o, cudaStream_t st);
 bool project_tc_fits(const void* x, int in_dtype, size_t H, size_t T, size_t D, const float* basis_vt, size_t R);
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable), looked up once
 void* tensor_map_encode_fn();

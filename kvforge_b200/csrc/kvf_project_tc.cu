@@ -301,7 +301,10 @@ __device__ __noinline__ void finish_row(const __half* __restrict__ x, size_t gro
   write_row<RG>(cd, grow, R, scale, mn, o, shist, hist_on);
 }
 
-template <int RG>
+// EXACT = false: the approximate engine. Codes come straight from the
+// tensor-core coefficients (no exact chains, no deferred rows), and the token
+// stage goes back to the TMA producer when its MMAs complete.
+template <int RG, bool EXACT>
 __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
     k_project_tc(const __grid_constant__ CUtensorMap xmap, const __half* __restrict__ x, int H, int T,
                  const float* __restrict__ bvt, const uint64_t* __restrict__ ranks, int R, PtLayout L, ProjectOut o) {
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&x_full[s], 1);
-      mbar_init(&x_empty[s], 4);
+      mbar_init(&x_empty[s], EXACT ? 4 : 1);
     }
     for (int a = 0; a < kAcc; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -529,6 +532,10 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                            sa(&acc_full[a]))
                        : "memory");
+          if (!EXACT)  // the epilogue reads no x: the stage is free once the MMAs have read it
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             sa(&x_empty[s]))
+                         : "memory");
           last_acc = n;
         }
       }
@@ -553,7 +560,8 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
       const bool ok = t < T;
       const size_t grow = (size_t)h * T + (size_t)(ok ? t : 0);
       bool got = mbar_wait(&bfull[b], (uint32_t)((hs / kSlots) & 1), abort_flag);
-      got = got && mbar_wait(&x_full[s], (uint32_t)((n / kStages) & 1), abort_flag);
+      // (the approximate engine reads no x, and its stage may already hold a later tile)
+      if (EXACT) got = got && mbar_wait(&x_full[s], (uint32_t)((n / kStages) & 1), abort_flag);
       got = got && mbar_wait(&acc_full[a], (uint32_t)((n / kAcc) & 1), abort_flag);
       if (__any_sync(0xffffffffu, !got)) {  // the warp leaves together (tcgen05.ld is warp-wide)
         timed_out = true;
@@ -587,6 +595,24 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if constexpr (!EXACT) {
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+          const float v = __fadd_rn(P[r], 0.0f);  // -0.0 as +0.0, as mm_update
+          mn = (r < R) ? fminf(mn, v) : mn;
+          mx = (r < R) ? fmaxf(mx, v) : mx;
+        }
+        const float scale = make_scale(mn, mx, levels);
+        const float inv = __frcp_rn(scale);
+        uint32_t cd[RG];
+#pragma unroll
+        for (int r = 0; r < RG; ++r) cd[r] = qcode_fast(P[r], mn, scale, inv, levels);
+        if (ok) write_row<RG>(cd, grow, R, scale, mn, ro, shist, hist_on);
+        __syncwarp();
+        if (lane == 0) atomicAdd(&done[b], 1);
+        continue;
+      }
       // the smallest and largest approximate coefficients
       int rA = 0, rB = 0;
       float qa = P[0], qb = P[0];
@@ -714,10 +740,10 @@ bool encode_x_map(CUtensorMap* map, const __half* x, size_t rows) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int RG>
+template <int RG, bool EXACT>
 cudaError_t launch_tc_rg(const CUtensorMap& map, const __half* x, size_t H, size_t T, const float* bvt,
                          const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st) {
-  auto kern = k_project_tc<RG>;
+  auto kern = k_project_tc<RG, EXACT>;
   constexpr PtLayout L = pt_layout<RG>();
   // more than half of the SM's shared memory: one CTA per SM, so no other
   // TMEM-allocating kernel of this library shares the SM and the allocation
@@ -752,16 +778,22 @@ bool project_tc_fits(const void* x, int in_dtype, size_t H, size_t T, size_t D, 
 }
 
 cudaError_t launch_project_tc(const void* x, int in_dtype, size_t H, size_t T, size_t D, const float* basis_vt,
-                              const uint64_t* ranks, size_t R, const ProjectOut& o, cudaStream_t st) {
+                              const uint64_t* ranks, size_t R, bool exact, const ProjectOut& o, cudaStream_t st) {
   if (o.mode != 2 || !project_tc_fits(x, in_dtype, H, T, D, basis_vt, R) || (o.packed && (R & 1)) || H * T >= (1ull << 32))
     return cudaErrorNotSupported;
   CUtensorMap map{};
   if (!encode_x_map(&map, static_cast<const __half*>(x), H * T)) return cudaErrorNotSupported;
   const __half* xh = static_cast<const __half*>(x);
-  if (R <= 8) return launch_tc_rg<8>(map, xh, H, T, basis_vt, ranks, R, o, st);
-  if (R <= 16) return launch_tc_rg<16>(map, xh, H, T, basis_vt, ranks, R, o, st);
-  if (R <= 32) return launch_tc_rg<32>(map, xh, H, T, basis_vt, ranks, R, o, st);
-  return launch_tc_rg<64>(map, xh, H, T, basis_vt, ranks, R, o, st);
+  if (exact) {
+    if (R <= 8) return launch_tc_rg<8, true>(map, xh, H, T, basis_vt, ranks, R, o, st);
+    if (R <= 16) return launch_tc_rg<16, true>(map, xh, H, T, basis_vt, ranks, R, o, st);
+    if (R <= 32) return launch_tc_rg<32, true>(map, xh, H, T, basis_vt, ranks, R, o, st);
+    return launch_tc_rg<64, true>(map, xh, H, T, basis_vt, ranks, R, o, st);
+  }
+  if (R <= 8) return launch_tc_rg<8, false>(map, xh, H, T, basis_vt, ranks, R, o, st);
+  if (R <= 16) return launch_tc_rg<16, false>(map, xh, H, T, basis_vt, ranks, R, o, st);
+  if (R <= 32) return launch_tc_rg<32, false>(map, xh, H, T, basis_vt, ranks, R, o, st);
+  return launch_tc_rg<64, false>(map, xh, H, T, basis_vt, ranks, R, o, st);
 }
 
 }  // namespace kvf

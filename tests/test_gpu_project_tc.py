@@ -121,3 +121,45 @@ def test_tensor_core_projection_large_layer(kvf, oracle):
     vb = kvf.Basis.compute(v, cfg.projection_variance_threshold)
     bvt, ranks, _ = vb.host()
     _check(kvf, oracle, host(v), bvt, ranks, bvt.shape[1], INT4)
+
+
+@pytest.mark.parametrize("R", [3, 12, 17, 33, 58])
+def test_tensor_core_projection_approx_engine(kvf, oracle, R):
+    """KVF_PROJ_TENSOR_CORE_APPROX quantizes the tensor-core coefficients
+    directly. Tolerances (against the oracle's quantization of its own exact
+    coefficients): at most 0.5 % of codes differ and none by more than one
+    level; a row's scale and min within 1e-5 of the norm of the row's input
+    (divided by the levels for the scale) -- a tensor-core coefficient's error
+    scales with sum |x_c v_c| <= ||x||, not with the coefficient -- and the
+    dequantized rows within relative Frobenius error 2e-2 (the tensor-core
+    bar) of the oracle's."""
+    from kvforge_b200 import _lib as L
+    rng = np.random.default_rng(2000 + R)
+    H, T, D = 3, 1000, 128
+    ranks = np.array([R, max(1, R - 3), max(1, R // 2)], np.uint64)
+    bvt = _basis(rng, H, R, D, ranks)
+    coef = rng.standard_normal((H, T, R)).astype(np.float32) * (0.9 ** np.arange(R, dtype=np.float32))
+    x16 = (np.einsum("htr,hrd->htd", coef, bvt) + 0.05 * rng.standard_normal((H, T, D))).astype(np.float16)
+    P = oracle.project(x16.astype(np.float32), bvt, ranks, threads=8)
+    for dt in (INT4, INT8):
+        p, s, m = oracle.quantize(P, dt, PT)
+        gp, gs, gm = _run(kvf, x16, bvt, ranks, R, dt, L.PROJ_TENSOR_CORE_APPROX)
+        if dt == INT4 and R % 2 == 0:
+            a = np.stack([gp & 0xF, gp >> 4], -1).reshape(-1).astype(np.int16)
+            b = np.stack([p & 0xF, p >> 4], -1).reshape(-1).astype(np.int16)
+        else:
+            if dt == INT4:  # odd R: unpack over the flat index
+                a = np.stack([gp & 0xF, gp >> 4], -1).reshape(-1)[: H * T * R].astype(np.int16)
+                b = np.stack([p & 0xF, p >> 4], -1).reshape(-1)[: H * T * R].astype(np.int16)
+            else:
+                a, b = gp.astype(np.int16), p.astype(np.int16)
+        d = np.abs(a - b)
+        assert d.max() <= 1 and (d > 0).mean() < 5e-3, (d.max(), (d > 0).mean())
+        levels = 15.0 if dt == INT4 else 255.0
+        xn = np.linalg.norm(x16.astype(np.float64).reshape(H * T, D), axis=1)
+        es = np.abs(gs.astype(np.float64) - s) / (xn / levels + 1e-30)
+        em = np.abs(gm.astype(np.float64) - m) / (xn + 1e-30)
+        assert es.max() < 1e-5 and em.max() < 1e-5, (es.max(), em.max())
+        deq_g = a.reshape(H * T, R) * gs[:, None] + gm[:, None]
+        deq_o = b.reshape(H * T, R) * s[:, None] + m[:, None]
+        assert np.linalg.norm(deq_g - deq_o) / np.linalg.norm(deq_o) < 2e-2
