@@ -102,6 +102,26 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
                         "R": None, "bytes": plen + 8 * npar + 4 * n, "ms": ms, "in_step": True})
         return res
 
+    # the value projection on the tensor-core engines as well (exact codes, and
+    # the approximate engine), timed beside the default CUDA-core kernel
+    tc_engines = ((L.PROJ_TENSOR_CORE, "_tcgen05_exact", "k_project_tc<RG, true> (tcgen05 + exact min/max chains)"),
+                  (L.PROJ_TENSOR_CORE_APPROX, "_tcgen05_approx",
+                   "k_project_tc<RG, false> (tcgen05, approximate codes)"))
+    for eng, suffix, kern_name in (tc_engines if v.dtype == torch.float16 and D == 128 and vb.R <= 64 else ()):
+        R = vb.R
+        n = H * T * R
+        packed = torch.empty((n + 1) // 2, dtype=torch.uint8, device=v.device)
+        sc = torch.empty(H * T, device=v.device)
+        mn = torch.empty(H * T, device=v.device)
+        L.check(lib.kvf_set_projection_engine(ctx, eng))
+        try:
+            ms = timed(lambda: L.check(lib.kvf_fused_project_quantize(
+                ctx, P(v), 1, H, T, D, C.c_void_p(vb.device_vt()), C.c_void_p(vb.device_ranks()), R, 0, 1,
+                P(packed), P(sc), P(mn), sp)))
+        finally:
+            L.check(lib.kvf_set_projection_engine(ctx, L.PROJ_AUTO))
+        res.append({"name": "project_values_int4_per_token" + suffix, "kernel": kern_name,
+                    "bytes": v.numel() * 2 + (n + 1) // 2 + 8 * H * T, "ms": ms, "R": R, "in_step": False})
     for name, x, b, per_token in (("project_values_int4_per_token", v, vb, True), ("project_keys", k, kb, False)):
         R = b.R
         if per_token:
