@@ -376,6 +376,11 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
                          int axis, uint8_t* packed, float* scales, float* mins, uint32_t* hist,
                          cudaStream_t st) {
   const size_t n = H * T * D;
+  if (axis == KVF_PER_CHANNEL) {  // one pass over the input where the shape allows it
+    const cudaError_t e = launch_quantize_channel_cluster(qin, qdt, H, T, D, dt, packed, scales, mins, hist, st);
+    if (e == cudaSuccess) return KVF_OK;
+    if (e != cudaErrorNotSupported) return fail(KVF_ERR_CUDA, std::string("per-channel quantize: ") + cudaGetErrorString(e));
+  }
   int* keys = nullptr;
   if (axis == KVF_PER_CHANNEL) {
     keys = sc.get<int>(3 * H * D);  // min keys, max keys, reciprocal scales

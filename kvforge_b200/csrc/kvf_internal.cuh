@@ -221,6 +221,14 @@ cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t 
                                   float* mins, int* minmax_keys, cudaStream_t st);
 cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,
                              cudaStream_t st);
+// per-channel quantization in one launch (a thread-block cluster per head,
+// partial ranges exchanged through distributed shared memory; the codes pass
+// re-reads the tokens from L2): INT8 codes or INT4 bytes packed over the flat
+// index into `out`, scales/mins [H, D], optional histogram of the bytes
+// written. cudaErrorNotSupported when D / 4 is not a power of two or D > 128.
+cudaError_t launch_quantize_channel_cluster(const void* x, int in_dtype, size_t H, size_t T, size_t D, int data_type,
+                                            uint8_t* out, float* scales, float* mins, uint32_t* hist,
+                                            cudaStream_t st);
 // kmin/kmax <- keys of +inf / -inf
 cudaError_t launch_minmax_init(int* kmin, int* kmax, size_t np, cudaStream_t st);
 // codes (+ INT4 packing, + optional histogram) of projected keys P [H,T,R]

@@ -10,7 +10,10 @@
 //
 // Memory layout: x [H, T, D] row-major; codes are one byte per element
 // (flat index), INT4 packing into nibbles is a separate pass.
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "kvf_internal.cuh"
@@ -251,6 +254,192 @@ __global__ void __launch_bounds__(256) k_quant_channel(const TIn* __restrict__ x
                                               __ldg(invs + pb + c), levels);
     }
   }
+}
+
+// ---- per-channel in one launch: a thread-block cluster per head -------------
+// The per-(head, channel) range needs every token of the head before the
+// first code (quantize.rs:67-101). A cluster of C CTAs owns one head: CTA i
+// streams tokens [i*S, (i+1)*S) (S = ceil(T / C)) and takes their per-channel
+// min/max in registers; the C partial ranges meet through distributed shared
+// memory (each CTA reads all C), every CTA forms the same scale and min, then
+// reads its tokens again -- from L2, where the first pass just left them --
+// and writes their codes. One launch, no atomics, no parameter pass, and a
+// small shared-memory footprint, so every cluster is resident at once.
+// Thread j handles channels 4(j % (D/4)) .. + 3 of rows j / (D/4),
+// j / (D/4) + 256 / (D/4), ... (D / 4 a power of two, D <= 128). INT4 pairs
+// (2k, 2k + 1) lie in one row (D even), so a thread packs its four codes into
+// two bytes. The optional histogram counts the bytes written.
+constexpr int kQcThreads = 256;
+
+template <typename TIn, bool INT4>
+__global__ void __launch_bounds__(kQcThreads) k_quant_channel_cluster(const TIn* __restrict__ x, int T, int D,
+                                                                      int slab, float levels,
+                                                                      uint8_t* __restrict__ out,
+                                                                      float* __restrict__ scales,
+                                                                      float* __restrict__ mins,
+                                                                      uint32_t* __restrict__ hist) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float cmin[128], cmax[128];            // this CTA's partial range per channel
+  __shared__ float wred[8][2][128];                 // per-warp partials; then scale, min, 1/scale
+  __shared__ uint32_t shist[256];
+  const int h = blockIdx.y, rank = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  const int tpr = D >> 2;                           // threads per row (one float4 / 4 halves each)
+  const int rpp = kQcThreads / tpr;                 // rows per pass
+  const int rsub = tid / tpr, q = tid - rsub * tpr;
+  const int t0 = rank * slab;
+  const int nr = max(0, min(slab, T - t0));
+  const TIn* xh = x + ((size_t)h * T + (size_t)t0) * D + 4 * q;
+  if (hist)
+    for (int i = tid; i < 256; i += kQcThreads) shist[i] = 0u;
+  float mn[4] = {INFINITY, INFINITY, INFINITY, INFINITY}, mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  {
+    int r = rsub;
+    for (; r + 3 * rpp < nr; r += 4 * rpp) {  // four rows in flight per thread
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = ld4(xh, (size_t)(r + u * rpp) * D);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mm_update(v[u].x, mn[0], mx[0]);
+        mm_update(v[u].y, mn[1], mx[1]);
+        mm_update(v[u].z, mn[2], mx[2]);
+        mm_update(v[u].w, mn[3], mx[3]);
+      }
+    }
+    for (; r < nr; r += rpp) {
+      const float4 v = ld4(xh, (size_t)r * D);
+      mm_update(v.x, mn[0], mx[0]);
+      mm_update(v.y, mn[1], mx[1]);
+      mm_update(v.z, mn[2], mx[2]);
+      mm_update(v.w, mn[3], mx[3]);
+    }
+  }
+  // partial ranges: lanes of a warp that share channels (rows of one pass)
+  // meet by shuffles, then the warps' partials in shared memory
+  const int w = tid >> 5, lane = tid & 31;
+  for (int k = 0; k < 4; ++k) {
+    for (int o = tpr; o < 32; o <<= 1) {
+      mn[k] = fminf(mn[k], __shfl_xor_sync(0xffffffffu, mn[k], o));
+      mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], o));
+    }
+  }
+  if (lane < tpr) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      wred[w][0][4 * lane + k] = mn[k];
+      wred[w][1][4 * lane + k] = mx[k];
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < D; c += kQcThreads) {
+    float a = INFINITY, b = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      a = fminf(a, wred[k][0][c]);
+      b = fmaxf(b, wred[k][1][c]);
+    }
+    cmin[c] = a;
+    cmax[c] = b;
+  }
+  cluster.sync();  // every CTA's partial range is in its shared memory
+  float* gsc = &wred[0][0][0];  // reuse: [D] scales, [D] mins, [D] reciprocals of this head
+  float* gmn = gsc + 128;
+  float* ginv = gsc + 256;
+  for (int c = tid; c < D; c += kQcThreads) {
+    float a = INFINITY, b = -INFINITY;
+    for (unsigned k = 0; k < cluster.num_blocks(); ++k) {
+      const float* rmin = cluster.map_shared_rank(cmin, k);
+      const float* rmax = cluster.map_shared_rank(cmax, k);
+      a = fminf(a, rmin[c]);
+      b = fmaxf(b, rmax[c]);
+    }
+    const float sc = make_scale(a, b, levels);
+    gsc[c] = sc;
+    gmn[c] = a;
+    ginv[c] = __frcp_rn(sc);
+    if (rank == 0) {
+      scales[(size_t)h * D + c] = sc;
+      mins[(size_t)h * D + c] = a;
+    }
+  }
+  cluster.sync();  // no CTA leaves (or reuses wred) while another still reads its partials
+  float s4[4], m4[4], i4[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    s4[k] = gsc[4 * q + k];
+    m4[k] = gmn[4 * q + k];
+    i4[k] = ginv[4 * q + k];
+  }
+  auto emit = [&](int r, const float4& f) {
+    const float v[4] = {f.x, f.y, f.z, f.w};
+    uint32_t c[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) c[k] = qcode_fast(v[k], m4[k], s4[k], i4[k], levels);
+    const size_t flat = ((size_t)h * T + (size_t)(t0 + r)) * D + 4 * q;
+    if (INT4) {
+      const uint32_t b0 = (c[0] & 0xFu) | ((c[1] & 0xFu) << 4), b1 = (c[2] & 0xFu) | ((c[3] & 0xFu) << 4);
+      *reinterpret_cast<uint16_t*>(out + flat / 2) = (uint16_t)(b0 | (b1 << 8));
+      if (hist) {
+        atomicAdd(&shist[b0], 1u);
+        atomicAdd(&shist[b1], 1u);
+      }
+    } else {
+      *reinterpret_cast<uint32_t*>(out + flat) = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+      if (hist)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) atomicAdd(&shist[c[k]], 1u);
+    }
+  };
+  {
+    int r = rsub;
+    for (; r + 3 * rpp < nr; r += 4 * rpp) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = ld4(xh, (size_t)(r + u * rpp) * D);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) emit(r + u * rpp, v[u]);
+    }
+    for (; r < nr; r += rpp) emit(r, ld4(xh, (size_t)r * D));
+  }
+  if (hist) {
+    __syncthreads();
+    for (int i = tid; i < 256; i += kQcThreads)
+      if (shist[i]) atomicAdd(&hist[i], shist[i]);
+  }
+}
+
+template <typename TIn, bool INT4>
+cudaError_t launch_qcc(const TIn* x, size_t H, size_t T, size_t D, int C, int slab, float levels, uint8_t* out,
+                       float* scales, float* mins, uint32_t* hist, size_t smem, cudaStream_t st) {
+  auto kern = k_quant_channel_cluster<TIn, INT4>;
+  constexpr int kDevs = 64;
+  static std::atomic<int> opted[kDevs];  // shared memory opted in so far, per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kDevs) return cudaErrorInvalidDevice;
+  if ((int)smem > opted[dev].load(std::memory_order_acquire)) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+      return e;
+    opted[dev].store((int)smem, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)C, (unsigned)H, 1);
+  cfg.blockDim = dim3(kQcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, x, (int)T, (int)D, slab, levels, out, scales, mins, hist);
+  note_launches(1);
+  return e;
 }
 
 // ---- INT4 nibble packing over the flat index (quantize.rs:136-150) ----------
@@ -574,6 +763,33 @@ cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t 
   if (in_dtype == KVF_IN_F16)
     return quantize_typed(static_cast<const __half*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
   return quantize_typed(static_cast<const float*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
+}
+
+cudaError_t launch_quantize_channel_cluster(const void* x, int in_dtype, size_t H, size_t T, size_t D, int data_type,
+                                            uint8_t* out, float* scales, float* mins, uint32_t* hist,
+                                            cudaStream_t st) {
+  const size_t esz = in_dtype == KVF_IN_F16 ? 2 : 4;
+  const size_t tpr = D / 4;  // threads per row: a power of two (the shuffle reduction pairs lanes tpr apart)
+  if (D == 0 || D > 128 || D % 4 || (tpr & (tpr - 1)) || H == 0 || H > 65535 || T == 0 || T > (1u << 30) ||
+      !aligned(x, 4 * esz) || !aligned(out, data_type == KVF_INT4 ? 2 : 4))
+    return cudaErrorNotSupported;
+  // CTAs per head (a cluster of 1, 2, 4 or 8): enough CTAs for every SM,
+  // and at least 32 rows each
+  int C = 1;
+  while (C < 8 && H * (size_t)C < 4 * 148 && (T + 2 * C - 1) / (2 * C) >= 32) C *= 2;
+  const int slab = (int)((T + C - 1) / C);
+  const size_t smem = 0;
+  const float levels = quant_levels(data_type);
+  if (in_dtype == KVF_IN_F16) {
+    const __half* xh = static_cast<const __half*>(x);
+    return data_type == KVF_INT4
+               ? launch_qcc<__half, true>(xh, H, T, D, C, slab, levels, out, scales, mins, hist, smem, st)
+               : launch_qcc<__half, false>(xh, H, T, D, C, slab, levels, out, scales, mins, hist, smem, st);
+  }
+  const float* xf = static_cast<const float*>(x);
+  return data_type == KVF_INT4
+             ? launch_qcc<float, true>(xf, H, T, D, C, slab, levels, out, scales, mins, hist, smem, st)
+             : launch_qcc<float, false>(xf, H, T, D, C, slab, levels, out, scales, mins, hist, smem, st);
 }
 
 cudaError_t launch_minmax_init(int* kmin, int* kmax, size_t np, cudaStream_t st) {
