@@ -970,18 +970,49 @@ def stream_arm(args):
         if errs:
             raise errs[0]
 
-    def timed(reuse, steps, a0):
+    # batched: one kvf_compress_layers call per step for all layers of this
+    # rank (one kernel launch), outputs per layer
+    nl = len(layers)
+    bouts = [(torch.empty((H, A, D), dtype=torch.float32, device=f"cuda:{dev}"),
+              torch.empty((H, A, D), dtype=torch.float32, device=f"cuda:{dev}")) for _ in range(nl)]
+    PA = C.c_void_p * max(nl, 1)
+    b_idx = (C.c_size_t * max(nl, 1))(*[lay[0] for lay in layers])
+    b_kb = PA(*[lay[3].value if lay[3] is not None else None for lay in layers])
+    b_vb = PA(*[lay[4].value if lay[4] is not None else None for lay in layers])
+    b_ko = PA(*[o[0].data_ptr() for o in bouts])
+    b_vo = PA(*[o[1].data_ptr() for o in bouts])
+    b_keys = [PA(*[lay[1][a].data_ptr() for lay in layers]) for a in range(n_chunks)]
+    b_vals = [PA(*[lay[2][a].data_ptr() for lay in layers]) for a in range(n_chunks)]
+    b_out = PA()
+    sp_main = C.c_void_p(stream.cuda_stream)
+
+    def batched_step(a, keep=None):
+        L.check(lib.kvf_compress_layers(ctx, nl, b_keys[a], b_vals[a], in_code, H, A, D, b_idx, C.byref(cfg), b_kb,
+                                        b_vb, b_out, b_ko, b_vo, sp_main))
+        if keep is not None:
+            for i in range(nl):
+                keep(i, C.c_void_p(b_out[i]), bouts[i][0], bouts[i][1], sp_main)
+        for i in range(nl):
+            lib.kvf_compressed_free(C.c_void_p(b_out[i]))
+
+    batched = args.stream_mode == "batched"
+
+    def timed(reuse, steps, a0, use_batch=False):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
-        for s_ in tstreams:
-            s_.wait_event(e0)
-        for s in range(steps):
-            append_step((a0 + s) % n_chunks, reuse)
-        for s_ in tstreams:
-            ev = torch.cuda.Event()
-            ev.record(s_)
-            stream.wait_event(ev)
+        if use_batch:
+            for s in range(steps):
+                batched_step((a0 + s) % n_chunks)
+        else:
+            for s_ in tstreams:
+                s_.wait_event(e0)
+            for s in range(steps):
+                append_step((a0 + s) % n_chunks, reuse)
+            for s_ in tstreams:
+                ev = torch.cuda.Event()
+                ev.record(s_)
+                stream.wait_event(ev)
         e1.record(stream)
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / steps
@@ -999,7 +1030,10 @@ def stream_arm(args):
             per_layer.append((i, n.value - (b.value if reuse else 0), float(((ko - kf) ** 2).sum()),
                               float((kf ** 2).sum()), float(((vo - vf) ** 2).sum()), float((vf ** 2).sum())))
 
-        append_step(0, reuse, keep)
+        if reuse and batched:
+            batched_step(0, keep)
+        else:
+            append_step(0, reuse, keep)
         torch.cuda.synchronize()
         per_layer.sort()
         keys_ = ("comp", "err2_k", "ref2_k", "err2_v", "ref2_v")
@@ -1009,7 +1043,10 @@ def stream_arm(args):
     L.check(lib.kvf_set_reconstruct_engine(ctx, engines[args.recon_engine]))
     meas = {r: measure(r) for r in (True, False)}
     for s in range(args.warmup):
-        append_step(s % n_chunks, True)
+        if batched:
+            batched_step(s % n_chunks)
+        else:
+            append_step(s % n_chunks, True)
     L.check(lib.kvf_sync(ctx, None))
     if world > 1:
         import torch.distributed as dist
@@ -1018,11 +1055,25 @@ def stream_arm(args):
     clocks = ClockSampler(dev)
     clocks.start()
     n0 = lib.kvf_launch_count()
-    ms = timed(True, args.steps, args.warmup)
+    ms = timed(True, args.steps, args.warmup, use_batch=batched)
     n1 = lib.kvf_launch_count()
     clk = clocks.stop()
     if world > 1:
         dist.barrier()
+    # the same appends through the per-layer entry point (host threads, one
+    # stream each), for comparison with the batched call
+    ms_layers = None
+    if batched:
+        for s in range(2):
+            append_step(s % n_chunks, True)
+        L.check(lib.kvf_sync(ctx, None))
+        if world > 1:
+            dist.barrier()
+        ms_layers = timed(True, max(3, min(args.steps, 20)), 0)
+        if world > 1:
+            t_ = torch.tensor([ms_layers], device=f"cuda:{dev}")
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            ms_layers = float(t_.item())
     append_step(0, False)  # warm the fresh-basis path
     ms_fresh = timed(False, fresh_steps, 0)
     L.check(lib.kvf_sync(ctx, None))
@@ -1070,8 +1121,10 @@ def stream_arm(args):
                    "output_dtype": "f32", "basis": "the prefix's calibrated basis, reused by every chunk",
                    "step": "one append to every layer", "chunk_pool": n_chunks,
                    "l2": "chunks are L2-resident (256 KiB each); the step is latency-bound",
-                   "parallelism": f"layer-sharded x{world}", "host_threads_per_gpu": nthr,
-                   "reconstruct_engine": args.recon_engine},
+                   "parallelism": f"layer-sharded x{world}", "host_threads_per_gpu": 1 if batched else nthr,
+                   "entry_point": "kvf_compress_layers (all layers of the rank in one call)" if batched
+                   else "kvf_compress_layer + kvf_decompress_layer per layer",
+                   "reconstruct_engine": "cuda (inside the batched kernel)" if batched else args.recon_engine},
         "tokens_per_s": A * r["layers"] / (r["ms"] / 1e3),
         "us_per_layer_append": 1e3 * r["ms"] / max(len(mine), 1),
         "ratio_amortized": r["original_bytes"] / r["compressed_bytes"],
@@ -1083,6 +1136,9 @@ def stream_arm(args):
         "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (r["ms"] / 1e3) / GB,
                           "peak": peak * world, "frac": alg / (r["ms"] / 1e3) / GB / (peak * world),
                           "peak_kind": peak_kind},
+        "per_layer_entry_point": None if ms_layers is None else {
+            "ms_per_step": ms_layers, "host_threads_per_gpu": nthr, "reconstruct_engine": args.recon_engine,
+            "batched_speedup": ms_layers / r["ms"]},
         "prefix_ms_per_layer_untimed": 1e3 * t_prefix / max(len(layers), 1),
         "gpu_launches": int(n1 - n0),
         "clocks": clk,
@@ -1104,6 +1160,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--e2e-threads", type=int, default=4, help="host threads (one stream each) for the e2e leg")
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
+    ap.add_argument("--stream-mode", default="batched", choices=["batched", "threads"],
+                    help="streaming workloads: one kvf_compress_layers call per step, or per-layer calls on threads")
     ap.add_argument("--order", default="interleaved", choices=["interleaved", "phased"],
                     help="per layer compress then decompress, or all compressions then all decompressions")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -328,6 +328,24 @@ kvf_status kvf_compress_layer(kvf_ctx* ctx, const void* keys, const void* values
 kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* keys_out,
                                 float* values_out, void* stream);
 
+/* Many layers in one call (the layers of a step: a streaming append, or a
+ * rank's shard). Arrays of L device pointers / handles; layer_idx may be NULL
+ * (0..L-1). The result out[l] is what kvf_compress_layer gives for layer l,
+ * codes, parameters and sizes bit for bit. With keys_out and values_out
+ * (arrays of L f32 [H,T,D] device buffers, or both NULL) every layer is also
+ * decompressed, as kvf_decompress_layer does (the CUDA-core reconstruction;
+ * exact mode honoured). Short chunks -- T <= 128, head_dim <= 128 and a
+ * multiple of 4, projection width <= 64, given bases for projection presets,
+ * no entropy coding, no calibration -- take one kernel launch for all layers
+ * (one CTA per layer, tensor and head); other shapes run the per-layer path
+ * for each layer. Stream-ordered; no host synchronisation. No counterpart in
+ * the reference, which compresses one KVCache per call (core/src/pipeline.rs:73-80). */
+kvf_status kvf_compress_layers(kvf_ctx* ctx, size_t L, const void* const* keys, const void* const* values,
+                               int32_t in_dtype, size_t H, size_t T, size_t D, const size_t* layer_idx,
+                               const kvf_pipeline_config* cfg, const kvf_basis* const* k_bases,
+                               const kvf_basis* const* v_bases, kvf_compressed** out, float* const* keys_out,
+                               float* const* values_out, void* stream);
+
 /* Host-buffer variants (pinned or pageable host memory): copy in, run, copy
  * out on `stream`; they synchronise before returning. */
 kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host,

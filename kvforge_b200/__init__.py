@@ -395,6 +395,58 @@ class CompressionPipeline:
         c._inputs = (k, v)  # keep the inputs alive until the stream has consumed them
         return c
 
+    def compress_layers(self, kvs, cfg, key_bases=None, value_bases=None, decompress: bool = False):
+        """Compress the chunks of many layers (same [H, T, D] and input dtype)
+        in one call, kvf_compress_layers: short chunks take one kernel launch
+        for all layers. cfg is a preset name or a PipelineConfig; key_bases /
+        value_bases are lists of Basis (one per layer) or None. Returns the
+        list of CompressedKV, bit for bit what compress_with_config gives per
+        layer; with decompress=True also the list of decompressed KVCache (f32,
+        the CUDA-core reconstruction), without a host synchronisation."""
+        if isinstance(cfg, (str, int)):
+            cfg = config_from_preset(cfg)
+        dev = self._dev
+        kvs = list(kvs)
+        n = len(kvs)
+        ks, vs = [], []
+        for kv in kvs:
+            k = _as_device(kv.keys_tensor, dev)
+            v = _as_device(kv.values_tensor, dev)
+            if k.dtype != v.dtype:
+                v = v.to(k.dtype)
+            ks.append(k)
+            vs.append(v)
+        if n == 0:
+            return ([], []) if decompress else []
+        H, T, D = ks[0].shape
+        for k, v in zip(ks, vs):
+            if tuple(k.shape) != (H, T, D) or tuple(v.shape) != (H, T, D) or k.dtype != ks[0].dtype:
+                raise KvForgeError(L.ERR_SHAPE_MISMATCH, "compress_layers: every layer needs the same shape and dtype")
+        P = C.c_void_p * n
+        kp = P(*[k.data_ptr() for k in ks])
+        vp = P(*[v.data_ptr() for v in vs])
+        idx = (C.c_size_t * n)(*[kv.layer_idx for kv in kvs])
+        kb = P(*[b.handle.value if b is not None else None for b in key_bases]) if key_bases else None
+        vb = P(*[b.handle.value if b is not None else None for b in value_bases]) if value_bases else None
+        outs = P()
+        ko = vo = None
+        kop = vop = None
+        if decompress:
+            ko = [torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}") for _ in range(n)]
+            vo = [torch.empty((H, T, D), dtype=torch.float32, device=f"cuda:{dev}") for _ in range(n)]
+            kop = P(*[t.data_ptr() for t in ko])
+            vop = P(*[t.data_ptr() for t in vo])
+        L.check(L.lib().kvf_compress_layers(L.context(dev), n, kp, vp, _dtype_code(ks[0]), H, T, D, idx, C.byref(cfg),
+                                            kb, vb, outs, kop, vop, _stream(dev)))
+        cs = []
+        for i in range(n):
+            c = CompressedKV(C.c_void_p(outs[i]), dev)
+            c._inputs = (ks[i], vs[i])
+            cs.append(c)
+        if not decompress:
+            return cs
+        return cs, [KVCache(ko[i], vo[i], kvs[i].layer_idx) for i in range(n)]
+
     def decompress(self, compressed: CompressedKV) -> KVCache:
         dev = compressed.device
         H, T, D = compressed.shape
@@ -445,6 +497,20 @@ class StreamingCompressor:
                 raise KvForgeError(L.ERR_INVALID_CONFIG, f"layer {kv.layer_idx}: append before prefill")
             kb, vb = self._bases[kv.layer_idx]
         return self._pipe.compress_with_config(kv, self._cfg, kb, vb)
+
+    def append_layers(self, kvs, decompress: bool = False):
+        """Compress one appended chunk of each of many layers (same shape) in
+        one call (CompressionPipeline.compress_layers); with basis reuse each
+        layer projects onto its own prefix's bases."""
+        kvs = list(kvs)
+        kb = vb = None
+        if self._reuse and self._cfg.enable_projection:
+            for kv in kvs:
+                if kv.layer_idx not in self._bases:
+                    raise KvForgeError(L.ERR_INVALID_CONFIG, f"layer {kv.layer_idx}: append before prefill")
+            kb = [self._bases[kv.layer_idx][0] for kv in kvs]
+            vb = [self._bases[kv.layer_idx][1] for kv in kvs]
+        return self._pipe.compress_layers(kvs, self._cfg, kb, vb, decompress)
 
     def bases(self, layer_idx: int):
         """(key Basis, value Basis) kept for a layer, or None."""

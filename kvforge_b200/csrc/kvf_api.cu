@@ -10,6 +10,7 @@
 // order at the end of each call; result buffers belong to the kvf_compressed
 // object.
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -260,6 +261,25 @@ struct kvf_basis {
   std::shared_ptr<BasisData> d;
 };
 
+// One device block shared by the objects that one batched call builds; it
+// goes back to the pool, on the building stream, when the last of them is
+// freed (each free first makes that stream wait for its own readers, so the
+// final release follows every reader of every object).
+struct SharedBlock {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  void* p = nullptr;
+  SharedBlock() = default;
+  SharedBlock(const SharedBlock&) = delete;
+  SharedBlock& operator=(const SharedBlock&) = delete;
+  ~SharedBlock() {
+    if (p) {
+      DeviceGuard g(device);
+      cudaFreeAsync(p, stream);
+    }
+  }
+};
+
 struct kvf_compressed {
   kvf_ctx* ctx = nullptr;
   int device = 0;
@@ -268,6 +288,7 @@ struct kvf_compressed {
   TensorC key, value;
   float* d_scores = nullptr;
   std::vector<void*> owned;
+  std::shared_ptr<SharedBlock> block;  // buffers inside a block shared with other objects
   // Cross-stream lifetime: `ready` is recorded on `stream` once the object's
   // buffers are complete, and a reader on another stream waits for it first;
   // each reader stream records its own event after its last use, and
@@ -1572,6 +1593,150 @@ kvf_status kvf_decompress_layer(kvf_ctx* ctx, const kvf_compressed* c, float* ke
   if (s == KVF_OK && je != cudaSuccess) s = fail(KVF_ERR_CUDA, cudaGetErrorString(je));
   const kvf_status ls = reader_leave(c, st);  // even after a failure: launched kernels may still read
   return s != KVF_OK ? s : ls;
+}
+
+namespace {
+// the per-layer path for every layer (shapes or configurations the batched
+// kernel does not take)
+kvf_status compress_layers_each(kvf_ctx* ctx, size_t L, const void* const* keys, const void* const* values,
+                                int32_t in_dtype, size_t H, size_t T, size_t D, const size_t* layer_idx,
+                                const kvf_pipeline_config* cfg, const kvf_basis* const* k_bases,
+                                const kvf_basis* const* v_bases, kvf_compressed** out, float* const* keys_out,
+                                float* const* values_out, void* stream) {
+  for (size_t l = 0; l < L; ++l) {
+    KVF_TRY(kvf_compress_layer(ctx, keys[l], values[l], in_dtype, H, T, D, layer_idx ? layer_idx[l] : l, cfg,
+                               k_bases ? k_bases[l] : nullptr, v_bases ? v_bases[l] : nullptr, &out[l], stream));
+    if (keys_out && values_out)
+      KVF_TRY(kvf_decompress_layer(ctx, out[l], keys_out[l], values_out[l], stream));
+  }
+  return KVF_OK;
+}
+}  // namespace
+
+kvf_status kvf_compress_layers(kvf_ctx* ctx, size_t L, const void* const* keys, const void* const* values,
+                               int32_t in_dtype, size_t H, size_t T, size_t D, const size_t* layer_idx,
+                               const kvf_pipeline_config* cfg, const kvf_basis* const* k_bases,
+                               const kvf_basis* const* v_bases, kvf_compressed** out, float* const* keys_out,
+                               float* const* values_out, void* stream) {
+  KVF_TRY(check_ctx(ctx));
+  KVF_TRY(check_dtype(in_dtype));
+  KVF_TRY(check_shape(H, T, D));
+  if (!cfg || !out || (L && (!keys || !values))) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  if ((keys_out == nullptr) != (values_out == nullptr))
+    return fail(KVF_ERR_INVALID_CONFIG, "decompression outputs: give both keys_out and values_out, or neither");
+  for (size_t l = 0; l < L; ++l) out[l] = nullptr;
+  if (L == 0) return KVF_OK;
+  KVF_TRY(check_qcfg(cfg->key_data_type, KVF_PER_CHANNEL));
+  KVF_TRY(check_qcfg(cfg->value_data_type, KVF_PER_TOKEN));
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = S(stream);
+  const bool proj = cfg->enable_projection != 0;
+  // the batched kernel covers projection with given bases, no entropy coding
+  // and no calibration (whose result the reference discards, pipeline.rs:104-111)
+  bool batch = !cfg->enable_entropy_coding && !(cfg->enable_calibration && T >= 64);
+  size_t qmax = D;
+  if (batch && proj) {
+    if (!k_bases || !v_bases) batch = false;
+    qmax = 0;
+    for (size_t l = 0; batch && l < L; ++l)
+      for (const kvf_basis* b : {k_bases[l], v_bases[l]}) {
+        if (!b || b->d->H != H || b->d->D != D) {
+          batch = false;
+          break;
+        }
+        qmax = std::max(qmax, b->d->R);
+        if (H > 1 && (T * b->d->R) % 2) batch = false;
+      }
+  }
+  if (batch) batch = chunk_batch_fits(in_dtype, H, T, D, qmax, proj);
+  // rows are read 16 bytes (f32) or 8 bytes (f16) at a time
+  const uintptr_t amask = in_dtype == KVF_IN_F32 ? 15 : 7;
+  for (size_t l = 0; batch && l < L; ++l)
+    if (!keys[l] || !values[l] || ((reinterpret_cast<uintptr_t>(keys[l]) | reinterpret_cast<uintptr_t>(values[l])) & amask))
+      batch = false;
+  if (!batch)
+    return compress_layers_each(ctx, L, keys, values, in_dtype, H, T, D, layer_idx, cfg, k_bases, v_bases, out,
+                                keys_out, values_out, stream);
+
+  std::vector<std::unique_ptr<kvf_compressed>> cs(L);
+  std::vector<BatchTensor> desc(2 * L);
+  auto release = [&](kvf_status s) {
+    std::string msg = g_err;
+    for (auto& c : cs)
+      if (c) kvf_compressed_free(c.release());
+    g_err = msg;
+    return s;
+  };
+  // every layer's parameters and codes in one pool allocation: per tensor
+  // scales, mins, codes at offsets off[l][which][0..2]
+  std::vector<std::array<std::array<size_t, 3>, 2>> off(L);
+  size_t total = 0;
+  for (size_t l = 0; l < L; ++l)
+    for (int which = 0; which < 2; ++which) {
+      const int dt = which ? cfg->value_data_type : cfg->key_data_type;
+      const size_t q = proj ? (which ? v_bases[l] : k_bases[l])->d->R : D;
+      const size_t sp = align_up(num_params(H, T, q, which ? KVF_PER_TOKEN : KVF_PER_CHANNEL) * 4, kScratchAlign);
+      off[l][which] = {total, total + sp, total + 2 * sp};
+      total += 2 * sp + align_up(std::max<size_t>(packed_len(H * T * q, dt), 1), kScratchAlign);
+    }
+  auto block = std::make_shared<SharedBlock>();
+  block->device = ctx->device;
+  block->stream = st;
+  if (cudaMallocFromPoolAsync(&block->p, total, ctx->pool, st) != cudaSuccess) {
+    block->p = nullptr;
+    return fail(KVF_ERR_CUDA, "allocation failed");
+  }
+  for (size_t l = 0; l < L; ++l) {
+    cs[l].reset(new kvf_compressed());
+    kvf_compressed* c = cs[l].get();
+    c->ctx = ctx;
+    c->device = ctx->device;
+    c->stream = st;
+    c->block = block;
+    c->layer_idx = layer_idx ? layer_idx[l] : l;
+    c->H = H; c->T = T; c->D = D;
+    c->original_size_bytes = 2 * H * T * D * 4;  // KVCache::size_bytes, f32 (types.rs:30-32)
+    for (int which = 0; which < 2; ++which) {
+      TensorC& t = which ? c->value : c->key;
+      t.data_type = which ? cfg->value_data_type : cfg->key_data_type;
+      t.axis = which ? KVF_PER_TOKEN : KVF_PER_CHANNEL;
+      t.H = H; t.T = T; t.D = D;
+      t.entropy = false;
+      t.has_freq = false;
+      if (proj) t.basis = (which ? v_bases[l] : k_bases[l])->d;
+      t.qcols = proj ? t.basis->R : D;
+      t.packed_len = packed_len(H * T * t.qcols, t.data_type);
+      t.num_params = num_params(H, T, t.qcols, t.axis);
+      uint8_t* base = static_cast<uint8_t*>(block->p);
+      t.d_scales = reinterpret_cast<float*>(base + off[l][which][0]);
+      t.d_mins = reinterpret_cast<float*>(base + off[l][which][1]);
+      t.d_data = base + off[l][which][2];
+      t.data_cap = t.data_len = t.packed_len;
+      t.len_known = true;
+      BatchTensor& bt = desc[2 * l + which];
+      bt.x = which ? values[l] : keys[l];
+      bt.bvt = proj ? t.basis->d_vt : nullptr;
+      bt.ranks = proj ? t.basis->d_ranks : nullptr;
+      bt.cols = (int)t.qcols;
+      bt.axis = t.axis;
+      bt.data_type = t.data_type;
+      bt.levels = quant_levels(t.data_type);
+      bt.packed = t.d_data;
+      bt.scales = t.d_scales;
+      bt.mins = t.d_mins;
+      bt.out = keys_out ? (which ? values_out[l] : keys_out[l]) : nullptr;
+    }
+  }
+  {
+    const cudaError_t e = launch_chunk_batch(desc.data(), L, in_dtype, H, T, D, qmax, proj, ctx->exact_reconstruct, st);
+    if (e != cudaSuccess) return release(fail(KVF_ERR_CUDA, std::string("batched chunks: ") + cudaGetErrorString(e)));
+  }
+  for (size_t l = 0; l < L; ++l) {
+    const kvf_status s = mark_ready(cs[l].get());
+    if (s != KVF_OK) return release(s);
+  }
+  for (size_t l = 0; l < L; ++l) out[l] = cs[l].release();
+  return KVF_OK;
 }
 
 kvf_status kvf_compress_layer_host(kvf_ctx* ctx, const void* keys_host, const void* values_host, int32_t in_dtype,

@@ -326,6 +326,34 @@ cudaError_t launch_selftest_mbar(unsigned* status, unsigned long long limit_ns, 
 cudaError_t launch_selftest_lookback(unsigned long long* lb, unsigned* status, unsigned long long limit_ns,
                                      cudaStream_t st);
 
+// ---- batched short chunks (kvf_batch.cu) ------------------------------------
+// one tensor of one layer: input [H, T, D], optional basis [H, cols, D] and
+// ranks [H] (projection), outputs: codes (INT4 packed over the flat index or
+// INT8), scales/mins (per channel [H, cols] or per token [H, T]), optional
+// byte histogram, optional f32 reconstruction [H, T, D]
+struct BatchTensor {
+  const void* x = nullptr;
+  const float* bvt = nullptr;
+  const uint64_t* ranks = nullptr;
+  int cols = 0;
+  int axis = 0;
+  int data_type = 0;
+  float levels = 15.0f;
+  uint8_t* packed = nullptr;
+  float* scales = nullptr;
+  float* mins = nullptr;
+  uint32_t* hist = nullptr;
+  float* out = nullptr;
+};
+// whether one launch can take layers of this shape (T <= 128, D <= 128,
+// D % 4 == 0, cols <= 64 with a basis, a head's INT4 block on a byte)
+bool chunk_batch_fits(int in_dtype, size_t H, size_t T, size_t D, size_t cols_max, bool proj);
+// descs: 2 * L host descriptors (keys then values of each layer), passed as
+// the kernel parameter, up to 128 layers a launch; grid (H, 2, layers).
+// exact: the reconstruction rounds each product and sum separately.
+cudaError_t launch_chunk_batch(const BatchTensor* descs, size_t L, int in_dtype, size_t H, size_t T, size_t D,
+                               size_t cols_max, bool proj, int exact, cudaStream_t st);
+
 // ---- fused dequantize + decode attention (kvf_attn.cu) ----------------------
 // keys per channel [H, T, Rk] codes with [H, Rk] params, values per token
 // [H, T, Rv] codes with [H, T] params; kvt / vvt [H, R, D] bases or NULL
