@@ -36,17 +36,23 @@
 //     quantizes them as the oracle does.
 // One persistent CTA per SM walks (head, 128-token tile) items with warp roles:
 //   warp 0: TMA producer, two 2-D tensor-map loads per tile (64 channels x 128
-//           rows each, 128-byte swizzle) into a 4-stage ring (no multicast);
-//   warp 1: TMEM allocation; converts each new head's basis into one of two
-//           B-operand slots (a slot is reused once every tile of the head two
-//           back is done); lane 0 issues 8 MMAs (K = 16 each) per tile into
-//           one of four accumulators and commits them to an mbarrier;
-//   warps 2-9: two epilogue groups of four warps, alternating tiles; a thread
-//           owns one token row (its TMEM lane), reads its coefficients, its
-//           x row from the stage (norm and exact chains) and writes the
-//           quantized row or defers it. The stage is released after the
-//           epilogue; the deferred rows are finished by all epilogue threads
-//           at the end.
+//           rows each, 128-byte swizzle) into a ring of 5 stages (4 above 16
+//           coefficients; no multicast);
+//   warp 1: TMEM allocation; converts each new head's basis into a B-operand
+//           slot (two slots up to 32 coefficients, one at 64; a slot is reused
+//           once every tile of its previous head is done; the f32 rows arrive
+//           by bulk copy); lane 0 issues 8 MMAs (K = 16 each) per tile into
+//           one of 6 accumulators (4 above 32 coefficients) and commits them
+//           to an mbarrier;
+//   warps 2-13: three epilogue groups of four warps, taking tiles in turn; a
+//           thread owns one token row (its TMEM lane), reads its
+//           coefficients, its x row from the stage (norm and exact chains)
+//           and writes the quantized row or defers it. The stage is released
+//           after the epilogue; the deferred rows are finished by all
+//           epilogue threads at the end.
+// EXACT = false (KVF_PROJ_TENSOR_CORE_APPROX) skips steps 2-4: the row's
+// minimum, maximum and codes come from Q itself, and the stage is released as
+// soon as the tile's MMAs complete.
 // Every wait is bounded; a wait that runs out raises an abort flag that ends
 // every role, and KVF_ERR_DEVICE_TIMEOUT in the status word.
 #include <cuda.h>
