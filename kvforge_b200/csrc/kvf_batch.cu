@@ -31,6 +31,7 @@ constexpr int kBtThreads = 256;
 constexpr int kBtMaxT = 128, kBtMaxD = 128, kBtMaxR = 64;
 constexpr int kBtCh = 16;  // coefficients per thread in the projection (four r-blocks of 16)
 constexpr size_t kBatchSmallCap = 16, kBatchCap = 128;  // layers per launch
+constexpr int kBtLoads = 8;  // global loads in flight per thread while staging
 
 struct BtLayout {  // byte offsets into dynamic shared memory
   int xs, vt, pp, cb, par, hist, total;
@@ -108,22 +109,45 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
     rank = (int)(rk < (uint64_t)Q ? rk : (uint64_t)Q);
   }
   const TIn* x = static_cast<const TIn*>(d.x) + (size_t)h * T * D;
-  // 1. rows and basis into shared memory
+  // 1. rows and basis into shared memory, eight loads in flight per thread
   const int d4 = D >> 2;
-  for (int i = tid; i < T * d4; i += kBtThreads) {
-    const int t = i / d4, c4 = i - t * d4;
-    const float4 v = ldx4<TIn>(x + (size_t)t * D + 4 * c4);
-    float* dst = xs + t * L.xstride + 4 * c4;
-    dst[0] = v.x;
-    dst[1] = v.y;
-    dst[2] = v.z;
-    dst[3] = v.w;
+  for (int i0 = tid; i0 < T * d4; i0 += kBtLoads * kBtThreads) {
+    float4 v[kBtLoads];
+#pragma unroll
+    for (int j = 0; j < kBtLoads; ++j) {
+      const int i = i0 + j * kBtThreads;
+      const int t = i / d4, c4 = i - t * d4;
+      if (i < T * d4) v[j] = ldx4<TIn>(x + (size_t)t * D + 4 * c4);
+    }
+#pragma unroll
+    for (int j = 0; j < kBtLoads; ++j) {
+      const int i = i0 + j * kBtThreads;
+      const int t = i / d4, c4 = i - t * d4;
+      if (i < T * d4) {
+        float* dst = xs + t * L.xstride + 4 * c4;
+        dst[0] = v[j].x;
+        dst[1] = v[j].y;
+        dst[2] = v[j].z;
+        dst[3] = v[j].w;
+      }
+    }
   }
   if (proj) {  // vT[c][r]: r-blocks of 16 contiguous per column; rows from the rank on are zero
     const float* B = d.bvt + (size_t)h * Q * D;
-    for (int i = tid; i < kBtMaxR * D; i += kBtThreads) {
-      const int r = i / D, c = i - r * D;
-      vT[c * L.vstride + r] = (r < Q && r < rank) ? __ldg(B + (size_t)r * D + c) : 0.0f;
+    const int nrow = rank;  // rank <= Q: rows from the rank on are not read
+    for (int i0 = tid; i0 < kBtMaxR * D; i0 += kBtLoads * kBtThreads) {
+      float v[kBtLoads];
+#pragma unroll
+      for (int j = 0; j < kBtLoads; ++j) {
+        const int i = i0 + j * kBtThreads;
+        v[j] = (i < nrow * D) ? __ldg(B + i) : 0.0f;  // B + r * D + c
+      }
+#pragma unroll
+      for (int j = 0; j < kBtLoads; ++j) {
+        const int i = i0 + j * kBtThreads;
+        const int r = i / D, c = i - r * D;
+        if (i < kBtMaxR * D) vT[c * L.vstride + r] = v[j];
+      }
     }
   }
   if (d.hist)
@@ -141,6 +165,7 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
       for (int k = 0; k < kBtCh; ++k) acc[k] = 0.0f;
       const float* xr = xs + t * L.xstride;
       const float* vb = vT + g * kBtCh;
+#pragma unroll 4
       for (int c = 0; c < D; ++c) {
         const float xv = xr[c];
         const float4* v4 = reinterpret_cast<const float4*>(vb + c * L.vstride);
@@ -166,23 +191,34 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
   const float levels = d.levels;
   const int w = tid >> 5, lane = tid & 31;
   if (d.axis == KVF_PER_TOKEN) {
-    for (int t = w; t < T; t += kBtThreads / 32) {
+    // eight lanes per row, four rows per warp at a time
+    const int sub = lane & 7;
+    for (int t = w * 4 + (lane >> 3); t < ((T + 3) & ~3); t += 4 * (kBtThreads / 32)) {
+      const bool in = t < T;
       float mn = INFINITY, mx = -INFINITY;
-      for (int r = lane; r < Q; r += 32) mm_update(P[t * pstride + r], mn, mx);
-      warp_minmax(mn, mx);
-      const float scale = make_scale(mn, mx, levels);
-      const float inv = __frcp_rn(scale);
-      for (int r = lane; r < Q; r += 32) cb[t * Q + r] = (uint8_t)qcode_fast(P[t * pstride + r], mn, scale, inv, levels);
-      if (lane == 0) {
-        d.scales[(size_t)h * T + t] = scale;
-        d.mins[(size_t)h * T + t] = mn;
-        psc[t] = scale;
-        pmn[t] = mn;
+      if (in)
+        for (int r = sub; r < Q; r += 8) mm_update(P[t * pstride + r], mn, mx);
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      if (in) {
+        const float scale = make_scale(mn, mx, levels);
+        const float inv = __frcp_rn(scale);
+        for (int r = sub; r < Q; r += 8) cb[t * Q + r] = (uint8_t)qcode_fast(P[t * pstride + r], mn, scale, inv, levels);
+        if (sub == 0) {
+          d.scales[(size_t)h * T + t] = scale;
+          d.mins[(size_t)h * T + t] = mn;
+          psc[t] = scale;
+          pmn[t] = mn;
+        }
       }
     }
   } else {
     for (int r = tid; r < Q; r += kBtThreads) {
       float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 8
       for (int t = 0; t < T; ++t) mm_update(P[t * pstride + r], mn, mx);
       const float scale = make_scale(mn, mx, levels);
       psc[r] = scale;
@@ -253,6 +289,7 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
           float acc[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+#pragma unroll 2
           for (int r = 0; r < rank; ++r) {
             const float v = vT[c * L.vstride + r];
             const float4* p4 = reinterpret_cast<const float4*>(dT + r * ts + t0);
