@@ -992,18 +992,21 @@ def stream_arm(args):
         if keep is not None:
             for i in range(nl):
                 keep(i, C.c_void_p(b_out[i]), bouts[i][0], bouts[i][1], sp_main)
-        for i in range(nl):
-            lib.kvf_compressed_free(C.c_void_p(b_out[i]))
+        L.check(lib.kvf_compressed_free_many(b_out, nl))
 
     batched = args.stream_mode == "batched"
+
+    host_ms = {}
 
     def timed(reuse, steps, a0, use_batch=False):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
         if use_batch:
+            h0 = time.perf_counter()
             for s in range(steps):
                 batched_step((a0 + s) % n_chunks)
+            host_ms["batched"] = 1e3 * (time.perf_counter() - h0) / steps
         else:
             for s_ in tstreams:
                 s_.wait_event(e0)
@@ -1136,6 +1139,7 @@ def stream_arm(args):
         "step_roofline": {"algorithmic_bytes": alg, "achieved_gbs": alg / (r["ms"] / 1e3) / GB,
                           "peak": peak * world, "frac": alg / (r["ms"] / 1e3) / GB / (peak * world),
                           "peak_kind": peak_kind},
+        "host_issue_ms_per_step": host_ms.get("batched"),
         "per_layer_entry_point": None if ms_layers is None else {
             "ms_per_step": ms_layers, "host_threads_per_gpu": nthr, "reconstruct_engine": args.recon_engine,
             "batched_speedup": ms_layers / r["ms"]},

@@ -449,6 +449,9 @@ kvf_status kvf_compressed_serialize(kvf_compressed* c, uint8_t* buf_host, size_t
 kvf_status kvf_compressed_deserialize(kvf_ctx* ctx, const uint8_t* buf_host, size_t len,
                                       kvf_compressed** out, void* stream);
 kvf_status kvf_compressed_free(kvf_compressed* c);
+/* kvf_compressed_free of cs[0], ..., cs[n-1] in order (NULL entries are
+ * skipped): one call for the objects of a kvf_compress_layers step. */
+kvf_status kvf_compressed_free_many(kvf_compressed* const* cs, size_t n);
 
 #ifdef __cplusplus
 }

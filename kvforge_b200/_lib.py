@@ -55,7 +55,7 @@ EXPORTS = [
     "kvf_compressed_deserialize", "kvf_compressed_free",
     "kvf_bandwidth_bytes_per_us", "kvf_cost_measure", "kvf_cost_estimate", "kvf_cost_select",
     "kvf_launch_count", "kvf_stage_name", "kvf_profile_enable", "kvf_profile_read", "kvf_calibrate_noalloc",
-    "kvf_set_projection_engine", "kvf_compress_layers",
+    "kvf_set_projection_engine", "kvf_compress_layers", "kvf_compressed_free_many",
 ]
 
 NUM_STAGES = 8
@@ -124,6 +124,7 @@ def _declare(L):
         "kvf_set_reconstruct_engine": (st, [p, C.c_int]),
         "kvf_set_projection_engine": (st, [p, C.c_int]),
         "kvf_compress_layers": (st, [p, sz, p, p, i32, sz, sz, sz, p, C.POINTER(PipelineConfig), p, p, p, p, p, p]),
+        "kvf_compressed_free_many": (st, [p, sz]),
         "kvf_selftest_wait_timeout": (st, [p, C.c_int, p]),
         "kvf_sync": (st, [p, p]),
         "kvf_pipeline_config_from_preset": (st, [i32, C.POINTER(PipelineConfig)]),

@@ -265,18 +265,20 @@ struct kvf_basis {
 // goes back to the pool, on the building stream, when the last of them is
 // freed (each free first makes that stream wait for its own readers, so the
 // final release follows every reader of every object).
+// The objects also share one `ready` event, recorded once for the call.
 struct SharedBlock {
+  kvf_ctx* ctx = nullptr;
   int device = 0;
   cudaStream_t stream = nullptr;
   void* p = nullptr;
+  cudaEvent_t ready = nullptr;
   SharedBlock() = default;
   SharedBlock(const SharedBlock&) = delete;
   SharedBlock& operator=(const SharedBlock&) = delete;
   ~SharedBlock() {
-    if (p) {
-      DeviceGuard g(device);
-      cudaFreeAsync(p, stream);
-    }
+    DeviceGuard g(device);
+    if (p) cudaFreeAsync(p, stream);
+    if (ready) ctx->order_event_release(ready);
   }
 };
 
@@ -1680,6 +1682,7 @@ kvf_status kvf_compress_layers(kvf_ctx* ctx, size_t L, const void* const* keys, 
       total += 2 * sp + align_up(std::max<size_t>(packed_len(H * T * q, dt), 1), kScratchAlign);
     }
   auto block = std::make_shared<SharedBlock>();
+  block->ctx = ctx;
   block->device = ctx->device;
   block->stream = st;
   if (cudaMallocFromPoolAsync(&block->p, total, ctx->pool, st) != cudaSuccess) {
@@ -1731,11 +1734,16 @@ kvf_status kvf_compress_layers(kvf_ctx* ctx, size_t L, const void* const* keys, 
     const cudaError_t e = launch_chunk_batch(desc.data(), L, in_dtype, H, T, D, qmax, proj, ctx->exact_reconstruct, st);
     if (e != cudaSuccess) return release(fail(KVF_ERR_CUDA, std::string("batched chunks: ") + cudaGetErrorString(e)));
   }
-  for (size_t l = 0; l < L; ++l) {
-    const kvf_status s = mark_ready(cs[l].get());
-    if (s != KVF_OK) return release(s);
+  // one ready event for all objects of the call
+  {
+    cudaError_t e = ctx->order_event(&block->ready);
+    if (e == cudaSuccess) e = cudaEventRecord(block->ready, st);
+    if (e != cudaSuccess) return release(fail(KVF_ERR_CUDA, std::string("ready event: ") + cudaGetErrorString(e)));
   }
-  for (size_t l = 0; l < L; ++l) out[l] = cs[l].release();
+  for (size_t l = 0; l < L; ++l) {
+    cs[l]->ready = block->ready;
+    out[l] = cs[l].release();
+  }
   return KVF_OK;
 }
 
@@ -1949,10 +1957,17 @@ kvf_status kvf_compressed_free(kvf_compressed* c) {
       cudaStreamWaitEvent(c->stream, u.second, 0);
       c->ctx->order_event_release(u.second);
     }
-    if (c->ready) c->ctx->order_event_release(c->ready);
+    // an event shared through the block goes back with the block
+    if (c->ready && !(c->block && c->ready == c->block->ready)) c->ctx->order_event_release(c->ready);
     for (void* p : c->owned) cudaFreeAsync(p, c->stream);
   }
   delete c;
+  return KVF_OK;
+}
+
+kvf_status kvf_compressed_free_many(kvf_compressed* const* cs, size_t n) {
+  if (!cs && n) return fail(KVF_ERR_INVALID_CONFIG, "null pointer");
+  for (size_t i = 0; i < n; ++i) kvf_compressed_free(cs[i]);
   return KVF_OK;
 }
 
