@@ -8,7 +8,9 @@ seed 100 + l, low-rank (rank 24) + 0.1 N(0,1) noise, 4 outlier key channels per
 head at U[8, 16]. Layers are sharded across ranks (one process per GPU); the
 total work is fixed, so scaling is strong. The calibrated projection bases are
 computed once per layer before timing (the basis step may stay outside the
-timed path); the timed step is everything else, on the device.
+timed path); the timed step is everything else, on the device, issued as one
+replay of a CUDA graph that captured the step's library calls (--no-graph
+issues them from the host every step).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
@@ -515,7 +517,8 @@ def _config(args, w):
             "heads": w["H"], "tokens": w["T"], "head_dim": w["D"], "input_dtype": w["dtype"],
             "output_dtype": "f32", "basis": "calibrated per layer, computed before the timed region",
             "l2": "inputs larger than L2 (no flush)", "parallelism": f"layer-sharded x{args.gpus}",
-            "streams_per_gpu": getattr(args, "streams", 1), "order": getattr(args, "order", "interleaved")}
+            "streams_per_gpu": getattr(args, "streams", 1), "order": getattr(args, "order", "interleaved"),
+            "cuda_graph": bool(getattr(args, "graph", False))}
 
 
 # ---------------------------------------------------------------------------
@@ -591,15 +594,19 @@ def gpu_arm(args):
     start_ev = torch.cuda.Event()
     done_ev = [torch.cuda.Event() for _ in workers]
 
+    # the issuing stream is looked up at call time: inside a CUDA graph
+    # capture it is the capture stream
     def fork():
-        start_ev.record(stream)
+        cur = torch.cuda.current_stream(dev)
+        start_ev.record(cur)
         for w in workers:
             w.wait_event(start_ev)
 
     def join():
+        cur = torch.cuda.current_stream(dev)
         for w, e in zip(workers, done_ev):
             e.record(w)
-            stream.wait_event(e)
+            cur.wait_event(e)
 
     def step():
         fork()
@@ -644,6 +651,34 @@ def gpu_arm(args):
     in_bytes = sum(lay[1].numel() * lay[1].element_size() * 2 for lay in layers)
     orig_bytes = len(layers) * 2 * H * T * D * 4
 
+    # by default one step (every library call of every layer, all streams) is
+    # captured once as a CUDA graph and each warm-up and timed step replays it:
+    # the GPU runs the same kernels, with one host launch per step instead of
+    # hundreds of API calls (with 8 ranks on one host the per-call issue cost
+    # had left each GPU waiting); --no-graph issues every call from the host
+    graph, graph_launches, graph_err = None, None, None
+    if args.graph:
+        torch.cuda.synchronize()
+        na = lib.kvf_launch_count()
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                step()
+            graph, graph_launches = g, lib.kvf_launch_count() - na
+            for _ in range(args.warmup):
+                graph.replay()
+        except Exception as ex:  # capture refused: eager steps, reported in the line
+            graph_err = str(ex).splitlines()[0][:200]
+            graph = None
+        torch.cuda.synchronize()
+        L.check(lib.kvf_sync(ctx, sptr))
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+
     # timed region
     if world > 1:
         import torch.distributed as dist
@@ -654,11 +689,15 @@ def gpu_arm(args):
     n0 = lib.kvf_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        run_step()
+    host_issue_ms = 1e3 * (time.perf_counter() - h0) / args.steps
     e1.record(stream)
     torch.cuda.synchronize()
     n1 = lib.kvf_launch_count()
+    if graph is not None:  # the library counts launches when they are issued: once, at capture
+        n1 = n0 + graph_launches * args.steps
     ms = e0.elapsed_time(e1) / args.steps
     clk = clocks.stop()
     L.check(lib.kvf_sync(ctx, sptr))
@@ -857,6 +896,9 @@ def gpu_arm(args):
         "decode_attention_layer0": attn,
         "stages_ms_per_step_overlapped": {k: v[0] / prof_steps for k, v in prof.items() if v[1]},
         "basis_ms_per_layer_untimed": 1e3 * t_basis / max(len(layers), 1),
+        "host_issue_ms_per_step_rank0": host_issue_ms,
+        "cuda_graph": None if not args.graph else {"replayed": graph is not None,
+                                                   "launches_per_step": graph_launches, "capture_error": graph_err},
         "gpu_launches": int(n1 - n0),
         "clocks": clk,
     }
@@ -1164,6 +1206,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--e2e-threads", type=int, default=4, help="host threads (one stream each) for the e2e leg")
     ap.add_argument("--streams", type=int, default=4, help="streams layers are issued on")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="issue every step's library calls from the host instead of replaying one captured CUDA graph")
     ap.add_argument("--stream-mode", default="batched", choices=["batched", "threads"],
                     help="streaming workloads: one kvf_compress_layers call per step, or per-layer calls on threads")
     ap.add_argument("--order", default="interleaved", choices=["interleaved", "phased"],

@@ -1656,6 +1656,11 @@ kvf_status kvf_compress_layers(kvf_ctx* ctx, size_t L, const void* const* keys, 
   for (size_t l = 0; batch && l < L; ++l)
     if (!keys[l] || !values[l] || ((reinterpret_cast<uintptr_t>(keys[l]) | reinterpret_cast<uintptr_t>(values[l])) & amask))
       batch = false;
+  // decompressed rows are written 16 bytes at a time
+  for (size_t l = 0; batch && keys_out && l < L; ++l)
+    if (!keys_out[l] || !values_out[l] ||
+        ((reinterpret_cast<uintptr_t>(keys_out[l]) | reinterpret_cast<uintptr_t>(values_out[l])) & 15))
+      batch = false;
   if (!batch)
     return compress_layers_each(ctx, L, keys, values, in_dtype, H, T, D, layer_idx, cfg, k_bases, v_bases, out,
                                 keys_out, values_out, stream);
