@@ -29,12 +29,12 @@ namespace {
 
 constexpr int kBtThreads = 256;
 constexpr int kBtMaxT = 128, kBtMaxD = 128, kBtMaxR = 64;
-constexpr int kBtCh = 16;  // coefficients per thread in the projection (four r-blocks of 16)
 constexpr size_t kBatchSmallCap = 16, kBatchCap = 128;  // layers per launch
-constexpr int kBtLoads = 8;  // global loads in flight per thread while staging
+constexpr int kBtLoads = 8;    // 16- or 8-byte row loads in flight per thread while staging
+constexpr int kBtLoadsB = 32;  // basis element loads in flight per thread
 
 struct BtLayout {  // byte offsets into dynamic shared memory
-  int xs, vt, pp, cb, par, hist, total;
+  int xs, vt, pp, cb, par, hist, vr, total;
   int xstride;  // floats per x row (D + 1: rows on different banks)
   int vstride;  // floats per basis column (64 coefficients + 4: columns c and c + 1 on different banks)
   int tstride;  // floats per row of the transposed dequantized coefficients (T rounded up to 16)
@@ -47,7 +47,8 @@ __host__ __device__ inline BtLayout bt_layout(int T, int D, int Q, bool proj) {
   L.tstride = (T + 15) & ~15;
   int off = 0;
   L.xs = off;
-  off += T * L.xstride * 4;
+  const int xfloats = ((T + 3) & ~3) * L.xstride;  // rows up to a multiple of 4 (read, never used)
+  off += xfloats * 4;
   off = (off + 15) & ~15;
   L.vt = off;
   off += proj ? D * L.vstride * 4 : 0;
@@ -61,8 +62,115 @@ __host__ __device__ inline BtLayout bt_layout(int T, int D, int Q, bool proj) {
   off += 3 * 128 * 4;  // scale, min, 1/scale per row or per channel
   L.hist = off;
   off += 256 * 4;
+  // the basis row-major [rank][D] for the reconstruction: in the x rows'
+  // place (free after the projection) when they are large enough
+  L.vr = L.xs;
+  if (proj && xfloats < Q * D) {
+    L.vr = off;
+    off += Q * D * 4;
+  }
   L.total = off;
   return L;
+}
+
+__device__ __forceinline__ void fma2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ unsigned long long dup2(float x) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float2 split2(unsigned long long v) {
+  float2 f;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(v));
+  return f;
+}
+// Projection of rows RT * rg .. + RT - 1 onto coefficients 8 cg .. 8 cg + 7.
+// A warp takes 8 row groups x 4 coefficient groups, so its row loads hit 8
+// different banks and its basis loads 4 different 32-byte spans.
+template <int RT>
+__device__ __forceinline__ void proj_rows(const float* xs, int xstride, const float* vT, int vstride, int T, int D,
+                                          int Q, int rank, int ncg, float* P, int pstride) {
+  const int nrg = (T + RT - 1) / RT;
+  const int jobs = ((nrg + 7) & ~7) * ncg;
+  for (int job = threadIdx.x; job < jobs; job += kBtThreads) {
+    const int hi = job >> 3;
+    const int cg = hi % ncg, rg = (job & 7) + 8 * (hi / ncg);
+    if (rg >= nrg) continue;
+    const int t0 = RT * rg;
+    unsigned long long acc[RT][4];
+#pragma unroll
+    for (int i = 0; i < RT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0ull;
+    const float* xr = xs + t0 * xstride;
+    const float* vb = vT + 8 * cg;
+#pragma unroll 2
+    for (int c = 0; c < D; ++c) {
+      const ulonglong2 v01 = *reinterpret_cast<const ulonglong2*>(vb + c * vstride);
+      const ulonglong2 v23 = *reinterpret_cast<const ulonglong2*>(vb + c * vstride + 4);
+#pragma unroll
+      for (int i = 0; i < RT; ++i) {
+        const unsigned long long xx = dup2(xr[i * xstride + c]);
+        fma2(acc[i][0], xx, v01.x);
+        fma2(acc[i][1], xx, v01.y);
+        fma2(acc[i][2], xx, v23.x);
+        fma2(acc[i][3], xx, v23.y);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < RT; ++i) {
+      const int t = t0 + i;
+      if (t >= T) continue;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = split2(acc[i][q]);
+        const int r = 8 * cg + 2 * q;
+        if (r < Q) P[t * pstride + r] = (r < rank) ? f.x : 0.0f;  // projection.rs:96
+        if (r + 1 < Q) P[t * pstride + r + 1] = (r + 1 < rank) ? f.y : 0.0f;
+      }
+    }
+  }
+}
+
+// out rows t0 .. t0 + 7, channels 4cq .. 4cq + 3: sum over r < rank of
+// dT[r][t] * vR[r][c] in r order from +0.0, one rounding per term (packed
+// fma.rn.f32x2, each element rounded once) or, EXACT, product and sum
+// rounded separately
+template <bool EXACT>
+__device__ __forceinline__ void recon_tile(const float* dT, int ts, const float* vR, int D, int rank, int t0, int cq,
+                                           int T, float* out) {
+  unsigned long long acc[8][2];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = 0ull;
+#pragma unroll 2
+  for (int r = 0; r < rank; ++r) {
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(vR + r * D + 4 * cq);
+    const float4 d0 = *reinterpret_cast<const float4*>(dT + r * ts + t0);
+    const float4 d1 = *reinterpret_cast<const float4*>(dT + r * ts + t0 + 4);
+    const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (EXACT) {
+        const float2 a0 = split2(acc[i][0]), a1 = split2(acc[i][1]);
+        const float2 v0 = split2(v.x), v1 = split2(v.y);
+        const float2 b0 = make_float2(__fadd_rn(a0.x, __fmul_rn(dd[i], v0.x)), __fadd_rn(a0.y, __fmul_rn(dd[i], v0.y)));
+        const float2 b1 = make_float2(__fadd_rn(a1.x, __fmul_rn(dd[i], v1.x)), __fadd_rn(a1.y, __fmul_rn(dd[i], v1.y)));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(acc[i][0]) : "f"(b0.x), "f"(b0.y));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(acc[i][1]) : "f"(b1.x), "f"(b1.y));
+      } else {
+        const unsigned long long xx = dup2(dd[i]);
+        fma2(acc[i][0], xx, v.x);
+        fma2(acc[i][1], xx, v.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (t0 + i < T) {
+      const float2 a = split2(acc[i][0]), b = split2(acc[i][1]);
+      __stcs(reinterpret_cast<float4*>(out + (size_t)(t0 + i) * D + 4 * cq), make_float4(a.x, a.y, b.x, b.y));
+    }
+  }
 }
 
 template <typename TIn>
@@ -109,87 +217,80 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
     rank = (int)(rk < (uint64_t)Q ? rk : (uint64_t)Q);
   }
   const TIn* x = static_cast<const TIn*>(d.x) + (size_t)h * T * D;
-  // 1. rows and basis into shared memory, eight loads in flight per thread
+  // 1. rows and basis into shared memory: a thread's first rows and its basis
+  // elements are all requested before any of them is stored. Rows: thread =
+  // (row tr + k * rpp, 4-column group c4); basis: warp w takes rows w, w + 8,
+  // ..., lane l columns l, l + 32, ... (coalesced), stored transposed.
   const int d4 = D >> 2;
-  for (int i0 = tid; i0 < T * d4; i0 += kBtLoads * kBtThreads) {
-    float4 v[kBtLoads];
+  const int rpp = kBtThreads / d4;  // rows per pass
+  const int tr = tid / d4, c4 = tid - tr * d4;
+  const int w = tid >> 5, lane = tid & 31;
+  const float* B = proj ? d.bvt + (size_t)h * Q * D : nullptr;
+  auto load_rows = [&](int t0, float4 (&xv)[kBtLoads]) {
 #pragma unroll
-    for (int j = 0; j < kBtLoads; ++j) {
-      const int i = i0 + j * kBtThreads;
-      const int t = i / d4, c4 = i - t * d4;
-      if (i < T * d4) v[j] = ldx4<TIn>(x + (size_t)t * D + 4 * c4);
+    for (int k = 0; k < kBtLoads; ++k) {
+      const int t = t0 + k * rpp;
+      if (tr < rpp && t < T) xv[k] = ldx4<TIn>(x + (size_t)t * D + 4 * c4);
     }
+  };
+  auto store_rows = [&](int t0, const float4 (&xv)[kBtLoads]) {
 #pragma unroll
-    for (int j = 0; j < kBtLoads; ++j) {
-      const int i = i0 + j * kBtThreads;
-      const int t = i / d4, c4 = i - t * d4;
-      if (i < T * d4) {
+    for (int k = 0; k < kBtLoads; ++k) {
+      const int t = t0 + k * rpp;
+      if (tr < rpp && t < T) {
         float* dst = xs + t * L.xstride + 4 * c4;
-        dst[0] = v[j].x;
-        dst[1] = v[j].y;
-        dst[2] = v[j].z;
-        dst[3] = v[j].w;
+        dst[0] = xv[k].x;
+        dst[1] = xv[k].y;
+        dst[2] = xv[k].z;
+        dst[3] = xv[k].w;
       }
+    }
+  };
+  {  // every thread: its first rows and all its basis elements
+    float4 xv[kBtLoads];
+    load_rows(tr, xv);
+    if (proj) {
+      float bv[kBtLoadsB];
+#pragma unroll
+      for (int j = 0; j < kBtLoadsB; ++j) {
+        const int r = w + 8 * (j >> 2), c = lane + 32 * (j & 3);
+        bv[j] = (r < rank && c < D) ? __ldg(B + (size_t)r * D + c) : 0.0f;
+      }
+      store_rows(tr, xv);
+      // vT[c][r]: 64 coefficients per column; rows from the rank on are zero
+#pragma unroll
+      for (int j = 0; j < kBtLoadsB; ++j) {
+        const int r = w + 8 * (j >> 2), c = lane + 32 * (j & 3);
+        if (c < D) vT[c * L.vstride + r] = bv[j];
+      }
+    } else {
+      store_rows(tr, xv);
     }
   }
-  if (proj) {  // vT[c][r]: r-blocks of 16 contiguous per column; rows from the rank on are zero
-    const float* B = d.bvt + (size_t)h * Q * D;
-    const int nrow = rank;  // rank <= Q: rows from the rank on are not read
-    for (int i0 = tid; i0 < kBtMaxR * D; i0 += kBtLoads * kBtThreads) {
-      float v[kBtLoads];
-#pragma unroll
-      for (int j = 0; j < kBtLoads; ++j) {
-        const int i = i0 + j * kBtThreads;
-        v[j] = (i < nrow * D) ? __ldg(B + i) : 0.0f;  // B + r * D + c
-      }
-#pragma unroll
-      for (int j = 0; j < kBtLoads; ++j) {
-        const int i = i0 + j * kBtThreads;
-        const int r = i / D, c = i - r * D;
-        if (i < kBtMaxR * D) vT[c * L.vstride + r] = v[j];
-      }
-    }
+  for (int t0 = tr + kBtLoads * rpp; t0 < T; t0 += kBtLoads * rpp) {  // T > 8 rows per thread
+    float4 xv[kBtLoads];
+    load_rows(t0, xv);
+    store_rows(t0, xv);
   }
   if (d.hist)
     for (int i = tid; i < 256; i += kBtThreads) shist[i] = 0u;
   __syncthreads();
 
-  // 2. projection: thread = (row t, r-block g); the chains of one thread
-  // advance together, each over c in order
+  // 2. projection: thread = RT token rows x 8 coefficients (packed pairs); one
+  // pair of 16-byte basis loads feeds all RT rows, and every coefficient is
+  // its own chain over c in order (fma.rn.f32x2 rounds each element once, as
+  // fmaf). RT = 4 for wide bases, fewer rows per thread (more threads busy)
+  // for narrow ones.
   if (proj) {
-    const int groups = (Q + kBtCh - 1) / kBtCh;  // 1..4
-    for (int job = tid; job < T * groups; job += kBtThreads) {
-      const int t = job / groups, g = job - t * groups;
-      float acc[kBtCh];
-#pragma unroll
-      for (int k = 0; k < kBtCh; ++k) acc[k] = 0.0f;
-      const float* xr = xs + t * L.xstride;
-      const float* vb = vT + g * kBtCh;
-#pragma unroll 4
-      for (int c = 0; c < D; ++c) {
-        const float xv = xr[c];
-        const float4* v4 = reinterpret_cast<const float4*>(vb + c * L.vstride);
-#pragma unroll
-        for (int k4 = 0; k4 < kBtCh / 4; ++k4) {
-          const float4 v = v4[k4];
-          acc[4 * k4] = __fmaf_rn(xv, v.x, acc[4 * k4]);
-          acc[4 * k4 + 1] = __fmaf_rn(xv, v.y, acc[4 * k4 + 1]);
-          acc[4 * k4 + 2] = __fmaf_rn(xv, v.z, acc[4 * k4 + 2]);
-          acc[4 * k4 + 3] = __fmaf_rn(xv, v.w, acc[4 * k4 + 3]);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kBtCh; ++k) {
-        const int r = g * kBtCh + k;
-        if (r < Q) P[t * pstride + r] = (r < rank) ? acc[k] : 0.0f;  // projection.rs:96
-      }
-    }
+    const int ncg = (Q + 7) >> 3;
+    if (ncg >= 6) proj_rows<4>(xs, L.xstride, vT, L.vstride, T, D, Q, rank, ncg, P, pstride);
+    else if (ncg >= 3) proj_rows<2>(xs, L.xstride, vT, L.vstride, T, D, Q, rank, ncg, P, pstride);
+    else proj_rows<1>(xs, L.xstride, vT, L.vstride, T, D, Q, rank, ncg, P, pstride);
     __syncthreads();
   }
 
   // 3. quantization
   const float levels = d.levels;
-  const int w = tid >> 5, lane = tid & 31;
   if (d.axis == KVF_PER_TOKEN) {
     // eight lanes per row, four rows per warp at a time
     const int sub = lane & 7;
@@ -265,49 +366,32 @@ __global__ void __launch_bounds__(kBtThreads) k_chunk_batch(const __grid_constan
         __stcs(out + i, dq(cb[i], sc, mn));
       }
     } else {
-      // dT[r][t] = q * scale + min; rows from T to tstride are zero
+      // dT[r][t] = q * scale + min (rows from T to tstride zero); vR[r][c]
+      // the basis row-major, from its transposed copy
       float* dT = P;
+      float* vR = reinterpret_cast<float*>(bsm + L.vr);
       const int ts = L.tstride;
-      for (int i = tid; i < rank * ts; i += kBtThreads) {
-        const int r = i / ts, t = i - r * ts;
-        float v = 0.0f;
-        if (t < T) {
-          const float sc = (d.axis == KVF_PER_TOKEN) ? psc[t] : psc[r];
-          const float mn = (d.axis == KVF_PER_TOKEN) ? pmn[t] : pmn[r];
-          v = dq(cb[t * Q + r], sc, mn);
-        }
-        dT[i] = v;
-      }
-      __syncthreads();
-      // thread = (channel c, half of the rows in blocks of 16): one basis
-      // column, four broadcast 16-byte loads of coefficients per r
-      const int th = (((T + 1) / 2) + 15) & ~15;
-      for (int job = tid; job < D * 2; job += kBtThreads) {
-        const int c = job >> 1, half = job & 1;
-        const int ta = half ? th : 0, tb = half ? T : (th < T ? th : T);
-        for (int t0 = ta; t0 < tb; t0 += 16) {
-          float acc[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
-#pragma unroll 2
-          for (int r = 0; r < rank; ++r) {
-            const float v = vT[c * L.vstride + r];
-            const float4* p4 = reinterpret_cast<const float4*>(dT + r * ts + t0);
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 p = p4[k4];
-              const float pv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                float& a = acc[4 * k4 + j];
-                a = exact ? __fadd_rn(a, __fmul_rn(pv[j], v)) : __fmaf_rn(pv[j], v, a);
-              }
-            }
+      for (int r = w; r < rank; r += kBtThreads / 32)
+        for (int t = lane; t < ts; t += 32) {
+          float v = 0.0f;
+          if (t < T) {
+            const float sc = (d.axis == KVF_PER_TOKEN) ? psc[t] : psc[r];
+            const float mn = (d.axis == KVF_PER_TOKEN) ? pmn[t] : pmn[r];
+            v = dq(cb[t * Q + r], sc, mn);
           }
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            if (t0 + k < tb) __stcs(out + (size_t)(t0 + k) * D + c, acc[k]);
+          dT[r * ts + t] = v;
         }
+      for (int r = w; r < rank; r += kBtThreads / 32)
+        for (int c = lane; c < D; c += 32) vR[r * D + c] = vT[c * L.vstride + r];
+      __syncthreads();
+      // thread = 8 token rows x 4 channels (a warp: 32 channel quads of the
+      // same rows): one 16-byte basis load and two broadcast 16-byte loads of
+      // coefficients per r, one 16-byte streaming store per row
+      const int nrg = (T + 7) >> 3, ncq = D >> 2;
+      for (int job = tid; job < nrg * ncq; job += kBtThreads) {
+        const int cq = job % ncq, rg = job / ncq;
+        if (exact) recon_tile<true>(dT, ts, vR, D, rank, 8 * rg, cq, T, out);
+        else recon_tile<false>(dT, ts, vR, D, rank, 8 * rg, cq, T, out);
       }
     }
   }
