@@ -320,10 +320,11 @@ __global__ void __launch_bounds__(256) k_quant_channel(const TIn* __restrict__ x
 // and writes their codes. One launch, no atomics, no parameter pass, and a
 // small shared-memory footprint, so every cluster is resident at once.
 // Thread j handles channels 4(j % (D/4)) .. + 3 of rows j / (D/4),
-// j / (D/4) + 256 / (D/4), ... (D / 4 a power of two, D <= 128). INT4 pairs
+// j / (D/4) + kQcThreads / (D/4), ... (D / 4 a power of two, D <= 128). INT4 pairs
 // (2k, 2k + 1) lie in one row (D even), so a thread packs its four codes into
 // two bytes. The optional histogram counts the bytes written.
-constexpr int kQcThreads = 256;
+constexpr int kQcThreads = 512;
+constexpr int kQcWarps = kQcThreads / 32;
 constexpr int kQcFlight = 8;  // rows in flight per thread in both passes
 
 template <typename TIn, bool INT4>
@@ -336,7 +337,7 @@ __global__ void __launch_bounds__(kQcThreads) k_quant_channel_cluster(const TIn*
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float cmin[128], cmax[128];            // this CTA's partial range per channel
-  __shared__ float wred[8][2][128];                 // per-warp partials; then scale, min, 1/scale
+  __shared__ float wred[kQcWarps][2][128];          // per-warp partials; then scale, min, 1/scale
   __shared__ uint32_t shist[256];
   const int h = blockIdx.y, rank = (int)cluster.block_rank();
   const int tid = threadIdx.x;
@@ -391,7 +392,7 @@ __global__ void __launch_bounds__(kQcThreads) k_quant_channel_cluster(const TIn*
   for (int c = tid; c < D; c += kQcThreads) {
     float a = INFINITY, b = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < kQcWarps; ++k) {
       a = fminf(a, wred[k][0][c]);
       b = fmaxf(b, wred[k][1][c]);
     }
