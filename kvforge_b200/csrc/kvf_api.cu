@@ -404,6 +404,11 @@ kvf_status quantize_into(Scratch& sc, const void* qin, int qdt, size_t H, size_t
     if (e == cudaSuccess) return KVF_OK;
     if (e != cudaErrorNotSupported) return fail(KVF_ERR_CUDA, std::string("per-channel quantize: ") + cudaGetErrorString(e));
   }
+  if (axis == KVF_PER_TOKEN && D % 4) {  // even widths that the 16-byte kernel does not take: one pass, packed
+    const cudaError_t e = launch_quantize_token_pairs(qin, qdt, H, T, D, dt, packed, scales, mins, hist, st);
+    if (e == cudaSuccess) return KVF_OK;
+    if (e != cudaErrorNotSupported) return fail(KVF_ERR_CUDA, std::string("per-token quantize: ") + cudaGetErrorString(e));
+  }
   int* keys = nullptr;
   if (axis == KVF_PER_CHANNEL) {
     keys = sc.get<int>(3 * H * D);  // min keys, max keys, reciprocal scales

@@ -219,6 +219,11 @@ __device__ __forceinline__ float kfloat(int k) { return __int_as_float(k >= 0 ? 
 cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t T, size_t D,
                                   int data_type, int axis, uint8_t* codes, float* scales,
                                   float* mins, int* minmax_keys, cudaStream_t st);
+// per-token KIVI for even D <= 128 whose D is not a multiple of 4 (or any
+// even D): codes written packed (INT4) or as bytes (INT8), optional byte
+// histogram; cudaErrorNotSupported when the shape or alignment does not fit
+cudaError_t launch_quantize_token_pairs(const void* x, int in_dtype, size_t H, size_t T, size_t D, int data_type,
+                                       uint8_t* out, float* scales, float* mins, uint32_t* hist, cudaStream_t st);
 cudaError_t launch_pack_int4(const uint8_t* codes, size_t n, uint8_t* packed, uint32_t* hist,
                              cudaStream_t st);
 // per-channel quantization in one launch (a thread-block cluster per head,

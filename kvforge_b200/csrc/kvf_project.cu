@@ -181,7 +181,7 @@ __device__ __forceinline__ void fma_rows(unsigned long long (&acc)[kProjNR][RG /
 }
 
 template <typename TIn, int RG, bool CALIB, int MODE, bool TMA>
-__global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : 2))
+__global__ void __launch_bounds__(kProjThreads, (RG <= 12 ? 4 : RG == 32 ? 3 : 2))
     k_project(const __grid_constant__ CUtensorMap xmap, const TIn* __restrict__ x, int H, int T, int D,
               const float* __restrict__ bvt, const uint64_t* __restrict__ ranks, int R, int Rpad, ProjSmem L,
               ProjectOut o) {
@@ -560,7 +560,9 @@ cudaError_t project_launch(const CUtensorMap& map, const TIn* x, size_t H, size_
   off += 8 * kProjWarps * 4;  // up to 4 stage barriers per warp
   off = (off + 1023) & ~1023;  // swizzled stages start on a 1024-byte boundary
   L.xbuf = off;
-  L.stages = TMA ? 3 : 0;
+  // three stages per warp; two for the 32-wide groups (R > 24), whose basis
+  // copy is large, so that three CTAs fit on an SM
+  L.stages = TMA ? (RG == 32 ? 2 : 3) : 0;
   off += kProjWarps * L.stages * kWarpStage;
   L.total = off;
   if (L.total > max_dyn[dev]) return cudaErrorInvalidValue;

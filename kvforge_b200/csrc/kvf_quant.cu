@@ -143,6 +143,83 @@ __global__ void __launch_bounds__(256) k_quant_token_r4(const TIn* __restrict__ 
   }
 }
 
+// Even D <= 128 (projected coefficients whose count is not a multiple of
+// four): eight lanes per row, four rows per warp, lane s holds column pairs
+// s, s + 8, ... (8-byte loads). INT4: the pair's two codes are one packed
+// byte (pairs over the flat index stay inside a row when D is even), written
+// directly; INT8: two code bytes. HIST: the bytes written are counted.
+template <typename TIn, bool INT4, bool HIST>
+__global__ void __launch_bounds__(256) k_quant_token_pairs(const TIn* __restrict__ x, size_t rows, int D,
+                                                           float levels, uint8_t* __restrict__ out,
+                                                           float* __restrict__ scales, float* __restrict__ mins,
+                                                           uint32_t* __restrict__ hist) {
+  __shared__ uint32_t sh[HIST ? 256 : 1];
+  if (HIST) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sh[i] = 0u;
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const int np = D >> 1;  // pairs per row (<= 64)
+  for (size_t g0 = (((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4; g0 < rows; g0 += nwarps * 4) {
+    const size_t g = g0 + (lane >> 3);
+    const bool in = g < rows;
+    const size_t base = g * (size_t)D;
+    float2 v[8];
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int q = sub + 8 * k;
+      if (in && q < np) {
+        if constexpr (sizeof(TIn) == 4) {
+          v[k] = __ldg(reinterpret_cast<const float2*>(x + base) + q);
+        } else {
+          v[k] = __half22float2(__ldg(reinterpret_cast<const __half2*>(x + base) + q));
+        }
+        mm_update(v[k].x, mn, mx);
+        mm_update(v[k].y, mn, mx);
+      }
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (in) {
+      const float scale = make_scale(mn, mx, levels);
+      const float inv = __frcp_rn(scale);
+      if (sub == 0) {
+        scales[g] = scale;
+        mins[g] = mn;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int q = sub + 8 * k;
+        if (q < np) {
+          const uint32_t c0 = qcode_fast(v[k].x, mn, scale, inv, levels);
+          const uint32_t c1 = qcode_fast(v[k].y, mn, scale, inv, levels);
+          if (INT4) {
+            const uint32_t b = (c0 & 0xFu) | ((c1 & 0xFu) << 4);
+            out[base / 2 + q] = (uint8_t)b;
+            if (HIST) atomicAdd(&sh[b], 1u);
+          } else {
+            *reinterpret_cast<uint16_t*>(out + base + 2 * (size_t)q) = (uint16_t)(c0 | (c1 << 8));
+            if (HIST) {
+              atomicAdd(&sh[c0], 1u);
+              atomicAdd(&sh[c1], 1u);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (HIST) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      if (sh[i]) atomicAdd(&hist[i], sh[i]);
+  }
+}
+
 template <typename TIn>
 __global__ void __launch_bounds__(256) k_quant_token_scalar(const TIn* __restrict__ x, size_t rows,
                                                             int D, float levels,
@@ -875,6 +952,31 @@ cudaError_t launch_quantize_codes(const void* x, int in_dtype, size_t H, size_t 
   if (in_dtype == KVF_IN_F16)
     return quantize_typed(static_cast<const __half*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
   return quantize_typed(static_cast<const float*>(x), H, T, D, data_type, axis, codes, scales, mins, keys, st);
+}
+
+cudaError_t launch_quantize_token_pairs(const void* x, int in_dtype, size_t H, size_t T, size_t D, int data_type,
+                                       uint8_t* out, float* scales, float* mins, uint32_t* hist, cudaStream_t st) {
+  const size_t esz = in_dtype == KVF_IN_F16 ? 2 : 4;
+  const size_t rows = H * T;
+  if (D == 0 || D % 2 || D > 128 || rows == 0 || !aligned(x, 2 * esz) || (data_type == KVF_INT8 && !aligned(out, 2)))
+    return cudaErrorNotSupported;
+  const unsigned grid = grid_warps((rows + 3) / 4, 8);
+  const float levels = quant_levels(data_type);
+  const int Di = (int)D;
+#define KVF_QTP(TI, I4, HI)                                                                                 \
+  k_quant_token_pairs<TI, I4, HI><<<grid, 256, 0, st>>>(static_cast<const TI*>(x), rows, Di, levels, out, scales, \
+                                                       mins, hist)
+  const bool i4 = data_type == KVF_INT4, hi = hist != nullptr;
+  if (in_dtype == KVF_IN_F16) {
+    if (i4) { if (hi) KVF_QTP(__half, true, true); else KVF_QTP(__half, true, false); }
+    else { if (hi) KVF_QTP(__half, false, true); else KVF_QTP(__half, false, false); }
+  } else {
+    if (i4) { if (hi) KVF_QTP(float, true, true); else KVF_QTP(float, true, false); }
+    else { if (hi) KVF_QTP(float, false, true); else KVF_QTP(float, false, false); }
+  }
+#undef KVF_QTP
+  note_launches(1);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_quantize_channel_cluster(const void* x, int in_dtype, size_t H, size_t T, size_t D, int data_type,

@@ -57,7 +57,9 @@ def _x(shape, seed, f16=False, scale=1.0):
 
 
 # ---- quantization ---------------------------------------------------------------
+# (even widths that are not multiples of four take the paired per-token kernel)
 QSHAPES = [(4, 64, 32), (3, 17, 9), (1, 1, 1), (2, 128, 5), (2, 300, 128), (8, 1000, 128), (5, 7, 256),
+           (3, 101, 58), (2, 33, 6), (1, 7, 2), (4, 50, 126),
            (2, 9, 13), (1, 3000, 24), (3, 65, 100)]
 
 
