@@ -656,6 +656,10 @@ def gpu_arm(args):
     # the GPU runs the same kernels, with one host launch per step instead of
     # hundreds of API calls (with 8 ranks on one host the per-call issue cost
     # had left each GPU waiting); --no-graph issues every call from the host
+    # clocks are sampled from here (the graph's warm-up replays) to the end of
+    # the timed region, so short timed regions still carry samples under load
+    clocks = ClockSampler(dev)
+    clocks.start()
     graph, graph_launches, graph_err = None, None, None
     if args.graph:
         torch.cuda.synchronize()
@@ -684,8 +688,6 @@ def gpu_arm(args):
         import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(dev)
-    clocks.start()
     n0 = lib.kvf_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
