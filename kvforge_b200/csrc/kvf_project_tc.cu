@@ -307,6 +307,18 @@ __device__ __noinline__ void finish_row(const __half* __restrict__ x, size_t gro
   write_row<RG>(cd, grow, R, scale, mn, o, shist, hist_on);
 }
 
+// head h's R f32 basis rows (512 B each) into a slot's rows of kBStride
+// floats, by bulk copies that complete on `bar`; one thread
+__device__ __forceinline__ void copy_basis_rows(float* slot, int h, int R, const float* __restrict__ bvt,
+                                                uint64_t* bar) {
+  mbar_expect_tx(bar, (uint32_t)(R * kD * 4));
+  for (int r = 0; r < R; ++r)
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sa(slot + r * kBStride)),
+                 "l"(bvt + ((size_t)h * R + r) * kD), "r"(kD * 4), "r"(sa(bar))
+                 : "memory");
+}
+
 // EXACT = false: the approximate engine. Codes come straight from the
 // tensor-core coefficients (no exact chains, no deferred rows), and the token
 // stage goes back to the TMA producer when its MMAs complete.
@@ -370,6 +382,10 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
     *abort_flag = 0;
     *dcount = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the first head's f32 basis rows are requested before any token tile:
+    // behind every SM's first stages (about 24 MB) they would land several
+    // microseconds later, and no MMA can start before its basis is converted
+    if (nit > 0) copy_basis_rows(bf, h_first, R, bvt, &bcopy);
   }
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
@@ -440,15 +456,7 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
         // rows l and l + 32 in f32, every rounding upward.
         float* bfs = bf + (size_t)b * RG * kBStride;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot, then the copies
-        if (lane == 0) {
-          mbar_expect_tx(&bcopy, (uint32_t)(R * kD * 4));
-          for (int r = 0; r < R; ++r)
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    sa(bfs + r * kBStride)),
-                "l"(bvt + ((size_t)h * R + r) * kD), "r"(kD * 4), "r"(sa(&bcopy))
-                : "memory");
-        }
+        if (lane == 0 && hs > 0) copy_basis_rows(bfs, h, R, bvt, &bcopy);  // the first head's: at set-up
         const uint64_t rk = ranks[h];
         const int rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
         bool okc = mbar_wait(&bcopy, (uint32_t)(nconv & 1), abort_flag);
@@ -478,12 +486,17 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
           *reinterpret_cast<uint2*>(reg + rl * 128 + ((chunk ^ (rl & 7)) << 4) + half) =
               make_uint2(*reinterpret_cast<const uint32_t*>(&ll[0]), *reinterpret_cast<const uint32_t*>(&ll[2]));
         }
-        for (int r = lane; r < RG; r += 32) {
+        // 8 lanes per row (16 columns each), 4 rows at a time: partial sums
+        // of squares rounded upward, combined by upward-rounded shuffle adds,
+        // so every sum stays an upper bound of the exact one. Only the exact
+        // engine's verification reads the bounds.
+        for (int r0 = 0; EXACT && r0 < RG; r0 += 4) {
+          const int r = r0 + (lane >> 3), c0 = 16 * (lane & 7);
           float sv = 0.0f, sh = 0.0f, sl = 0.0f, se = 0.0f;
           if (r < rank) {
-#pragma unroll 4
-            for (int c4 = 0; c4 < kD / 4; ++c4) {
-              const float4 v4 = *reinterpret_cast<const float4*>(bfs + r * kBStride + 4 * c4);
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              const float4 v4 = *reinterpret_cast<const float4*>(bfs + r * kBStride + c0 + 4 * c4);
               const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
@@ -499,11 +512,18 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
               }
             }
           }
+#pragma unroll
+          for (int o = 4; o > 0; o >>= 1) {
+            sv = __fadd_ru(sv, __shfl_xor_sync(0xffffffffu, sv, o));
+            sh = __fadd_ru(sh, __shfl_xor_sync(0xffffffffu, sh, o));
+            sl = __fadd_ru(sl, __shfl_xor_sync(0xffffffffu, sl, o));
+            se = __fadd_ru(se, __shfl_xor_sync(0xffffffffu, se, o));
+          }
           // every sum and root rounded up, then 2^-10 more for the sums' rounding
           const float bnd = __fmaf_ru(
               kTcRelF, __fadd_ru(__fsqrt_ru(sh), __fmul_ru(__fsqrt_ru(sl), kLoInv)),
               __fmaf_ru(kChainRelF, __fsqrt_ru(sv), __fsqrt_ru(se)));
-          info[b].bn[r] = (r < rank) ? __fmul_ru(bnd, 1.0f + 1.0f / 1024.0f) : 0.0f;
+          if ((lane & 7) == 0 && r < RG) info[b].bn[r] = (r < rank) ? __fmul_ru(bnd, 1.0f + 1.0f / 1024.0f) : 0.0f;
         }
         bad = __any_sync(0xffffffffu, bad);
         if (lane == 0) {
