@@ -308,10 +308,10 @@ __device__ __noinline__ void finish_row(const __half* __restrict__ x, size_t gro
 }
 
 // head h's R f32 basis rows (512 B each) into a slot's rows of kBStride
-// floats, by bulk copies that complete on `bar`; one thread
+// floats, by bulk copies that complete on `bar` (whose expected bytes the
+// caller has raised); one thread
 __device__ __forceinline__ void copy_basis_rows(float* slot, int h, int R, const float* __restrict__ bvt,
                                                 uint64_t* bar) {
-  mbar_expect_tx(bar, (uint32_t)(R * kD * 4));
   for (int r = 0; r < R; ++r)
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      sa(slot + r * kBStride)),
@@ -359,6 +359,19 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
   const long long i1 = items * (blockIdx.x + 1) / gridDim.x;
   const int nit = (int)(i1 - i0);
   const int h_first = nit > 0 ? (int)(i0 / tiles) : 0;
+  // the range reaches a second head whose basis can be copied at set-up
+  const bool two_pre = kSlots > 1 && nit > 0 && (int)((i1 - 1) / tiles) > h_first;
+  // token tile n of this block's range into stage n % kStages (one thread)
+  auto issue_tile = [&](int n) {
+    const int s = n % kStages;
+    const long long it = i0 + n;
+    const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
+    const int row0 = h * T + tile * kRows;
+    uint8_t* dst = xs + (size_t)s * kTileBytes;
+    mbar_expect_tx(&x_full[s], (uint32_t)kTileBytes);
+    tma_load_2d(dst, &xmap, 0, row0, &x_full[s]);
+    tma_load_2d(dst + kRegionBytes, &xmap, 64, row0, &x_full[s]);
+  };
   const bool hist_on = o.hist != nullptr;
 
   if (w == 1) {
@@ -382,10 +395,16 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
     *abort_flag = 0;
     *dcount = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // the first head's f32 basis rows are requested before any token tile:
-    // behind every SM's first stages (about 24 MB) they would land several
-    // microseconds later, and no MMA can start before its basis is converted
-    if (nit > 0) copy_basis_rows(bf, h_first, R, bvt, &bcopy);
+    // the basis rows of the first head (and of the second, when the tile
+    // range reaches it and a second slot exists) are requested before any
+    // token tile: behind every SM's first stages (about 24 MB) they would
+    // land several microseconds later, and no MMA can start before its basis
+    // is converted (requesting the first tiles here too measured slower)
+    if (nit > 0) {
+      mbar_expect_tx(&bcopy, (uint32_t)((two_pre ? 2 : 1) * R * kD * 4));
+      copy_basis_rows(bf, h_first, R, bvt, &bcopy);
+      if (two_pre) copy_basis_rows(bf + RG * kBStride, h_first + 1, R, bvt, &bcopy);
+    }
   }
   if (hist_on)
     for (int i = tid; i < 256; i += blockDim.x) shist[i] = 0u;
@@ -405,13 +424,7 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
           timed_out = true;
           break;
         }
-        const long long it = i0 + n;
-        const int h = (int)(it / tiles), tile = (int)(it - (long long)h * tiles);
-        const int row0 = h * T + tile * kRows;
-        uint8_t* dst = xs + (size_t)s * kTileBytes;
-        mbar_expect_tx(&x_full[s], (uint32_t)kTileBytes);
-        tma_load_2d(dst, &xmap, 0, row0, &x_full[s]);
-        tma_load_2d(dst + kRegionBytes, &xmap, 64, row0, &x_full[s]);
+        issue_tile(n);
         issued = n + 1;
       }
       // copies still in flight land before the block's shared memory is released
@@ -452,15 +465,24 @@ __global__ void __launch_bounds__(PtCfg<RG>::kThreads, 1)
         // (512 B each) into the slot's exact-chain copy; then lane l writes
         // channels 4l .. 4l + 3 of every row as f16 parts, hi rows 0..RG-1 and
         // lo rows RG..2RG-1, in two 128-byte swizzled regions (region l / 16,
-        // 16-byte chunk (l % 16) / 2); finally lane l computes the bound b_r of
-        // rows l and l + 32 in f32, every rounding upward.
+        // 16-byte chunk (l % 16) / 2); finally (exact engine) 8 lanes per row
+        // compute the bound b_r in f32, every rounding upward.
         float* bfs = bf + (size_t)b * RG * kBStride;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot, then the copies
-        if (lane == 0 && hs > 0) copy_basis_rows(bfs, h, R, bvt, &bcopy);  // the first head's: at set-up
+        // the rows of the first head, and of the second with two_pre, were
+        // requested at set-up (one barrier phase for both)
+        const bool copied = hs == 0 || (hs == 1 && two_pre);
+        if (lane == 0 && !copied) {
+          mbar_expect_tx(&bcopy, (uint32_t)(R * kD * 4));
+          copy_basis_rows(bfs, h, R, bvt, &bcopy);
+        }
         const uint64_t rk = ranks[h];
         const int rank = (int)(rk < (uint64_t)R ? rk : (uint64_t)R);
-        bool okc = mbar_wait(&bcopy, (uint32_t)(nconv & 1), abort_flag);
-        ++nconv;
+        bool okc = true;
+        if (!(hs == 1 && two_pre)) {
+          okc = mbar_wait(&bcopy, (uint32_t)(nconv & 1), abort_flag);
+          ++nconv;
+        }
         if (!__all_sync(0xffffffffu, okc)) {
           timed_out = true;
           break;
