@@ -97,7 +97,10 @@ typedef struct kvf_basis kvf_basis;
 typedef struct kvf_compressed kvf_compressed;
 
 /* ---- context ---------------------------------------------------------- */
-/* replaces KernelLauncher::new (kernel_launcher.rs:13-17) */
+/* replaces KernelLauncher::new (kernel_launcher.rs:13-17). Free every
+ * kvf_compressed built or loaded on a context (kvf_compressed_free) before
+ * kvf_destroy(ctx): their buffers come from the context's memory pool and
+ * their ordering events from its event cache. */
 kvf_status kvf_init(int device, kvf_ctx** out);
 kvf_status kvf_destroy(kvf_ctx* ctx);
 const char* kvf_last_error(void);
