@@ -61,7 +61,9 @@ def _traffic(kernel: str):
 def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
     """Isolated launches of the step's bandwidth-bound kernels on layer 0, timed
     with CUDA events on their own stream: value/key projection (+ per-token INT4
-    quantization for values) and value/key reconstruction on both engines.
+    quantization for values), standalone calibration of the keys, and value/key
+    reconstruction on both engines. (The rANS coders return their container
+    length to the host, so they are timed per stage by stage_rooflines.)
     Algorithmic bytes per launch: inputs read once plus outputs written once."""
     _, k, v, kb, vb = lay
     H, T, D = k.shape
@@ -143,6 +145,13 @@ def kernel_rooflines(lib, L, K, torch, lay, dev, cfg, reps=20):
             nbytes = x.numel() * 2 + 4 * H * T * R
             kern = "k_project (MODE 0: coefficients)"
         res.append({"name": name, "kernel": kern, "bytes": nbytes, "ms": ms, "R": R, "in_step": True})
+    # calibration on its own (the step fuses its sums into the key projection):
+    # per-head fp64 sums of the key tensor, then the scores
+    scores = torch.empty(H, dtype=torch.float32, device=k.device)
+    ms = timed(lambda: L.check(lib.kvf_calibrate(ctx, P(k), L.IN_F16 if k.dtype == torch.float16 else L.IN_F32, H, T, D, 64,
+                                                 P(scores), sp)))
+    res.append({"name": "calibrate_keys", "kernel": "k_calib_partials + k_calib_finalize", "R": None,
+                "bytes": k.numel() * k.element_size() + 4 * H, "ms": ms, "in_step": False})
     # both reconstruction engines; the step uses the default choice (CUDA cores
     # up to 16 coefficients, tensor cores above), the other is timed beside it
     for engine, eng_name in ((L.RECON_CUDA_CORE, "cuda_core"), (L.RECON_TENSOR_CORE, "tcgen05")):

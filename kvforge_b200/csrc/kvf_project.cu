@@ -655,6 +655,61 @@ __global__ void __launch_bounds__(256) k_calib_partials(const TIn* __restrict__ 
   }
 }
 
+// The same sums from 16-byte vectors (8 halves or 4 floats), four vectors in
+// flight per thread; every element is still converted to fp64 and added on
+// its own. Requires a 16-byte aligned x and per_head * sizeof(TIn) a multiple
+// of 16 (every head's block and every tile start on a vector).
+template <typename TIn>
+__global__ void __launch_bounds__(256) k_calib_partials_v(const TIn* __restrict__ x, size_t per_head,
+                                                          double* __restrict__ cpart) {
+  constexpr int V = 16 / (int)sizeof(TIn);  // elements per vector
+  constexpr int kFlight = 4;
+  const int h = blockIdx.y;
+  const size_t e0 = (size_t)blockIdx.x * kCalibTile;
+  const size_t e1 = (e0 + kCalibTile < per_head) ? e0 + kCalibTile : per_head;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + (size_t)h * per_head);
+  const size_t q0 = e0 / V, q1 = e1 / V;
+  double s1 = 0.0, s2 = 0.0;
+  auto add = [&](const uint4& u) {
+    float f[8];
+    if constexpr (sizeof(TIn) == 2) {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+        f[2 * k] = t.x;
+        f[2 * k + 1] = t.y;
+      }
+    } else {
+      f[0] = __uint_as_float(u.x);
+      f[1] = __uint_as_float(u.y);
+      f[2] = __uint_as_float(u.z);
+      f[3] = __uint_as_float(u.w);
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const double v = (double)f[k];
+      s1 += v;
+      s2 += v * v;
+    }
+  };
+  size_t q = q0 + threadIdx.x;
+  for (; q + (kFlight - 1) * blockDim.x < q1; q += kFlight * blockDim.x) {
+    uint4 u[kFlight];
+#pragma unroll
+    for (int j = 0; j < kFlight; ++j) u[j] = __ldg(xv + q + j * blockDim.x);
+#pragma unroll
+    for (int j = 0; j < kFlight; ++j) add(u[j]);
+  }
+  for (; q < q1; q += blockDim.x) add(__ldg(xv + q));
+  block_sum2(s1, s2);
+  if (threadIdx.x == 0) {
+    const size_t slot = (size_t)h * gridDim.x + blockIdx.x;
+    cpart[2 * slot] = s1;
+    cpart[2 * slot + 1] = s2;
+  }
+}
+
 // calibration.rs:56-71: variance per head, clamped at 0, normalised by the max
 // (uniform 0.5 when the max is below 1e-12). One block; warp w sums the
 // partials of heads w, w + 8, ...: lane l adds every 32nd partial in order,
@@ -1174,10 +1229,15 @@ cudaError_t launch_calib_partials(const void* x, int in_dtype, size_t H, size_t 
   const size_t tiles = calib_partial_tiles(T, D);
   if (H == 0) return cudaSuccess;
   const dim3 grid((unsigned)tiles, (unsigned)H);
-  if (in_dtype == KVF_IN_F16)
-    k_calib_partials<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), T * D, calib_part);
-  else
-    k_calib_partials<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T * D, calib_part);
+  const size_t esz = in_dtype == KVF_IN_F16 ? 2 : 4;
+  const bool vec = aligned(x, 16) && (T * D * esz) % 16 == 0;  // kCalibTile * esz is a multiple of 16 too
+  if (in_dtype == KVF_IN_F16) {
+    if (vec) k_calib_partials_v<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), T * D, calib_part);
+    else k_calib_partials<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), T * D, calib_part);
+  } else {
+    if (vec) k_calib_partials_v<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T * D, calib_part);
+    else k_calib_partials<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T * D, calib_part);
+  }
   note_launches(1);
   return cudaGetLastError();
 }
