@@ -28,9 +28,12 @@
 // every encode and decode block builds it from the 256 counts it is given.
 //
 // Every read of the decoder is bounds-checked against the container; a
-// malformed container sets a status bit instead of faulting, and there are no
-// waits, so no kernel here can hang.
+// malformed container sets a status bit instead of faulting. The decoder has
+// no waits; the encoder's one wait (its look-back for the payload offsets of
+// lower-numbered chunks) is bounded and reports a timeout in the status word,
+// so no kernel here can hang.
 #include <algorithm>
+#include <atomic>
 
 #include "kvf_internal.cuh"
 
@@ -573,6 +576,28 @@ __global__ void __launch_bounds__(kDecBlockWarps * 32) k_rans_decode(const uint8
 
 }  // namespace
 
+namespace {
+// dynamic shared memory above the default, opted in once per (kernel, device)
+// for the largest size asked so far (the attribute is per device)
+constexpr int kOptDevs = 64;
+std::atomic<int> enc_opted[kOptDevs], dec_opted[kOptDevs];
+template <typename K>
+cudaError_t opt_in_smem(K kern, std::atomic<int>* opted, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kOptDevs) return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (bytes <= opted[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) {
+    int cur = opted[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !opted[dev].compare_exchange_weak(cur, bytes, std::memory_order_acq_rel)) {
+    }
+  }
+  return e;
+}
+}  // namespace
+
 cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, const uint32_t* freq,
                                unsigned long long* lookback, uint8_t* out, uint64_t* out_len, unsigned* status,
                                cudaStream_t st) {
@@ -582,7 +607,7 @@ cudaError_t launch_rans_encode(const uint8_t* data, size_t n, uint32_t chunk, co
   const size_t nc = rans_num_chunks(n, chunk);
   const size_t smem = (size_t)kEncWarps * enc_warp_smem(chunk);
   if (smem > kSmemOptIn) {
-    cudaError_t e = cudaFuncSetAttribute(k_rans_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = opt_in_smem(k_rans_encode, enc_opted, (int)smem);
     if (e != cudaSuccess) return e;
   }
   cudaError_t e = cudaMemsetAsync(lookback, 0, (nc + 1) * sizeof(unsigned long long), st);  // + the ticket
@@ -602,8 +627,7 @@ cudaError_t launch_rans_decode(const uint8_t* comp, size_t comp_len, const uint6
   // chunks, so a container with any chunk size named in its header decodes
   const size_t nc = rans_num_chunks(n, kRansChunk);
   const unsigned grid = (unsigned)((nc + kDecWarps - 1) / kDecWarps);
-  const cudaError_t e =
-      cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecSmem);
+  const cudaError_t e = opt_in_smem(k_rans_decode, dec_opted, (int)kDecSmem);
   if (e != cudaSuccess) return e;
   k_rans_decode<<<grid, kDecBlockWarps * 32, kDecSmem, st>>>(comp, comp_len, comp_len_dev, freq, n, out, status);
   note_launches(1);
